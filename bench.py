@@ -1,0 +1,319 @@
+#!/usr/bin/env python
+"""Batch-1 greedy decode benchmark on N B200s.
+
+One step = one full greedy generation of the configuration the metric is
+quoted on: the 48-layer Qwen3-30B-A3B synthetic model (seeded random GGUF
+quants, 10.25 GB), start token 42, 256 greedy tokens with the persistent INT8
+KV, all on the device (qx_cuda_generate).  `value` is tokens/s of the whole
+job with the weights resident in HBM; `e2e` is the same metric through the
+per-token C-ABI call qx_cuda_decode_step with host token in / host token out.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Under torchrun (N > 1) every rank runs its own engine replica on its GPU (the
+expert-parallel engine is not in this build yet); value = tokens of all ranks
+/ max-over-ranks time.
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qx-mini-c_b200"))
+
+import numpy as np  # noqa: E402
+
+import qxlib  # noqa: E402
+import workloads as W  # noqa: E402
+
+METRIC = "batch-1 decode tok/s"
+WORKLOAD = ("config4: full 48-layer Qwen3-30B-A3B greedy decode, seeded random GGUF quants "
+            "(IQ4_XS attn, IQ2_XS gate/up, IQ3_XXS down, Q4_K embd, Q6_K head), start token 42, "
+            "256 greedy steps, persistent INT8 KV")
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU arms
+def cpu_reference_sample(image, processes, tokens_per_process=1):
+    """Time the reference's own C decode (oracle/_ref/libqxref.so, src/qx_format.c
+    compiled unchanged) for one greedy token from START_TOKEN at position 0 in
+    `processes` forked workers sharing the model image; returns tokens/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle_bind
+    if not oracle_bind.available("ref"):
+        return None, "reference checker oracle/_ref/libqxref.so not built"
+    pids = []
+    t0 = time.perf_counter()
+    for _ in range(processes):
+        pid = os.fork()
+        if pid == 0:
+            try:
+                m = oracle_bind.Checker("ref").open_image(image)
+                kv = m.new_kv(tokens_per_process + 1)
+                tok = W.START_TOKEN
+                for s in range(tokens_per_process):
+                    tok = m.decode_step(tok, s, kv)["token"]
+                os._exit(0)
+            except Exception:
+                os._exit(1)
+        pids.append(pid)
+    ok = all(os.waitpid(p, 0)[1] == 0 for p in pids)
+    dt = time.perf_counter() - t0
+    if not ok:
+        return None, "reference worker failed"
+    return processes * tokens_per_process / dt, None
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    img = qxlib.build_image(W.model_config(full=True))
+    cores = os.cpu_count() or 1
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        v, why = cpu_reference_sample(img, cores)
+        dt = time.perf_counter() - t0
+        if v is None:
+            print(json.dumps({"impl": "reference", "unavailable": why}))
+            return 0
+        if i >= args.warmup:
+            times.append(dt)
+    total = sum(times)
+    value = cores * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded random-quant model; no real checkpoint available)",
+        "config": {"workload": WORKLOAD, "sample": "one greedy token (48 layers + head) per process",
+                   "parallelism": "%d independent CPU processes" % cores},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "reference",
+                         "sample": "%d processes x 1 greedy token of config 4 per step" % cores},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU arm
+def kernel_bytes(cfg, name, position):
+    """Algorithmic HBM bytes of one launch of each kernel (weights + KV it must read)."""
+    H, Q, KV, I = cfg.hidden, cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.moe_intermediate
+    return {
+        "embed_q4k": (H // 256) * 144,
+        "qkv_iq4xs": (Q + 2 * KV) * (H // 256) * 136 + 2 * H * 4,
+        "attn_splitkv": (position + 1) * (2 * KV + 8),
+        "oproj_iq4xs": H * (Q // 256) * 136 + Q * 4,
+        "router_top8": cfg.experts * H * 4 + H * 4,
+        "gateup_iq2xs_swiglu": 8 * 2 * I * (H // 256) * 74,
+        "down_iq3xxs_wsum": 8 * H * (I // 256) * 98,
+        "head_q6k_argmax": cfg.vocab * (H // 256) * 210 + H * 4,
+    }.get(name, 0)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    cfg = W.model_config(full=True)
+    img = qxlib.build_image(cfg)
+    stream = torch.cuda.Stream()
+    eng = qxlib.Engine(img, ctx=W.DECODE_STEPS + 8, device=local, stream=stream.cuda_stream)
+    steps_tok = W.DECODE_STEPS
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # device-resident arm: 256-token greedy generation per step
+    ref_tokens = None
+    for _ in range(args.warmup):
+        toks = eng.generate(W.START_TOKEN, 0, steps_tok)
+        ref_tokens = toks if ref_tokens is None else ref_tokens
+    p0 = eng.profile()
+    sampler = ClockSampler(local)
+    barrier()
+    sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        toks = eng.generate(W.START_TOKEN, 0, steps_tok)
+    ev1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    p1 = eng.profile()
+    if not np.array_equal(toks, ref_tokens):
+        raise SystemExit("non-deterministic greedy tokens across steps")
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps * steps_tok / (ms_max / 1000.0)
+    launches = int(p1["kernel_launches"] - p0["kernel_launches"])
+
+    # end-to-end arm: per-token C-ABI call with host token in / host token out
+    for _ in range(1):
+        tok = W.START_TOKEN
+        for s in range(steps_tok):
+            tok = eng.decode_step(tok, s)["token"]
+    q0 = eng.profile()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        tok = W.START_TOKEN
+        for s in range(steps_tok):
+            tok = eng.decode_step(tok, s)["token"]
+    e1.record(stream)
+    barrier()
+    q1 = eng.profile()
+    ems = e0.elapsed_time(e1)
+    t = torch.tensor([ems], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * args.steps * steps_tok / (float(t.item()) / 1000.0)
+    h2d = (q1["host_to_device_bytes"] - q0["host_to_device_bytes"]) // args.steps
+    d2h = (q1["device_to_host_bytes"] - q0["device_to_host_bytes"]) // args.steps
+
+    # per-kernel device time (CUDA events between launches, outside the timed region)
+    kt = eng.time_kernels(W.START_TOKEN, 0, 16)
+    per_token = {k: v[0] * v[1] / 16.0 for k, v in kt.items()}
+    total_ms = sum(per_token.values())
+    dom = max(per_token, key=per_token.get)
+    dom_ms, dom_n = kt[dom][0], kt[dom][1]
+    dom_bytes = kernel_bytes(cfg, dom, 8)
+    peak, peak_kind = peaks()
+    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get(dom)
+        except Exception:
+            traffic = None
+    step_bytes = W.weight_bytes_per_token(cfg) + sum(W.kv_bytes_per_token(cfg, p) for p in range(steps_tok)) / steps_tok
+    step_gbs = step_bytes * value / world / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-quant model and inputs; no real checkpoint available)",
+        "config": {"workload": WORKLOAD, "tokens_per_step": steps_tok, "batch": 1,
+                   "parallelism": "single GPU" if world == 1 else "%d independent replicas" % world,
+                   "l2": "inputs larger than L2 (10.25 GB of weights streamed per token)"},
+        "hbm_gbs_per_gpu": step_gbs, "hbm_frac_of_measured": step_gbs / peak,
+        "algorithmic_bytes_per_token": step_bytes,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
+                     "bytes_per_launch": dom_bytes, "avg_launch_ms": dom_ms, "share_of_step": per_token[dom] / total_ms},
+        "kernels_ms_per_token": {k: round(v, 5) for k, v in sorted(per_token.items(), key=lambda kv: -kv[1])},
+        "clocks": clocks,
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": launches,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, why = cpu_reference_sample(img, 1)
+        line["cpu_baseline"] = ({"value": v, "unit": "tok/s", "cores": 1, "kind": "reference",
+                                 "sample": "1 greedy token of config 4 (48 layers + head) on one core"}
+                                if v is not None else {"value": None, "unavailable": why})
+    if rank == 0:
+        print(json.dumps(line))
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

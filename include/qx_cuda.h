@@ -1,0 +1,177 @@
+/*
+ * qx_cuda.h - C ABI of the B200 decode engine for qx-mini-c's Qwen3-30B-A3B
+ * forward pass.
+ *
+ * The reference has no CUDA seam yet: its state loop rejects every
+ * `--cuda-policy` other than "none" (src/qx_format.c:6004-6005, CLI
+ * src/qx_qxf_main.c:443,512-514) and reserves a `cuda_profile` JSON block
+ * (src/qx_format.c:6683).  This header is the seam: a patched state loop calls
+ * these functions when cuda_policy == "b200" (INTEGRATION.md shows the
+ * binding).  Each entry point below names the reference function whose work
+ * it replaces.
+ *
+ * Conventions (same as the reference's public API, include/qx_format.h):
+ *   - every function returns 1 on success, 0 on failure, and then writes a
+ *     NUL-terminated message into err[err_len] (qx_set_err,
+ *     src/qx_format.c:186-194);
+ *   - outputs are written only on success (fail-closed);
+ *   - no function exits or aborts; CUDA errors become messages;
+ *   - plain pointers and sizes only; host pointers unless a name says _dev.
+ *
+ * Threading: an engine is used by one host thread at a time and owns one
+ * CUDA stream (or the caller's, qx_cuda_options.stream).
+ */
+#ifndef QX_CUDA_H
+#define QX_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QX_CUDA_ABI_VERSION 1u
+
+typedef struct qx_cuda_engine qx_cuda_engine;
+
+/* One QXF1 tensor as the caller holds it (a qx_tensor_dir_entry plus the
+ * bytes it covers, e.g. from qx_acquire_span over an mmap'd file). */
+typedef struct qx_cuda_tensor {
+    const char *name;          /* GGUF name, e.g. "blk.0.ffn_gate_exps.weight" */
+    uint32_t ggml_type;        /* qx_tensor_dir_entry.flags */
+    uint32_t rank;
+    uint64_t dims[4];          /* GGUF order: dims[0] = contiguous input length */
+    uint64_t byte_size;
+    uint64_t checksum;         /* qx_tensor_dir_entry.checksum (QXF1 FNV); checked with QX_CUDA_VERIFY_CHECKSUMS */
+    const void *data;          /* host bytes, native GGUF block layout */
+} qx_cuda_tensor;
+
+/* The qx_model_manifest fields the engine uses (include/qx_format.h:41-55). */
+typedef struct qx_cuda_model {
+    uint32_t layers, hidden, q_heads, kv_heads, head_dim, vocab, experts, experts_per_token, moe_intermediate;
+} qx_cuda_model;
+
+#define QX_CUDA_VERIFY_CHECKSUMS 0x1u   /* verify FNV checksums of every tensor once, at create */
+#define QX_CUDA_NO_GRAPH         0x2u   /* launch kernels one by one instead of replaying a CUDA graph */
+
+typedef struct qx_cuda_options {
+    int32_t device;            /* CUDA ordinal; -1 = current device */
+    uint32_t ctx_tokens;       /* persistent INT8 KV capacity, 1..65536 (reference caps at 4096) */
+    uint32_t flags;            /* QX_CUDA_* */
+    uint32_t ep_rank;          /* expert-parallel rank (0 when ep_world <= 1) */
+    uint32_t ep_world;         /* expert-parallel world size; 0 or 1 = single GPU */
+    uint32_t reserved;
+    void *stream;              /* cudaStream_t to run on; NULL = engine-owned stream */
+    void *nccl_comm;           /* ncclComm_t spanning ep_world ranks (ep_world > 1) */
+} qx_cuda_options;
+
+/* Counters for the reference's `cuda_profile` block (src/qx_format.c:6683). */
+typedef struct qx_cuda_profile {
+    char backend[32];          /* "b200-sm100a" */
+    uint64_t device_bytes;     /* HBM held by the engine */
+    uint64_t host_to_device_bytes;
+    uint64_t device_to_host_bytes;
+    uint64_t kernel_launches;
+    uint64_t graph_replays;
+    uint64_t decode_steps;
+} qx_cuda_profile;
+
+/* ---- lifetime --------------------------------------------------------- */
+
+/* Upload every tensor once into HBM in its native block layout and build the
+ * per-token CUDA graph.  Replaces the per-step span reads of the state loop
+ * (qx_acquire_span / qx_read_raw_span, src/qx_format.c:858, :1757) and the
+ * persistent KV allocation (:6138-6162).  The caller's buffers may be freed
+ * after return. */
+int qx_cuda_engine_create(const qx_cuda_model *model, const qx_cuda_tensor *tensors, uint32_t tensor_count,
+                          const qx_cuda_options *options, qx_cuda_engine **out, char *err, uint64_t err_len);
+
+/* Same, reading a QXF1 container: from a file (validated fail-closed like
+ * qx_open_file, src/qx_format.c:712-841, then mmap'd) or from a caller image. */
+int qx_cuda_engine_create_from_qxf(const char *path, const qx_cuda_options *options, qx_cuda_engine **out,
+                                   char *err, uint64_t err_len);
+int qx_cuda_engine_create_from_image(const void *image, uint64_t size, const qx_cuda_options *options,
+                                     qx_cuda_engine **out, char *err, uint64_t err_len);
+
+void qx_cuda_engine_destroy(qx_cuda_engine *engine);
+
+/* Zero the persistent KV cache and scales (the calloc at src/qx_format.c:6155-6160). */
+int qx_cuda_reset(qx_cuda_engine *engine, char *err, uint64_t err_len);
+
+/* ---- decode ------------------------------------------------------------ */
+
+/* One greedy step at `position`: embed `token`, run every layer (appending K/V
+ * at `position`), final RMSNorm, Q6_K head, argmax.  Replaces one iteration of
+ * the state loop's token loop (src/qx_format.c:6250-6627) with
+ * temperature 0 (qx_sample_from_top, :3049-3057).  Optional outputs (NULL to
+ * skip): logits[vocab], final_residual[hidden], experts[layers*8] (top-8 in
+ * rank order per layer), routing[layers*8] (renormalised weights). */
+int qx_cuda_decode_step(qx_cuda_engine *engine, uint32_t token, uint32_t position, uint32_t *next_token,
+                        float *logits, float *final_residual, uint32_t *experts, float *routing,
+                        char *err, uint64_t err_len);
+
+/* `steps` greedy steps starting at (token, position) with the argmax fed back
+ * on the device (no host round trip per token); tokens_out[steps] receives the
+ * selected tokens.  The state loop's generation phase (:6250-6627) for any
+ * number of steps up to the KV capacity. */
+int qx_cuda_generate(qx_cuda_engine *engine, uint32_t token, uint32_t position, uint32_t steps,
+                     uint32_t *tokens_out, char *err, uint64_t err_len);
+
+/* ---- stage entry points (the reference's parity seams) ----------------- */
+
+/* Final RMSNorm + full-vocabulary Q6_K head: qx_compute_real_final_head
+ * (src/qx_format.c:3554-3738).  normalized[hidden], logits[vocab] may be NULL;
+ * top_tokens/top_logits[top_n] (top_n 1..32) in descending order, ties to the
+ * lower index. */
+int qx_cuda_final_head(qx_cuda_engine *engine, const float *residual, float *normalized, float *logits,
+                       uint32_t top_n, uint32_t *top_tokens, float *top_logits, char *err, uint64_t err_len);
+
+/* One MoE FFN layer on a post-attention residual: qx_apply_real_moe_layer
+ * (src/qx_format.c:5198-5317).  layer_output = residual + moe_output. */
+int qx_cuda_moe_layer(qx_cuda_engine *engine, uint32_t layer, const float *residual_after_attention,
+                      float *layer_output, float *moe_output, uint32_t selected[8], float weights[8],
+                      char *err, uint64_t err_len);
+
+/* The attention half of one layer at `position`, state-loop order
+ * (src/qx_format.c:6283-6423 with qx_rope_gqa_attention_partial, :5051-5196):
+ * attn RMSNorm, K/V projection, K head norm + RoPE, INT8 append at
+ * [layer][position], Q projection + norm + RoPE, causal GQA softmax over
+ * positions 0..position, O projection.  residual[hidden] is updated in place;
+ * attn_out[hidden] and context[q_heads*head_dim] may be NULL. */
+int qx_cuda_attention_layer(qx_cuda_engine *engine, uint32_t layer, uint32_t position, float *residual,
+                            float *attn_out, float *context, char *err, uint64_t err_len);
+
+/* Token embedding row (Q4_K gather), qx_fill_residual_vector_from_embedding
+ * without norm (src/qx_format.c:3759-3819, full-MoE mode :6261). */
+int qx_cuda_embed(qx_cuda_engine *engine, uint32_t token, float *out, char *err, uint64_t err_len);
+
+/* ---- persistent KV ---------------------------------------------------- */
+
+/* Write / read `count` positions of layer `layer` starting at `first`:
+ * k,v int8[count*kv_heads*head_dim], scales float[count] (one scale per
+ * (layer, token) shared by all KV heads, src/qx_format.c:6343-6362).  Used to
+ * pre-fill history and to move KV between the CPU path and the engine (the
+ * QXKVSNP1 payload, src/qx_format.c:5860-5913). */
+int qx_cuda_kv_write(qx_cuda_engine *engine, uint32_t layer, uint32_t first, uint32_t count, const int8_t *k,
+                     const int8_t *v, const float *k_scales, const float *v_scales, char *err, uint64_t err_len);
+int qx_cuda_kv_read(qx_cuda_engine *engine, uint32_t layer, uint32_t first, uint32_t count, int8_t *k, int8_t *v,
+                    float *k_scales, float *v_scales, char *err, uint64_t err_len);
+
+/* ---- introspection ----------------------------------------------------- */
+
+int qx_cuda_profile_get(const qx_cuda_engine *engine, qx_cuda_profile *out);
+
+/* Per-kernel device time of the last `qx_cuda_time_kernels` run.  names is a
+ * ';'-separated list written into names[names_len]; ms_avg[i] / launches[i]
+ * for each (up to max_kernels). */
+int qx_cuda_time_kernels(qx_cuda_engine *engine, uint32_t token, uint32_t position, uint32_t steps,
+                         char *names, uint64_t names_len, float *ms_avg, uint32_t *launches,
+                         uint32_t max_kernels, uint32_t *kernel_count, char *err, uint64_t err_len);
+
+/* The engine's CUDA stream (cudaStream_t) for callers that time with events. */
+void *qx_cuda_stream(const qx_cuda_engine *engine);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,645 @@
+// Engine runtime behind include/qx_cuda.h: tensor table, one-time HBM upload
+// of the QXF1 tensors in their native block layouts, persistent INT8 KV,
+// per-token CUDA graph, and the C entry points.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "qx_cuda.h"
+#include "qx_host.h"
+#include "qx_kernels.h"
+
+#define QX_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+using qx::Dev;
+using qx::Dims;
+using qx::LayerW;
+
+struct Op {                  // one launch of the per-token sequence
+    const char* name;
+    int layer;
+    int kind;
+};
+
+enum OpKind { kEmbed, kQkv, kAttn, kOproj, kRouter, kGateup, kDown, kHead };
+const char* kOpNames[] = {"embed_q4k", "qkv_iq4xs", "attn_splitkv", "oproj_iq4xs",
+                          "router_top8", "gateup_iq2xs_swiglu", "down_iq3xxs_wsum", "head_q6k_argmax"};
+
+}  // namespace
+
+struct qx_cuda_engine {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    Dims dm{};
+    Dev dev{};
+    std::vector<LayerW> layers;
+    void* weights = nullptr;     // one arena for every tensor
+    size_t weight_bytes = 0;
+    void* work = nullptr;        // activations, KV, tables
+    size_t work_bytes = 0;
+    qx::Tables* tables = nullptr;
+    int* h_io = nullptr;         // pinned host staging: [0]=token [1]=pos [2]=next [3]=err
+    cudaGraphExec_t graph = nullptr;
+    bool use_graph = true;
+    std::vector<Op> ops;
+    int* d_topi = nullptr;
+    float* d_topv = nullptr;
+    float* d_norm = nullptr;
+    qx_cuda_profile prof{};
+};
+
+namespace {
+
+void set_err(char* err, uint64_t n, const std::string& m) {
+    if (err && n) snprintf(err, (size_t)n, "%s", m.c_str());
+}
+
+bool cuda_ok(cudaError_t e, const char* what, char* err, uint64_t n) {
+    if (e == cudaSuccess) return true;
+    set_err(err, n, std::string(what) + ": " + cudaGetErrorString(e));
+    return false;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+void run_op(qx_cuda_engine* E, const Op& op) {
+    const Dev& d = E->dev;
+    cudaStream_t st = E->stream;
+    switch (op.kind) {
+        case kEmbed: qx::launch_embed(d, st); break;
+        case kQkv: qx::launch_qkv(d, E->layers[op.layer], st); break;
+        case kAttn: qx::launch_attn(d, E->layers[op.layer], op.layer, st); break;
+        case kOproj: qx::launch_oproj(d, E->layers[op.layer], st); break;
+        case kRouter: qx::launch_router(d, E->layers[op.layer], op.layer, st); break;
+        case kGateup: qx::launch_gateup(d, E->layers[op.layer], op.layer, st); break;
+        case kDown: qx::launch_down(d, E->layers[op.layer], op.layer, st); break;
+        case kHead: qx::launch_head(d, st); break;
+    }
+}
+
+void build_ops(qx_cuda_engine* E) {
+    E->ops.clear();
+    E->ops.push_back({kOpNames[kEmbed], -1, kEmbed});
+    for (int l = 0; l < E->dm.layers; ++l)
+        for (int k = kQkv; k <= kDown; ++k) E->ops.push_back({kOpNames[k], l, k});
+    E->ops.push_back({kOpNames[kHead], -1, kHead});
+}
+
+bool run_step(qx_cuda_engine* E, char* err, uint64_t n) {
+    if (E->use_graph && E->graph) {
+        if (!cuda_ok(cudaGraphLaunch(E->graph, E->stream), "cudaGraphLaunch", err, n)) return false;
+        E->prof.graph_replays++;
+    } else {
+        for (const Op& op : E->ops) run_op(E, op);
+        if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return false;
+    }
+    E->prof.kernel_launches += E->ops.size();
+    E->prof.decode_steps++;
+    return true;
+}
+
+struct Tensor {
+    const qx_cuda_tensor* t;
+    size_t offset;               // in the weight arena
+};
+
+bool check_tensor(const std::unordered_map<std::string, const qx_cuda_tensor*>& by, const std::string& name,
+                  uint32_t type, uint32_t rank, uint64_t d0, uint64_t d1, uint64_t d2, char* err, uint64_t n) {
+    auto it = by.find(name);
+    if (it == by.end()) { set_err(err, n, "tensor not found: " + name); return false; }
+    const qx_cuda_tensor* t = it->second;
+    if (t->ggml_type != type) {
+        set_err(err, n, "unsupported ggml type " + std::to_string(t->ggml_type) + " for " + name +
+                            " (engine path expects " + std::to_string(type) + ")");
+        return false;
+    }
+    if (t->rank != rank || t->dims[0] != d0 || (rank > 1 && t->dims[1] != d1) || (rank > 2 && t->dims[2] != d2)) {
+        set_err(err, n, "unexpected dimensions for " + name);
+        return false;
+    }
+    uint32_t bv = 1, bb = 4;
+    qxh_block_info(type, &bv, &bb);
+    uint64_t elems = d0 * (rank > 1 ? d1 : 1) * (rank > 2 ? d2 : 1);
+    if (t->byte_size != elems / bv * bb || !t->data) { set_err(err, n, "byte size inconsistent for " + name); return false; }
+    return true;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
+    if (!E) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(E->device);
+    if (E->stream) cudaStreamSynchronize(E->stream);
+    if (E->graph) cudaGraphExecDestroy(E->graph);
+    if (E->weights) cudaFree(E->weights);
+    if (E->work) cudaFree(E->work);
+    if (E->h_io) cudaFreeHost(E->h_io);
+    if (E->own_stream && E->stream) cudaStreamDestroy(E->stream);
+    cudaSetDevice(prev);
+    delete E;
+}
+
+QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tensor* tensors, uint32_t count,
+                                 const qx_cuda_options* opt, qx_cuda_engine** out, char* err, uint64_t n) {
+    if (!model || !tensors || !count || !out) { set_err(err, n, "invalid argument"); return 0; }
+    *out = nullptr;
+    qx_cuda_options o{};
+    o.device = -1;
+    o.ctx_tokens = 4096;
+    if (opt) o = *opt;
+    if (o.ep_world > 1) { set_err(err, n, "expert-parallel engines are created with qx_cuda_engine_create_ep"); return 0; }
+    Dims dm{};
+    dm.layers = (int)model->layers; dm.hidden = (int)model->hidden; dm.q_heads = (int)model->q_heads;
+    dm.kv_heads = (int)model->kv_heads; dm.head_dim = (int)model->head_dim; dm.vocab = (int)model->vocab;
+    dm.experts = (int)model->experts; dm.moe_inter = (int)model->moe_intermediate; dm.ctx = (int)o.ctx_tokens;
+    if (dm.layers < 1 || dm.hidden < 256 || dm.hidden % 256 || dm.hidden > 8192 || dm.kv_heads < 1 ||
+        dm.q_heads % dm.kv_heads || dm.q_heads / dm.kv_heads > 8 || dm.head_dim != 128 || dm.q_dim() % 256 ||
+        dm.q_dim() > 8192 || dm.vocab < 16 || dm.vocab % 16 || dm.experts < 8 || dm.experts > 256 ||
+        model->experts_per_token != 8 || dm.moe_inter < 256 || dm.moe_inter % 256 || dm.moe_inter > 2048 ||
+        dm.ctx < 1 || dm.ctx > 65536) {
+        set_err(err, n, "unsupported model geometry for the B200 engine");
+        return 0;
+    }
+    std::unordered_map<std::string, const qx_cuda_tensor*> by;
+    for (uint32_t i = 0; i < count; ++i)
+        if (tensors[i].name) by[tensors[i].name] = &tensors[i];
+    const uint64_t H = dm.hidden, Q = dm.q_dim(), KV = dm.kv_dim(), Ee = dm.experts, I = dm.moe_inter;
+    std::vector<std::string> names;
+    auto need = [&](const std::string& nm, uint32_t type, uint32_t rank, uint64_t d0, uint64_t d1, uint64_t d2) {
+        names.push_back(nm);
+        return check_tensor(by, nm, type, rank, d0, d1, d2, err, n);
+    };
+    bool ok = need("token_embd.weight", QXH_Q4_K, 2, H, dm.vocab, 0) &&
+              need("output_norm.weight", QXH_F32, 1, H, 0, 0) && need("output.weight", QXH_Q6_K, 2, H, dm.vocab, 0);
+    for (int l = 0; ok && l < dm.layers; ++l) {
+        std::string p = "blk." + std::to_string(l) + ".";
+        ok = need(p + "attn_norm.weight", QXH_F32, 1, H, 0, 0) && need(p + "attn_q.weight", QXH_IQ4_XS, 2, H, Q, 0) &&
+             need(p + "attn_k.weight", QXH_IQ4_XS, 2, H, KV, 0) && need(p + "attn_v.weight", QXH_IQ4_XS, 2, H, KV, 0) &&
+             need(p + "attn_output.weight", QXH_IQ4_XS, 2, Q, H, 0) &&
+             need(p + "attn_q_norm.weight", QXH_F32, 1, dm.head_dim, 0, 0) &&
+             need(p + "attn_k_norm.weight", QXH_F32, 1, dm.head_dim, 0, 0) &&
+             need(p + "ffn_norm.weight", QXH_F32, 1, H, 0, 0) && need(p + "ffn_gate_inp.weight", QXH_F32, 2, H, Ee, 0) &&
+             need(p + "ffn_gate_exps.weight", QXH_IQ2_XS, 3, H, I, Ee) &&
+             need(p + "ffn_up_exps.weight", QXH_IQ2_XS, 3, H, I, Ee) &&
+             need(p + "ffn_down_exps.weight", QXH_IQ3_XXS, 3, I, H, Ee);
+    }
+    if (!ok) return 0;
+    if (o.flags & QX_CUDA_VERIFY_CHECKSUMS) {
+        for (const auto& nm : names) {
+            const qx_cuda_tensor* t = by[nm];
+            if (qxh_fnv1a64(t->data, t->byte_size) != t->checksum) { set_err(err, n, "tensor checksum mismatch: " + nm); return 0; }
+        }
+    }
+
+    auto* E = new qx_cuda_engine();
+    E->dm = dm;
+    int dev = o.device;
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    E->device = dev;
+    E->use_graph = !(o.flags & QX_CUDA_NO_GRAPH);
+    auto fail = [&](cudaError_t e, const char* what) {
+        cuda_ok(e, what, err, n);
+        qx_cuda_engine_destroy(E);
+        return 0;
+    };
+    cudaError_t ce = cudaSetDevice(dev);
+    if (ce != cudaSuccess) return fail(ce, "cudaSetDevice");
+    if (o.stream) E->stream = (cudaStream_t)o.stream;
+    else {
+        ce = cudaStreamCreateWithFlags(&E->stream, cudaStreamNonBlocking);
+        if (ce != cudaSuccess) return fail(ce, "cudaStreamCreate");
+        E->own_stream = true;
+    }
+    ce = qx::configure_kernels();
+    if (ce != cudaSuccess) return fail(ce, "cudaFuncSetAttribute");
+
+    // weight arena: every tensor, 256-byte aligned, in its native layout
+    std::map<std::string, size_t> off;
+    size_t wb = 0;
+    for (const auto& nm : names) {
+        off[nm] = wb;
+        wb = align_up(wb + by[nm]->byte_size, 256);
+    }
+    E->weight_bytes = wb;
+    ce = cudaMalloc(&E->weights, wb);
+    if (ce != cudaSuccess) return fail(ce, "cudaMalloc(weights)");
+    for (const auto& nm : names) {
+        ce = cudaMemcpyAsync((uint8_t*)E->weights + off[nm], by[nm]->data, by[nm]->byte_size, cudaMemcpyHostToDevice,
+                             E->stream);
+        if (ce != cudaSuccess) return fail(ce, "cudaMemcpy(weights)");
+        E->prof.host_to_device_bytes += by[nm]->byte_size;
+    }
+    auto W = [&](const std::string& nm) { return (const uint8_t*)E->weights + off[nm]; };
+    for (int l = 0; l < dm.layers; ++l) {
+        std::string p = "blk." + std::to_string(l) + ".";
+        LayerW lw{};
+        lw.attn_norm = (const float*)W(p + "attn_norm.weight");
+        lw.wq = W(p + "attn_q.weight");
+        lw.wk = W(p + "attn_k.weight");
+        lw.wv = W(p + "attn_v.weight");
+        lw.wo = W(p + "attn_output.weight");
+        lw.q_norm = (const float*)W(p + "attn_q_norm.weight");
+        lw.k_norm = (const float*)W(p + "attn_k_norm.weight");
+        lw.ffn_norm = (const float*)W(p + "ffn_norm.weight");
+        lw.router = (const float*)W(p + "ffn_gate_inp.weight");
+        lw.gate = W(p + "ffn_gate_exps.weight");
+        lw.up = W(p + "ffn_up_exps.weight");
+        lw.down = W(p + "ffn_down_exps.weight");
+        E->layers.push_back(lw);
+    }
+
+    // work buffers
+    Dev& d = E->dev;
+    d.dm = dm;
+    d.tok_embd = W("token_embd.weight");
+    d.out_norm = (const float*)W("output_norm.weight");
+    d.head = W("output.weight");
+    d.nsplit = (dm.ctx + qx::kAttnChunk - 1) / qx::kAttnChunk;
+    d.head_grid = qx::head_grid_size(dev);
+    const size_t L = dm.layers, C = dm.ctx, D = dm.head_dim;
+    struct Slot { void** p; size_t bytes; };
+    std::vector<Slot> slots;
+    size_t wk = 0;
+    auto add = [&](void** p, size_t bytes) { slots.push_back({p, bytes}); wk = align_up(wk + bytes, 256); };
+    add((void**)&E->tables, sizeof(qx::Tables));
+    add((void**)&d.rope, C * (D / 2) * 2 * sizeof(double));
+    add((void**)&d.x, H * 4);
+    add((void**)&d.xn, std::max(H, Q) * 4);
+    add((void**)&d.qkv, (Q + 2 * KV) * 4);
+    add((void**)&d.kcache, L * C * KV);
+    add((void**)&d.vcache, L * C * KV);
+    add((void**)&d.kscale, L * C * 4);
+    add((void**)&d.vscale, L * C * 4);
+    add((void**)&d.attn_part, (size_t)dm.q_heads * d.nsplit * (D + 2) * 4);
+    add((void**)&d.ctxv, Q * 4);
+    add((void**)&d.attn_out, H * 4);
+    add((void**)&d.moe_out, H * 4);
+    add((void**)&d.router_logits, Ee * 8);
+    add((void**)&d.sel, L * 8 * 4);
+    add((void**)&d.selw, L * 8 * 4);
+    add((void**)&d.selw_d, 8 * 8);
+    add((void**)&d.hbuf, 8 * I * 4);
+    add((void**)&d.logits, (size_t)dm.vocab * 4);
+    add((void**)&d.best_val, (size_t)d.head_grid * 4);
+    add((void**)&d.best_idx, (size_t)d.head_grid * 4);
+    add((void**)&d.counters, qx::kCntTotal * 4);
+    add((void**)&d.token, 4);
+    add((void**)&d.pos, 4);
+    add((void**)&d.tokens_out, C * 4);
+    add((void**)&d.err, 4);
+    add((void**)&E->d_topi, 32 * 4);
+    add((void**)&E->d_topv, 32 * 4);
+    add((void**)&E->d_norm, H * 4);
+    E->work_bytes = wk;
+    ce = cudaMalloc(&E->work, wk);
+    if (ce != cudaSuccess) return fail(ce, "cudaMalloc(work)");
+    ce = cudaMemsetAsync(E->work, 0, wk, E->stream);
+    if (ce != cudaSuccess) return fail(ce, "cudaMemset(work)");
+    size_t cur = 0;
+    for (auto& s : slots) {
+        *s.p = (uint8_t*)E->work + cur;
+        cur = align_up(cur + s.bytes, 256);
+    }
+    d.tables = E->tables;
+
+    // lattice tables and RoPE table (host libm, double, as src/qx_format.c:4630-4634)
+    qx::Tables ht{};
+    const qxh_iq_tables* T = qxh_tables();
+    for (int i = 0; i < 512; ++i) for (int j = 0; j < 8; ++j) ht.iq2xs[i][j] = (float)T->iq2xs[i][j];
+    for (int i = 0; i < 256; ++i) for (int j = 0; j < 4; ++j) ht.iq3xxs[i][j] = (float)T->iq3xxs[i][j];
+    memcpy(ht.ksigns, T->ksigns, 128);
+    static const int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+    for (int i = 0; i < 16; ++i) ht.kvalues[i] = (float)kv[i];
+    std::vector<double> rope(C * (D / 2) * 2);
+    for (size_t p = 0; p < C; ++p)
+        for (size_t i = 0; i < D / 2; ++i) {
+            const double f = pow(1000000.0, -(2.0 * (double)i) / (double)D);
+            const double a = (double)p * f;
+            rope[(p * (D / 2) + i) * 2] = cos(a);
+            rope[(p * (D / 2) + i) * 2 + 1] = sin(a);
+        }
+    ce = cudaMemcpyAsync(E->tables, &ht, sizeof(ht), cudaMemcpyHostToDevice, E->stream);
+    if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync((void*)d.rope, rope.data(), rope.size() * sizeof(double), cudaMemcpyHostToDevice, E->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
+    if (ce != cudaSuccess) return fail(ce, "upload tables");
+    ce = cudaHostAlloc((void**)&E->h_io, 64, cudaHostAllocDefault);
+    if (ce != cudaSuccess) return fail(ce, "cudaHostAlloc");
+    build_ops(E);
+
+    if (E->use_graph) {
+        cudaGraph_t g = nullptr;
+        ce = cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal);
+        if (ce != cudaSuccess) return fail(ce, "cudaStreamBeginCapture");
+        for (const Op& op : E->ops) run_op(E, op);
+        cudaError_t le = cudaGetLastError();
+        ce = cudaStreamEndCapture(E->stream, &g);
+        if (le != cudaSuccess) { if (g) cudaGraphDestroy(g); return fail(le, "capture launch"); }
+        if (ce != cudaSuccess) return fail(ce, "cudaStreamEndCapture");
+        ce = cudaGraphInstantiate(&E->graph, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) return fail(ce, "cudaGraphInstantiate");
+    }
+    E->prof.device_bytes = wb + wk;
+    snprintf(E->prof.backend, sizeof(E->prof.backend), "b200-sm100a");
+    *out = E;
+    return 1;
+}
+
+namespace {
+
+int create_from_file(const qxh_file& f, const qx_cuda_options* opt, qx_cuda_engine** out, char* err, uint64_t n) {
+    const qxh_manifest& m = f.header.manifest;
+    qx_cuda_model model{m.layers, m.hidden, m.q_heads, m.kv_heads, m.head_dim, m.vocab, m.experts,
+                        m.experts_per_token, m.moe_intermediate};
+    std::vector<qx_cuda_tensor> ts(f.header.tensor_count);
+    for (uint32_t i = 0; i < f.header.tensor_count; ++i) {
+        const qxh_dir_entry& e = f.dir[i];
+        qx_cuda_tensor& t = ts[i];
+        t.name = e.name;
+        t.ggml_type = e.flags;
+        t.rank = e.rank;
+        for (int k = 0; k < 4; ++k) t.dims[k] = e.dims[k];
+        t.byte_size = e.byte_size;
+        t.checksum = e.checksum;
+        t.data = f.base + e.offset;
+    }
+    return qx_cuda_engine_create(&model, ts.data(), (uint32_t)ts.size(), opt, out, err, n);
+}
+
+}  // namespace
+
+QX_API int qx_cuda_engine_create_from_qxf(const char* path, const qx_cuda_options* opt, qx_cuda_engine** out,
+                                          char* err, uint64_t n) {
+    qxh_file f;
+    if (!qxh_open_path(path, &f, err, n)) return 0;
+    int ok = create_from_file(f, opt, out, err, n);
+    qxh_close(&f);
+    return ok;
+}
+
+QX_API int qx_cuda_engine_create_from_image(const void* image, uint64_t size, const qx_cuda_options* opt,
+                                            qx_cuda_engine** out, char* err, uint64_t n) {
+    qxh_file f;
+    if (!qxh_open_image(image, size, &f, err, n)) return 0;
+    return create_from_file(f, opt, out, err, n);
+}
+
+namespace {
+
+struct DeviceGuard {
+    int prev = 0;
+    explicit DeviceGuard(int d) { cudaGetDevice(&prev); cudaSetDevice(d); }
+    ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+// Copy the error bits back, clear them, and turn them into a message.
+bool finish(qx_cuda_engine* E, char* err, uint64_t n) {
+    cudaError_t ce = cudaMemcpyAsync(E->h_io + 3, E->dev.err, 4, cudaMemcpyDeviceToHost, E->stream);
+    E->prof.device_to_host_bytes += 4;
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(E->dev.err, 0, 4, E->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
+    if (!cuda_ok(ce, "device execution", err, n)) return false;
+    const int bits = E->h_io[3];
+    if (bits & qx::kErrToken) { set_err(err, n, "token id out of range"); return false; }
+    if (bits & qx::kErrPosition) { set_err(err, n, "steps exceed ctx"); return false; }
+    if (bits & qx::kErrNonFinite) { set_err(err, n, "non-finite final logit"); return false; }
+    if (bits & qx::kErrRouter) { set_err(err, n, "invalid selected router weights"); return false; }
+    return true;
+}
+
+bool set_scalars(qx_cuda_engine* E, uint32_t token, uint32_t pos, char* err, uint64_t n) {
+    E->h_io[0] = (int)token;
+    E->h_io[1] = (int)pos;
+    cudaError_t ce = cudaMemcpyAsync(E->dev.token, E->h_io, 4, cudaMemcpyHostToDevice, E->stream);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(E->dev.pos, E->h_io + 1, 4, cudaMemcpyHostToDevice, E->stream);
+    E->prof.host_to_device_bytes += 8;
+    return cuda_ok(ce, "cudaMemcpyAsync(scalars)", err, n);
+}
+
+bool d2h(qx_cuda_engine* E, void* dst, const void* src, size_t bytes, char* err, uint64_t n) {
+    if (!dst) return true;
+    E->prof.device_to_host_bytes += bytes;
+    return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, E->stream), "cudaMemcpyAsync(d2h)", err, n);
+}
+
+bool h2d(qx_cuda_engine* E, void* dst, const void* src, size_t bytes, char* err, uint64_t n) {
+    E->prof.host_to_device_bytes += bytes;
+    return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, E->stream), "cudaMemcpyAsync(h2d)", err, n);
+}
+
+}  // namespace
+
+QX_API int qx_cuda_reset(qx_cuda_engine* E, char* err, uint64_t n) {
+    if (!E) { set_err(err, n, "invalid argument"); return 0; }
+    DeviceGuard g(E->device);
+    const size_t L = E->dm.layers, C = E->dm.ctx, KV = E->dm.kv_dim();
+    cudaError_t ce = cudaMemsetAsync(E->dev.kcache, 0, L * C * KV, E->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(E->dev.vcache, 0, L * C * KV, E->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(E->dev.kscale, 0, L * C * 4, E->stream);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(E->dev.vscale, 0, L * C * 4, E->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
+    return cuda_ok(ce, "reset", err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_decode_step(qx_cuda_engine* E, uint32_t token, uint32_t position, uint32_t* next_token,
+                               float* logits, float* final_residual, uint32_t* experts, float* routing, char* err,
+                               uint64_t n) {
+    if (!E || !next_token) { set_err(err, n, "invalid argument"); return 0; }
+    if (token >= (uint32_t)E->dm.vocab) { set_err(err, n, "prompt token out of range"); return 0; }
+    if (position >= (uint32_t)E->dm.ctx) { set_err(err, n, "steps exceed ctx"); return 0; }
+    DeviceGuard g(E->device);
+    if (!set_scalars(E, token, position, err, n) || !run_step(E, err, n)) return 0;
+    if (!d2h(E, E->h_io + 2, E->dev.token, 4, err, n)) return 0;
+    const size_t L = E->dm.layers;
+    if (!d2h(E, logits, E->dev.logits, (size_t)E->dm.vocab * 4, err, n) ||
+        !d2h(E, final_residual, E->dev.x, (size_t)E->dm.hidden * 4, err, n) ||
+        !d2h(E, experts, E->dev.sel, L * 8 * 4, err, n) || !d2h(E, routing, E->dev.selw, L * 8 * 4, err, n))
+        return 0;
+    if (!finish(E, err, n)) return 0;
+    *next_token = (uint32_t)E->h_io[2];
+    return 1;
+}
+
+QX_API int qx_cuda_generate(qx_cuda_engine* E, uint32_t token, uint32_t position, uint32_t steps,
+                            uint32_t* tokens_out, char* err, uint64_t n) {
+    if (!E || !tokens_out || !steps) { set_err(err, n, "invalid argument"); return 0; }
+    if (token >= (uint32_t)E->dm.vocab) { set_err(err, n, "prompt token out of range"); return 0; }
+    if ((uint64_t)position + steps > (uint64_t)E->dm.ctx) { set_err(err, n, "steps exceed ctx"); return 0; }
+    DeviceGuard g(E->device);
+    if (!set_scalars(E, token, position, err, n)) return 0;
+    for (uint32_t s = 0; s < steps; ++s)
+        if (!run_step(E, err, n)) return 0;
+    if (!d2h(E, tokens_out, E->dev.tokens_out + position, (size_t)steps * 4, err, n)) return 0;
+    return finish(E, err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_final_head(qx_cuda_engine* E, const float* residual, float* normalized, float* logits,
+                              uint32_t top_n, uint32_t* top_tokens, float* top_logits, char* err, uint64_t n) {
+    if (!E || !residual) { set_err(err, n, "invalid final head argument"); return 0; }
+    if (top_n > 32) top_n = 32;
+    DeviceGuard g(E->device);
+    if (!h2d(E, E->dev.x, residual, (size_t)E->dm.hidden * 4, err, n)) return 0;
+    E->h_io[1] = 0;
+    if (!cuda_ok(cudaMemcpyAsync(E->dev.pos, E->h_io + 1, 4, cudaMemcpyHostToDevice, E->stream), "h2d", err, n)) return 0;
+    qx::launch_head(E->dev, E->stream);
+    E->prof.kernel_launches++;
+    if (normalized) { qx::launch_final_norm(E->dev, E->d_norm, E->stream); E->prof.kernel_launches++; }
+    if (top_n) { qx::launch_topn(E->dev, (int)top_n, E->d_topi, E->d_topv, E->stream); E->prof.kernel_launches++; }
+    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    if (!d2h(E, normalized, E->d_norm, (size_t)E->dm.hidden * 4, err, n) ||
+        !d2h(E, logits, E->dev.logits, (size_t)E->dm.vocab * 4, err, n) ||
+        !d2h(E, top_n ? top_tokens : nullptr, E->d_topi, top_n * 4, err, n) ||
+        !d2h(E, top_n ? top_logits : nullptr, E->d_topv, top_n * 4, err, n))
+        return 0;
+    return finish(E, err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_moe_layer(qx_cuda_engine* E, uint32_t layer, const float* x, float* layer_output,
+                             float* moe_output, uint32_t selected[8], float weights[8], char* err, uint64_t n) {
+    if (!E || !x || layer >= (uint32_t)E->dm.layers) { set_err(err, n, "invalid packed expert matvec argument"); return 0; }
+    DeviceGuard g(E->device);
+    const LayerW& w = E->layers[layer];
+    if (!h2d(E, E->dev.x, x, (size_t)E->dm.hidden * 4, err, n)) return 0;
+    qx::launch_router(E->dev, w, (int)layer, E->stream);
+    qx::launch_gateup(E->dev, w, (int)layer, E->stream);
+    qx::launch_down(E->dev, w, (int)layer, E->stream);
+    E->prof.kernel_launches += 3;
+    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    if (!d2h(E, layer_output, E->dev.x, (size_t)E->dm.hidden * 4, err, n) ||
+        !d2h(E, moe_output, E->dev.moe_out, (size_t)E->dm.hidden * 4, err, n) ||
+        !d2h(E, selected, E->dev.sel + layer * 8, 32, err, n) || !d2h(E, weights, E->dev.selw + layer * 8, 32, err, n))
+        return 0;
+    return finish(E, err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_attention_layer(qx_cuda_engine* E, uint32_t layer, uint32_t position, float* residual,
+                                   float* attn_out, float* context, char* err, uint64_t n) {
+    if (!E || !residual || layer >= (uint32_t)E->dm.layers) { set_err(err, n, "invalid argument"); return 0; }
+    if (position >= (uint32_t)E->dm.ctx) { set_err(err, n, "steps exceed ctx"); return 0; }
+    DeviceGuard g(E->device);
+    const LayerW& w = E->layers[layer];
+    if (!h2d(E, E->dev.x, residual, (size_t)E->dm.hidden * 4, err, n)) return 0;
+    E->h_io[1] = (int)position;
+    if (!cuda_ok(cudaMemcpyAsync(E->dev.pos, E->h_io + 1, 4, cudaMemcpyHostToDevice, E->stream), "h2d", err, n)) return 0;
+    qx::launch_qkv(E->dev, w, E->stream);
+    qx::launch_attn(E->dev, w, (int)layer, E->stream);
+    qx::launch_oproj(E->dev, w, E->stream);
+    E->prof.kernel_launches += 3;
+    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    if (!d2h(E, residual, E->dev.x, (size_t)E->dm.hidden * 4, err, n) ||
+        !d2h(E, attn_out, E->dev.attn_out, (size_t)E->dm.hidden * 4, err, n) ||
+        !d2h(E, context, E->dev.ctxv, (size_t)E->dm.q_dim() * 4, err, n))
+        return 0;
+    return finish(E, err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_embed(qx_cuda_engine* E, uint32_t token, float* out, char* err, uint64_t n) {
+    if (!E || !out) { set_err(err, n, "invalid residual vector argument"); return 0; }
+    if (token >= (uint32_t)E->dm.vocab) { set_err(err, n, "token id out of range"); return 0; }
+    DeviceGuard g(E->device);
+    if (!set_scalars(E, token, 0, err, n)) return 0;
+    qx::launch_embed(E->dev, E->stream);
+    E->prof.kernel_launches++;
+    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    if (!d2h(E, out, E->dev.x, (size_t)E->dm.hidden * 4, err, n)) return 0;
+    return finish(E, err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_kv_write(qx_cuda_engine* E, uint32_t layer, uint32_t first, uint32_t count, const int8_t* k,
+                            const int8_t* v, const float* ks, const float* vs, char* err, uint64_t n) {
+    if (!E || !k || !v || !ks || !vs || layer >= (uint32_t)E->dm.layers || (uint64_t)first + count > (uint64_t)E->dm.ctx) {
+        set_err(err, n, "invalid KV range"); return 0;
+    }
+    DeviceGuard g(E->device);
+    const size_t KV = E->dm.kv_dim(), base = (size_t)layer * E->dm.ctx + first;
+    bool ok = h2d(E, E->dev.kcache + base * KV, k, count * KV, err, n) &&
+              h2d(E, E->dev.vcache + base * KV, v, count * KV, err, n) &&
+              h2d(E, E->dev.kscale + base, ks, count * 4, err, n) && h2d(E, E->dev.vscale + base, vs, count * 4, err, n);
+    if (!ok) return 0;
+    return cuda_ok(cudaStreamSynchronize(E->stream), "kv write", err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_kv_read(qx_cuda_engine* E, uint32_t layer, uint32_t first, uint32_t count, int8_t* k, int8_t* v,
+                           float* ks, float* vs, char* err, uint64_t n) {
+    if (!E || layer >= (uint32_t)E->dm.layers || (uint64_t)first + count > (uint64_t)E->dm.ctx) {
+        set_err(err, n, "invalid KV range"); return 0;
+    }
+    DeviceGuard g(E->device);
+    const size_t KV = E->dm.kv_dim(), base = (size_t)layer * E->dm.ctx + first;
+    bool ok = d2h(E, k, E->dev.kcache + base * KV, count * KV, err, n) &&
+              d2h(E, v, E->dev.vcache + base * KV, count * KV, err, n) &&
+              d2h(E, ks, E->dev.kscale + base, count * 4, err, n) && d2h(E, vs, E->dev.vscale + base, count * 4, err, n);
+    if (!ok) return 0;
+    return cuda_ok(cudaStreamSynchronize(E->stream), "kv read", err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_profile_get(const qx_cuda_engine* E, qx_cuda_profile* out) {
+    if (!E || !out) return 0;
+    *out = E->prof;
+    return 1;
+}
+
+QX_API void* qx_cuda_stream(const qx_cuda_engine* E) { return E ? (void*)E->stream : nullptr; }
+
+QX_API int qx_cuda_time_kernels(qx_cuda_engine* E, uint32_t token, uint32_t position, uint32_t steps, char* names,
+                                uint64_t names_len, float* ms_avg, uint32_t* launches, uint32_t max_kernels,
+                                uint32_t* kernel_count, char* err, uint64_t n) {
+    if (!E || !steps || (uint64_t)position + steps > (uint64_t)E->dm.ctx) { set_err(err, n, "invalid argument"); return 0; }
+    DeviceGuard g(E->device);
+    if (!set_scalars(E, token, position, err, n)) return 0;
+    const size_t nops = E->ops.size();
+    std::vector<cudaEvent_t> ev(nops * steps + 1);
+    for (auto& e : ev) cudaEventCreate(&e);
+    size_t k = 0;
+    cudaEventRecord(ev[k++], E->stream);
+    for (uint32_t s = 0; s < steps; ++s)
+        for (const Op& op : E->ops) {
+            run_op(E, op);
+            cudaEventRecord(ev[k++], E->stream);
+        }
+    bool ok = cuda_ok(cudaGetLastError(), "kernel launch", err, n) && finish(E, err, n);
+    std::vector<std::string> order;
+    std::map<std::string, std::pair<double, uint32_t>> acc;
+    if (ok) {
+        k = 0;
+        for (uint32_t s = 0; s < steps; ++s)
+            for (const Op& op : E->ops) {
+                float ms = 0.f;
+                cudaEventElapsedTime(&ms, ev[k], ev[k + 1]);
+                ++k;
+                if (!acc.count(op.name)) order.push_back(op.name);
+                acc[op.name].first += ms;
+                acc[op.name].second += 1;
+            }
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    if (!ok) return 0;
+    std::string joined;
+    uint32_t c = 0;
+    for (const auto& nm : order) {
+        if (c < max_kernels) {
+            ms_avg[c] = (float)(acc[nm].first / acc[nm].second);
+            launches[c] = acc[nm].second;
+        }
+        joined += (c ? ";" : "") + nm;
+        ++c;
+    }
+    if (kernel_count) *kernel_count = c;
+    if (names && names_len) snprintf(names, (size_t)names_len, "%s", joined.c_str());
+    E->prof.kernel_launches += nops * steps;
+    return 1;
+}

@@ -1,0 +1,328 @@
+// Exact integer dot products on the tensor cores (mma.sync int8, sm_100a).
+//
+// Every weight of the GGUF block formats on the decode path is a small
+// integer times per-block scales:
+//   IQ2_XS  w = d/8 * (1+2s) * g,   g in +-{8,25,43},   s 4-bit per 16 values
+//   IQ3_XXS w = d/4 * (1+2s) * g,   g in +-{4..62},     s 4-bit per 32 values
+//   IQ4_XS  w = d * (ls-32) * kv,   kv in [-127,113],   ls 6-bit per 32 values
+//   Q6_K    w = d * sc * (q-32),    q 6-bit,            sc int8 per 16 values
+// (src/qx_format.c:1914-2169).  The activation x of each 256-value block is
+// turned into a 56-bit fixed-point integer X = round(x * 2^S_b) (exact for
+// every element within 2^31 of the block maximum), offset to X' = X + 2^55 >= 0
+// and split into 7 unsigned bytes ("limbs").  One m16n8k{16,32} s8*u8 MMA then
+// gives, per row, the exact integer sums of (integer weight) * (limb) for the
+// 7 limbs in columns 0..6, and in column 7 (a column of ones) the integer sum
+// of the weights, which removes the offset.  The per-group integer scales are
+// applied to the int32 results with IMAD, and each block's result is folded
+// into a double accumulator with its (exact) block factor d * 2^-S_b.  The
+// only roundings are the double additions, so the result agrees with the
+// reference's double accumulation to ~1e-16 and rounds to the same float.
+#pragma once
+#include <cstdint>
+
+#include "qx_dev.cuh"
+
+namespace qx {
+
+constexpr int kLimbs = 7;           // 56-bit fixed point
+constexpr int kOffsetBits = 55;
+
+// B operand in shared memory: for each 16-value group G, 32 words in lane
+// order; lane 4n+t holds limb n of values 16G+4t .. 16G+4t+3 (one byte each,
+// value order).  Lane group n = 7 holds the constant 1 (offset column).
+struct XQ {
+    const uint32_t* b;   // [K/16][32]
+    const int* s;        // [K/256] block exponents S_b
+};
+
+// ---- activation quantization ------------------------------------------------
+
+// X' = round(|x| * 2^S) * sign + 2^55, split in two words.
+__device__ __forceinline__ void to_fixed(float x, int S, uint32_t& hi, uint32_t& lo) {
+    const uint32_t bits = __float_as_uint(x);
+    int e = (int)((bits >> 23) & 255u);
+    uint32_t m = bits & 0x7fffffu;
+    if (e) m |= 0x800000u; else e = 1;
+    const int sh = e - 150 + S;           // |x| * 2^S = m * 2^sh, sh <= 31 by the choice of S
+    uint64_t mag = 0;
+    if (m) {
+        if (sh >= 0) mag = (uint64_t)m << sh;
+        else if (sh > -40) mag = ((uint64_t)m + ((1ull << (-sh)) >> 1)) >> (-sh);
+    }
+    const int64_t X = (bits >> 31) ? -(int64_t)mag : (int64_t)mag;
+    const uint64_t Xp = (uint64_t)(X + (1ll << kOffsetBits));
+    hi = (uint32_t)(Xp >> 32);
+    lo = (uint32_t)Xp;
+}
+
+// 4x4 byte transpose: out[n] = byte n of in[0..3], in value order.
+__device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t out[4]) {
+    const uint32_t t0 = __byte_perm(a, b, 0x5140), t1 = __byte_perm(a, b, 0x7362);
+    const uint32_t t2 = __byte_perm(c, d, 0x5140), t3 = __byte_perm(c, d, 0x7362);
+    out[0] = __byte_perm(t0, t2, 0x5410);
+    out[1] = __byte_perm(t0, t2, 0x7632);
+    out[2] = __byte_perm(t1, t3, 0x5410);
+    out[3] = __byte_perm(t1, t3, 0x7632);
+}
+
+// Quantize xs[0..K) (shared memory floats, K a multiple of 256) into the B
+// layout.  Every warp of the CTA must call it (warp-wide max per block).
+__device__ __forceinline__ void build_xq(const float* xs, int K, uint32_t* xb, int* sb) {
+    const int lane = threadIdx.x & 31;
+    for (int base = threadIdx.x * 8; base - lane * 8 < K; base += blockDim.x * 8) {
+        const bool active = base < K;
+        float v[8];
+        float mx = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            v[i] = active ? xs[base + i] : 0.f;
+            mx = fmaxf(mx, fabsf(v[i]));
+        }
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (!active) continue;
+        const int E = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 255u) - 127 : -126;
+        const int S = 54 - (E < -126 ? -126 : E);
+        if (lane == 0) sb[base / 256] = S;
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) to_fixed(v[i], S, hi[i], lo[i]);
+        const int G = base / 16, t0 = (base % 16) / 4;
+        uint32_t w[4];
+        uint32_t* dst = xb + G * 32;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {           // values base+4h .. base+4h+3 -> lane t0+h
+            const int t = t0 + h;
+            transpose4(lo[4 * h], lo[4 * h + 1], lo[4 * h + 2], lo[4 * h + 3], w);
+#pragma unroll
+            for (int n = 0; n < 4; ++n) dst[n * 4 + t] = w[n];
+            transpose4(hi[4 * h], hi[4 * h + 1], hi[4 * h + 2], hi[4 * h + 3], w);
+#pragma unroll
+            for (int n = 0; n < 3; ++n) dst[(4 + n) * 4 + t] = w[n];
+            dst[28 + t] = 0x01010101u;
+        }
+    }
+}
+
+// Weight of accumulator register r of lane (g,t): limb n = 2t + (r & 1)
+// carries 2^(8n).  Column 7 (sum of the integer weights) is folded into limb
+// 6 in the int32 domain before conversion (Acc::flush), so its weight is 0.
+__device__ __forceinline__ double limb_weight(int lane, int r) {
+    const int n = 2 * (lane & 3) + (r & 1);
+    return n < kLimbs ? ldexp(1.0, 8 * n) : 0.0;
+}
+
+// ---- tensor-core primitives -------------------------------------------------
+__device__ __forceinline__ void mma_k32(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void mma_k16(int d[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Per-lane accumulation state of one 16-row tile: int32 per block, double overall.
+struct Acc {
+    int i[4];
+    double d[4];
+    __device__ __forceinline__ void zero_block() { i[0] = i[1] = i[2] = i[3] = 0; }
+    __device__ __forceinline__ void add(const int D[4], int s_lo, int s_hi) {   // s_lo: row g, s_hi: row g+8
+        i[0] += s_lo * D[0];
+        i[1] += s_lo * D[1];
+        i[2] += s_hi * D[2];
+        i[3] += s_hi * D[3];
+    }
+    // fold this block: f_lo / f_hi = block factor of rows g / g+8 (d * 2^-S / c)
+    __device__ __forceinline__ void flush(double f_lo, double f_hi, const double lw[2]) {
+        // lane t = 3 holds limb 6 (offset bit 7 of that byte) and column 7:
+        // remove 2^55 * sum(w) exactly: limb6 -= 128 * column7.
+        if ((threadIdx.x & 3) == 3) {
+            i[0] -= 128 * i[1];
+            i[2] -= 128 * i[3];
+        }
+        d[0] = fma((double)i[0], f_lo * lw[0], d[0]);
+        d[1] = fma((double)i[1], f_lo * lw[1], d[1]);
+        d[2] = fma((double)i[2], f_hi * lw[0], d[2]);
+        d[3] = fma((double)i[3], f_hi * lw[1], d[3]);
+    }
+    // After the last block: lane (g, 0) returns rows g (lo) and g+8 (hi).
+    __device__ __forceinline__ void finish(double& lo, double& hi) const {
+        double a = d[0] + d[1], b = d[2] + d[3];
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        b += __shfl_xor_sync(0xffffffffu, b, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        b += __shfl_xor_sync(0xffffffffu, b, 2);
+        lo = a;
+        hi = b;
+    }
+};
+
+// Small lattice tables staged in shared memory by the expert kernels.
+struct IqTab {
+    uint32_t grid2[512][2];      // IQ2_XS lattice, 8 magnitude bytes per entry     4 KB
+    uint32_t grid3[256];         // IQ3_XXS lattice, 4 magnitude bytes per entry    1 KB
+    uint8_t ksigns[128];         // 7 stored sign bits + even parity bit
+};
+
+// Negate byte k of `mag` when bit k of `nib` is set (|values| < 128, no carries).
+__device__ __forceinline__ uint32_t signed_bytes(uint32_t mag, uint32_t nib) {
+    const uint32_t m1 = ((nib & 15u) * 0x00204081u) & 0x01010101u;
+    return (mag ^ (m1 * 255u)) + m1;
+}
+
+// ---- per-format tile dots ---------------------------------------------------
+// One warp; rows r0 (= g) and r1 (= g+8) of a 16-row tile staged in shared
+// memory; blocks [b0, b1) of the row.  Accumulates into acc.
+
+// IQ4_NL codebook lookup of the four nibbles held in bits 0-3 of each byte
+// of n (bytes 0..15), via byte permutes of the 16-byte table K[0..3].
+__device__ __forceinline__ uint32_t kv_lookup4(uint32_t n, const uint32_t K[4]) {
+    const uint32_t i3 = n & 0x07070707u;
+    const uint32_t packed = i3 | (i3 >> 4);                       // byte0 = n0|n1<<4, byte2 = n2|n3<<4
+    const uint32_t sel = __byte_perm(packed, 0u, 0x0020);         // n0 | n1<<4 | n2<<8 | n3<<12
+    const uint32_t lo = __byte_perm(K[0], K[1], sel), hi = __byte_perm(K[2], K[3], sel);
+    const uint32_t hbit = (n & 0x08080808u) << 4;                  // bit 3 -> bit 7
+    const uint32_t mask = __byte_perm(hbit, 0u, 0xba98);          // replicate bit 7 over each byte
+    return (hi & mask) | (lo & ~mask);
+}
+
+// IQ4_XS: m16n8k32, natural order (lane t: bytes 4t..4t+3 of each 16-byte
+// group -> values 4t.. (low nibbles) and 16+4t.. (high nibbles)).
+__device__ __forceinline__ void dot_iq4_xs_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,
+                                               const uint32_t K[4], int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3;
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + b * 136;
+        const uint8_t* p1 = r1 + b * 136;
+        const uint32_t sh0 = ld16(p0 + 2), sh1 = ld16(p1 + 2);
+        const uint32_t sl0 = *reinterpret_cast<const uint32_t*>(p0 + 4);
+        const uint32_t sl1 = *reinterpret_cast<const uint32_t*>(p1 + 4);
+        acc.zero_block();
+#pragma unroll 4
+        for (int ib = 0; ib < 8; ++ib) {
+            const int ls0 = ((sl0 >> (4 * ib)) & 15) | (((sh0 >> (2 * ib)) & 3) << 4);
+            const int ls1 = ((sl1 >> (4 * ib)) & 15) | (((sh1 >> (2 * ib)) & 3) << 4);
+            const uint32_t q0 = *reinterpret_cast<const uint32_t*>(p0 + 8 + 16 * ib + 4 * t);
+            const uint32_t q1 = *reinterpret_cast<const uint32_t*>(p1 + 8 + 16 * ib + 4 * t);
+            const uint32_t a0 = kv_lookup4(q0, K), a2 = kv_lookup4(q0 >> 4, K);
+            const uint32_t a1 = kv_lookup4(q1, K), a3 = kv_lookup4(q1 >> 4, K);
+            const int G = b * 16 + 2 * ib;
+            int D[4];
+            mma_k32(D, a0, a1, a2, a3, x.b[G * 32 + lane], x.b[(G + 1) * 32 + lane]);
+            acc.add(D, ls0 - 32, ls1 - 32);
+        }
+        const double sc = ldexp(1.0, -x.s[b]);
+        acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
+    }
+}
+
+// IQ2_XS: m16n8k16 per 16-value scale group; lane t takes values 4t..4t+3 =
+// half (t&1) of grid entry 2G' + (t>>1).
+__device__ __forceinline__ void dot_iq2_xs_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,
+                                               const IqTab& T, int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3, half = t & 1, sub = t >> 1;
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + b * 74;
+        const uint8_t* p1 = r1 + b * 74;
+        acc.zero_block();
+#pragma unroll 4
+        for (int gq = 0; gq < 16; ++gq) {       // 16-value group: ib32 = gq/2, scale nibble gq&1
+            const int e = 2 * gq + sub;           // grid entry index within the block
+            const uint32_t q0 = ld16(p0 + 2 + 2 * e), q1 = ld16(p1 + 2 + 2 * e);
+            const uint32_t s0 = T.ksigns[q0 >> 9], s1 = T.ksigns[q1 >> 9];
+            const uint32_t a0 = signed_bytes(T.grid2[q0 & 511u][half], s0 >> (4 * half));
+            const uint32_t a1 = signed_bytes(T.grid2[q1 & 511u][half], s1 >> (4 * half));
+            const int sc0 = 1 + 2 * ((p0[66 + (gq >> 1)] >> (4 * (gq & 1))) & 15);
+            const int sc1 = 1 + 2 * ((p1[66 + (gq >> 1)] >> (4 * (gq & 1))) & 15);
+            int D[4];
+            mma_k16(D, a0, a1, x.b[(b * 16 + gq) * 32 + lane]);
+            acc.add(D, sc0, sc1);
+        }
+        const double sc = ldexp(1.0, -x.s[b]) * 0.125;
+        acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
+    }
+}
+
+// IQ3_XXS: m16n8k32 per 32-value group; lane t: grid index bytes t (values
+// 4t..) and 4+t (values 16+4t..); sign group = t>>1 resp. 2+(t>>1), half t&1.
+__device__ __forceinline__ void dot_iq3_xxs_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,
+                                                const IqTab& T, int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3, half = t & 1, sg = t >> 1;
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + b * 98;
+        const uint8_t* p1 = r1 + b * 98;
+        acc.zero_block();
+#pragma unroll 2
+        for (int ib = 0; ib < 8; ++ib) {
+            const uint32_t aux0 = ld32u(p0 + 66 + 4 * ib), aux1 = ld32u(p1 + 66 + 4 * ib);
+            const uint32_t sA0 = T.ksigns[(aux0 >> (7 * sg)) & 127u], sB0 = T.ksigns[(aux0 >> (7 * (2 + sg))) & 127u];
+            const uint32_t sA1 = T.ksigns[(aux1 >> (7 * sg)) & 127u], sB1 = T.ksigns[(aux1 >> (7 * (2 + sg))) & 127u];
+            const uint32_t a0 = signed_bytes(T.grid3[p0[2 + 8 * ib + t]], sA0 >> (4 * half));
+            const uint32_t a2 = signed_bytes(T.grid3[p0[2 + 8 * ib + 4 + t]], sB0 >> (4 * half));
+            const uint32_t a1 = signed_bytes(T.grid3[p1[2 + 8 * ib + t]], sA1 >> (4 * half));
+            const uint32_t a3 = signed_bytes(T.grid3[p1[2 + 8 * ib + 4 + t]], sB1 >> (4 * half));
+            const int G = b * 16 + 2 * ib;
+            int D[4];
+            mma_k32(D, a0, a1, a2, a3, x.b[G * 32 + lane], x.b[(G + 1) * 32 + lane]);
+            acc.add(D, 1 + 2 * (int)(aux0 >> 28), 1 + 2 * (int)(aux1 >> 28));
+        }
+        const double sc = ldexp(1.0, -x.s[b]) * 0.25;
+        acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
+    }
+}
+
+// Q6_K: m16n8k16 per 16-value scale group.  Values of a 128-value half:
+// pos = 32*s + l (section s, l in 0..31); lane t takes l = 16*lh + 4t .. +3.
+__device__ __forceinline__ uint32_t q6_word(uint32_t ql, uint32_t qh, int s) {
+    const uint32_t lo = (s < 2 ? ql : ql >> 4) & 0x0f0f0f0fu;
+    const uint32_t hb = ((qh >> (2 * s)) & 0x03030303u) << 4;
+    return ((lo | hb | 0x80808080u) - 0x20202020u) ^ 0x80808080u;   // bytewise q - 32
+}
+
+__device__ __forceinline__ void dot_q6_k_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,
+                                             int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3;
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + b * 210;
+        const uint8_t* p1 = r1 + b * 210;
+        const int8_t* c0 = reinterpret_cast<const int8_t*>(p0 + 192);
+        const int8_t* c1 = reinterpret_cast<const int8_t*>(p1 + 192);
+        acc.zero_block();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int lh = 0; lh < 2; ++lh) {
+                const int l = 16 * lh + 4 * t;
+                const uint32_t qlA0 = ld32u(p0 + 64 * h + l), qlB0 = ld32u(p0 + 64 * h + 32 + l);
+                const uint32_t qh0 = ld32u(p0 + 128 + 32 * h + l);
+                const uint32_t qlA1 = ld32u(p1 + 64 * h + l), qlB1 = ld32u(p1 + 64 * h + 32 + l);
+                const uint32_t qh1 = ld32u(p1 + 128 + 32 * h + l);
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const uint32_t a0 = q6_word((s & 1) ? qlB0 : qlA0, qh0, s);
+                    const uint32_t a1 = q6_word((s & 1) ? qlB1 : qlA1, qh1, s);
+                    const int gq = 8 * h + 2 * s + lh;      // 16-value group index in the block
+                    int D[4];
+                    mma_k16(D, a0, a1, x.b[(b * 16 + gq) * 32 + lane]);
+                    const int si = 8 * h + lh + 2 * s;
+                    acc.add(D, (int)c0[si], (int)c1[si]);
+                }
+            }
+        }
+        const double sc = ldexp(1.0, -x.s[b]);
+        acc.flush((double)h2f(ld16(p0 + 208)) * sc, (double)h2f(ld16(p1 + 208)) * sc, lw);
+    }
+}
+
+}  // namespace qx

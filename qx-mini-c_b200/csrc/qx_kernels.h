@@ -1,0 +1,87 @@
+// Internal interface between the engine runtime (qx_engine.cu) and the
+// kernels (qx_kernels.cu).  Not part of the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "qx_dev.cuh"
+
+namespace qx {
+
+struct LayerW {                  // device pointers into the weight arena (native GGUF layouts)
+    const float* attn_norm;      // F32 [H]
+    const uint8_t* wq;           // IQ4_XS [Q rows][H]
+    const uint8_t* wk;           // IQ4_XS [KV rows][H]
+    const uint8_t* wv;           // IQ4_XS [KV rows][H]
+    const uint8_t* wo;           // IQ4_XS [H rows][Q]
+    const float* q_norm;         // F32 [D]
+    const float* k_norm;         // F32 [D]
+    const float* ffn_norm;       // F32 [H]
+    const float* router;         // F32 [E rows][H]
+    const uint8_t* gate;         // IQ2_XS [E][I rows][H]
+    const uint8_t* up;           // IQ2_XS [E][I rows][H]
+    const uint8_t* down;         // IQ3_XXS [E][H rows][I]
+};
+
+struct Dims {
+    int layers, hidden, q_heads, kv_heads, head_dim, vocab, experts, moe_inter, ctx;
+    __host__ __device__ int q_dim() const { return q_heads * head_dim; }
+    __host__ __device__ int kv_dim() const { return kv_heads * head_dim; }
+};
+
+// Per-engine device state (all device pointers).
+struct Dev {
+    Dims dm;
+    const Tables* tables;
+    const uint8_t* tok_embd;     // Q4_K [V rows][H]
+    const float* out_norm;       // F32 [H]
+    const uint8_t* head;         // Q6_K [V rows][H]
+    const double* rope;          // [ctx][D/2][2] cos, sin (host libm, double)
+    float* x;                    // residual [H]
+    float* xn;                   // normed input of the current projection [max(H,Q)]
+    float* qkv;                  // raw Q|K|V projections [Q + 2KV]
+    int8_t* kcache;              // [L][ctx][KV]
+    int8_t* vcache;
+    float* kscale;               // [L][ctx]
+    float* vscale;
+    float* attn_part;            // split-KV partials [Hq][nsplit][D + 2]
+    float* ctxv;                 // attention context [Q]
+    float* attn_out;             // O projection output [H] (stage API)
+    float* moe_out;              // MoE output [H] (stage API)
+    double* router_logits;       // [E]
+    int* sel;                    // [L][8] selected experts, rank order
+    float* selw;                 // [L][8] renormalised weights (float copies)
+    double* selw_d;              // [8] weights of the current layer (double)
+    float* hbuf;                 // SwiGLU outputs [8][I]
+    float* logits;               // [V]
+    float* best_val;             // per-CTA argmax partials
+    int* best_idx;
+    unsigned* counters;          // ticket counters for last-CTA reductions
+    int* token;                  // current input token (device scalar)
+    int* pos;                    // current position (device scalar)
+    int* tokens_out;             // [ctx] argmax written at index pos
+    int* err;                    // error bits
+    int head_grid;               // CTAs of the head kernel (partials length)
+    int nsplit;                  // split-KV chunks (ctx / kAttnChunk rounded up)
+};
+
+constexpr int kAttnChunk = 64;
+
+enum CounterSlot { kCntAttn = 0, kCntRouter = 8, kCntHead = 9, kCntTotal = 16 };
+
+// Launchers.  All run on `st` and read pos/token from device memory, so they
+// can be captured once into a CUDA graph.
+void launch_embed(const Dev& d, cudaStream_t st);
+void launch_qkv(const Dev& d, const LayerW& w, cudaStream_t st);
+void launch_attn(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
+void launch_oproj(const Dev& d, const LayerW& w, cudaStream_t st);
+void launch_router(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
+void launch_gateup(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
+void launch_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
+void launch_head(const Dev& d, cudaStream_t st);
+void launch_topn(const Dev& d, int top_n, int* out_idx, float* out_val, cudaStream_t st);
+void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st);
+int head_grid_size(int device);
+cudaError_t configure_kernels();
+
+}  // namespace qx

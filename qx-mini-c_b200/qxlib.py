@@ -109,3 +109,174 @@ def normal_vector(seed, n):
     out = np.empty(n, dtype=np.float32)
     host().qxh_normal_vector(seed, out.ctypes.data, n)
     return out
+
+
+# ---- engine (libqxcuda.so) ---------------------------------------------------
+ENGINE_SYMBOLS = [
+    "qx_cuda_engine_create", "qx_cuda_engine_create_from_qxf", "qx_cuda_engine_create_from_image",
+    "qx_cuda_engine_destroy", "qx_cuda_reset", "qx_cuda_decode_step", "qx_cuda_generate", "qx_cuda_final_head",
+    "qx_cuda_moe_layer", "qx_cuda_attention_layer", "qx_cuda_embed", "qx_cuda_kv_write", "qx_cuda_kv_read",
+    "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_stream",
+]
+
+VERIFY_CHECKSUMS = 0x1
+NO_GRAPH = 0x2
+
+
+def cuda():
+    """Load libqxcuda.so and declare its C signatures (include/qx_cuda.h)."""
+    global _cuda
+    if _cuda is None:
+        lib = _load("libqxcuda.so")
+        P, U32, U64, I32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32
+        E = C.c_char_p
+        sig = {
+            "qx_cuda_engine_create_from_qxf": [C.c_char_p, C.POINTER(CudaOptions), C.POINTER(P), E, U64],
+            "qx_cuda_engine_create_from_image": [P, U64, C.POINTER(CudaOptions), C.POINTER(P), E, U64],
+            "qx_cuda_reset": [P, E, U64],
+            "qx_cuda_decode_step": [P, U32, U32, P, P, P, P, P, E, U64],
+            "qx_cuda_generate": [P, U32, U32, U32, P, E, U64],
+            "qx_cuda_final_head": [P, P, P, P, U32, P, P, E, U64],
+            "qx_cuda_moe_layer": [P, U32, P, P, P, P, P, E, U64],
+            "qx_cuda_attention_layer": [P, U32, U32, P, P, P, E, U64],
+            "qx_cuda_embed": [P, U32, P, E, U64],
+            "qx_cuda_kv_write": [P, U32, U32, U32, P, P, P, P, E, U64],
+            "qx_cuda_kv_read": [P, U32, U32, U32, P, P, P, P, E, U64],
+            "qx_cuda_profile_get": [P, C.POINTER(CudaProfile)],
+            "qx_cuda_time_kernels": [P, U32, U32, U32, C.c_char_p, U64, P, P, U32, P, E, U64],
+        }
+        for name, args in sig.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = C.c_int
+        lib.qx_cuda_engine_destroy.argtypes = [P]
+        lib.qx_cuda_engine_destroy.restype = None
+        lib.qx_cuda_stream.argtypes = [P]
+        lib.qx_cuda_stream.restype = P
+        _cuda = lib
+    return _cuda
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+class Engine:
+    """Thin owner of a qx_cuda_engine*; every method is one C-ABI call."""
+
+    def __init__(self, image=None, path=None, ctx=4096, device=-1, flags=0, stream=None):
+        lib = cuda()
+        opt = CudaOptions()
+        opt.device = device
+        opt.ctx_tokens = ctx
+        opt.flags = flags
+        opt.stream = stream
+        h = C.c_void_p()
+        err = err_buf()
+        if path is not None:
+            ok = lib.qx_cuda_engine_create_from_qxf(path.encode(), C.byref(opt), C.byref(h), err, len(err))
+        else:
+            ok = lib.qx_cuda_engine_create_from_image(image.ctypes.data, image.nbytes, C.byref(opt), C.byref(h), err,
+                                                      len(err))
+        check(ok, err, "qx_cuda_engine_create")
+        self.h = h
+        self.lib = lib
+        self.ctx = ctx
+        hdr = np.frombuffer((image[:272].tobytes() if image is not None else open(path, "rb").read(272)), np.uint32)
+        m = hdr[14:27]
+        self.layers, self.hidden, self.q_heads, self.kv_heads, self.head_dim = (int(m[2]), int(m[3]), int(m[5]),
+                                                                                  int(m[6]), int(m[7]))
+        self.vocab, self.experts, self.moe_intermediate = int(m[8]), int(m[10]), int(m[12])
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.qx_cuda_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _call(self, name, *args):
+        err = err_buf()
+        check(getattr(self.lib, name)(self.h, *args, err, len(err)), err, name)
+
+    def reset(self):
+        self._call("qx_cuda_reset")
+
+    def decode_step(self, token, position, want_logits=False, want_residual=False, want_experts=False):
+        nxt = np.zeros(1, np.uint32)
+        logits = np.zeros(self.vocab, np.float32) if want_logits else None
+        res = np.zeros(self.hidden, np.float32) if want_residual else None
+        ex = np.zeros((self.layers, 8), np.uint32) if want_experts else None
+        rw = np.zeros((self.layers, 8), np.float32) if want_experts else None
+        self._call("qx_cuda_decode_step", token, position, _p(nxt), _p(logits), _p(res), _p(ex), _p(rw))
+        return dict(token=int(nxt[0]), logits=logits, residual=res, experts=ex, routing=rw)
+
+    def generate(self, token, position, steps):
+        out = np.zeros(steps, np.uint32)
+        self._call("qx_cuda_generate", token, position, steps, _p(out))
+        return out
+
+    def final_head(self, residual, top_n=8):
+        residual = np.ascontiguousarray(residual, np.float32)
+        normed = np.zeros(self.hidden, np.float32)
+        logits = np.zeros(self.vocab, np.float32)
+        tt = np.zeros(top_n, np.uint32)
+        tl = np.zeros(top_n, np.float32)
+        self._call("qx_cuda_final_head", _p(residual), _p(normed), _p(logits), top_n, _p(tt), _p(tl))
+        return normed, logits, tt, tl
+
+    def moe_layer(self, layer, x):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros(self.hidden, np.float32)
+        moe = np.zeros(self.hidden, np.float32)
+        sel = np.zeros(8, np.uint32)
+        w = np.zeros(8, np.float32)
+        self._call("qx_cuda_moe_layer", layer, _p(x), _p(out), _p(moe), _p(sel), _p(w))
+        return out, moe, sel, w
+
+    def attention_layer(self, layer, position, residual):
+        res = np.array(residual, np.float32, copy=True)
+        ao = np.zeros(self.hidden, np.float32)
+        ctxv = np.zeros(self.q_heads * self.head_dim, np.float32)
+        self._call("qx_cuda_attention_layer", layer, position, _p(res), _p(ao), _p(ctxv))
+        return res, ao, ctxv
+
+    def embed(self, token):
+        out = np.zeros(self.hidden, np.float32)
+        self._call("qx_cuda_embed", token, _p(out))
+        return out
+
+    def kv_write(self, layer, first, k, v, ks, vs):
+        k, v = np.ascontiguousarray(k, np.int8), np.ascontiguousarray(v, np.int8)
+        ks, vs = np.ascontiguousarray(ks, np.float32), np.ascontiguousarray(vs, np.float32)
+        self._call("qx_cuda_kv_write", layer, first, len(ks), _p(k), _p(v), _p(ks), _p(vs))
+
+    def kv_read(self, layer, first, count):
+        kvv = self.kv_heads * self.head_dim
+        k = np.zeros((count, kvv), np.int8)
+        v = np.zeros((count, kvv), np.int8)
+        ks = np.zeros(count, np.float32)
+        vs = np.zeros(count, np.float32)
+        self._call("qx_cuda_kv_read", layer, first, count, _p(k), _p(v), _p(ks), _p(vs))
+        return k, v, ks, vs
+
+    def profile(self):
+        p = CudaProfile()
+        self.lib.qx_cuda_profile_get(self.h, C.byref(p))
+        return {f: (getattr(p, f).decode() if f == "backend" else int(getattr(p, f))) for f, _ in p._fields_}
+
+    def time_kernels(self, token, position, steps):
+        names = C.create_string_buffer(4096)
+        ms = np.zeros(64, np.float32)
+        ln = np.zeros(64, np.uint32)
+        cnt = np.zeros(1, np.uint32)
+        self._call("qx_cuda_time_kernels", token, position, steps, names, len(names), _p(ms), _p(ln), 64, _p(cnt))
+        keys = names.value.decode().split(";")
+        return {k: (float(ms[i]), int(ln[i])) for i, k in enumerate(keys[:int(cnt[0])])}
+
+    def stream(self):
+        return self.lib.qx_cuda_stream(self.h)

@@ -1,0 +1,252 @@
+"""CUDA engine parity through the C ABI (include/qx_cuda.h) on a B200.
+
+Checked against the reference's own outputs (tests/golden/, produced by
+src/qx_format.c compiled unchanged) and, where no fixture exists, against the
+C restatement in oracle/ that test_oracle_pin.py pins bit-exact to the
+reference.  Indices (top-8 experts, argmax tokens) must match exactly; float
+vectors within 1e-4 relative (tests/qxtol.py).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import qxlib
+import workloads as W
+from qxtol import assert_close, rel_err
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def gold(name):
+    with open(os.path.join(GOLD, name)) as f:
+        return json.load(f)
+
+
+def f32(a):
+    return np.asarray(a, np.float32)
+
+
+@pytest.fixture(scope="module")
+def mini(mini_image):
+    e = qxlib.Engine(mini_image, ctx=256)
+    yield e
+    e.close()
+
+
+@pytest.fixture(scope="module")
+def full(full_image):
+    e = qxlib.Engine(full_image, ctx=4096)
+    yield e
+    e.close()
+
+
+def port_quantizer(port):
+    def q(vec):
+        vec = np.ascontiguousarray(vec, np.float32)
+        out = np.zeros(vec.size, np.int8)
+        s = port.f["quantize_int8"](vec.ctypes.data, out.ctypes.data, vec.size)
+        return out, np.float32(s)
+    return q
+
+
+# ---------------------------------------------------------------- mini model
+def test_embed_is_bit_exact(mini):
+    g = gold("golden_mini.json")
+    np.testing.assert_array_equal(mini.embed(g["embed_token"]), f32(g["embed"]))
+
+
+def test_head_mini(mini):
+    g = gold("golden_mini.json")["head"]
+    normed, logits, tt, tl = mini.final_head(W.head_input(mini.hidden), 8)
+    assert_close(logits, g["logits"], what="logits")
+    assert_close(normed, g["normalized"], rel=1e-6, what="final norm")
+    assert list(tt) == g["top_tokens"][:8]
+
+
+def test_moe_mini_every_layer(mini, port, mini_image):
+    P = port.open_image(mini_image)
+    for layer in range(mini.layers):
+        for seed in (1, 2, 3):
+            x = qxlib.normal_vector(seed, mini.hidden)
+            lo, moe, sel, w = mini.moe_layer(layer, x)
+            rlo, rmoe, rsel, rw = P.moe_layer(layer, x)
+            assert list(sel) == list(rsel)
+            assert_close(w, rw, rel=1e-6, what="routing weights")
+            assert_close(moe, rmoe, what="moe output")
+            assert_close(lo, rlo, what="layer output")
+
+
+def test_attention_mini_history(mini):
+    g = gold("golden_mini.json")["attention"]
+    import oracle_bind
+    q = port_quantizer(oracle_bind.Checker("port"))
+    layer = g["layer"]
+    kvv = mini.kv_heads * mini.head_dim
+    for case in g["cases"]:
+        P = case["position"]
+        mini.reset()
+        if P:
+            k, v, ks, vs = W.attn_history(P, kvv, q)
+            mini.kv_write(layer, 0, k, v, ks, vs)
+        res, ao, ctxv = mini.attention_layer(layer, P, W.attn_input(mini.hidden))
+        assert_close(ctxv, case["context"], what="context P=%d" % P)
+        assert_close(ao, case["attn_out"], what="attention output P=%d" % P)
+        assert_close(res, case["residual"], what="residual P=%d" % P)
+        k, v, ks, vs = mini.kv_read(layer, P, 1)
+        assert abs(ks[0] - case["k_scale"]) <= 1e-5 * case["k_scale"]
+        assert abs(vs[0] - case["v_scale"]) <= 1e-5 * case["v_scale"]
+        assert np.max(np.abs(k[0].astype(int) - np.asarray(case["k_row"]))) <= 1
+        assert np.max(np.abs(v[0].astype(int) - np.asarray(case["v_row"]))) <= 1
+
+
+def test_attention_mini_matches_port_over_many_positions(mini, port, mini_image):
+    """Positions 0..199 appended one by one (crosses three 64-token chunks)."""
+    P = port.open_image(mini_image)
+    kv = P.new_kv(mini.ctx)
+    mini.reset()
+    for step in range(200):
+        x = qxlib.normal_vector(500 + step, mini.hidden)
+        res, ao, ctxv = mini.attention_layer(1, step, x)
+        rres, rao, rctx, _, _ = P.attention_layer(1, step, kv, x)
+        assert_close(ctxv, rctx, what="context step %d" % step)
+        assert_close(res, rres, what="residual step %d" % step)
+
+
+def test_decode_mini_matches_reference(mini):
+    g = gold("golden_mini.json")["decode"]
+    mini.reset()
+    tok = g[0]["input"]
+    for s, st in enumerate(g):
+        r = mini.decode_step(tok, s, want_residual=True, want_experts=True)
+        assert r["token"] == st["token"], "step %d" % s
+        np.testing.assert_array_equal(r["experts"], np.asarray(st["experts"], np.uint32))
+        if st["residual"] is not None:
+            assert_close(r["residual"], st["residual"], what="final residual step %d" % s)
+        tok = r["token"]
+
+
+def test_generate_equals_stepwise_decode(mini):
+    mini.reset()
+    steps = []
+    tok = W.START_TOKEN
+    for s in range(40):
+        tok = mini.decode_step(tok, s)["token"]
+        steps.append(tok)
+    mini.reset()
+    gen = mini.generate(W.START_TOKEN, 0, 40)
+    assert list(gen) == steps
+    mini.reset()
+    again = mini.generate(W.START_TOKEN, 0, 40)
+    assert list(again) == steps
+
+
+def test_generate_mini_matches_port(mini, port, mini_image):
+    P = port.open_image(mini_image)
+    kv = P.new_kv(mini.ctx)
+    want = []
+    tok = W.START_TOKEN
+    for s in range(100):
+        tok = P.decode_step(tok, s, kv)["token"]
+        want.append(tok)
+    mini.reset()
+    assert list(mini.generate(W.START_TOKEN, 0, 100)) == want
+
+
+def test_errors_fail_closed(mini):
+    with pytest.raises(RuntimeError, match="prompt token out of range"):
+        mini.decode_step(mini.vocab, 0)
+    with pytest.raises(RuntimeError, match="steps exceed ctx"):
+        mini.decode_step(1, mini.ctx)
+    with pytest.raises(RuntimeError, match="steps exceed ctx"):
+        mini.generate(1, mini.ctx - 2, 4)
+    # still usable afterwards
+    mini.reset()
+    assert mini.decode_step(W.START_TOKEN, 0)["token"] == gold("golden_mini.json")["decode"][0]["token"]
+
+
+def test_profile_counts_traffic(mini):
+    p0 = mini.profile()
+    mini.decode_step(W.START_TOKEN, 0)
+    p1 = mini.profile()
+    assert p1["backend"] == "b200-sm100a"
+    assert p1["decode_steps"] == p0["decode_steps"] + 1
+    assert p1["host_to_device_bytes"] - p0["host_to_device_bytes"] == 8
+    assert p1["device_to_host_bytes"] - p0["device_to_host_bytes"] == 8
+    assert p1["kernel_launches"] - p0["kernel_launches"] == 2 + 6 * mini.layers
+
+
+# ---------------------------------------------------------------- full size
+def test_config1_head(full):
+    g = gold("golden_full.json")["head"]
+    normed, logits, tt, tl = full.final_head(W.head_input(full.hidden), 32)
+    assert list(tt) == g["top_tokens"]
+    assert_close(tl, g["top_logits"], what="top logits")
+    assert_close(logits[g["logits_sample_idx"]], g["logits_sample"], what="logits")
+    assert_close(normed, g["normalized"], rel=1e-6, what="final norm")
+    assert abs(float(np.sum(logits, dtype=np.float64)) - g["logits_sum"]) <= 1e-4 * np.sqrt(g["logits_sumsq"])
+
+
+def test_config2_moe_layer(full):
+    g = gold("golden_full.json")["moe"]
+    lo, moe, sel, w = full.moe_layer(g["layer"], W.moe_input(full.hidden))
+    assert list(sel) == g["selected"]
+    assert_close(w, g["weights"], rel=1e-6, what="routing weights")
+    assert_close(moe, g["moe_output"], what="moe output")
+    assert_close(lo, g["layer_output"], what="layer output")
+
+
+@pytest.mark.parametrize("case_index", [0, 1])
+def test_config3_attention_with_history(full, port, case_index):
+    g = gold("golden_full.json")["attention"]
+    case = g["cases"][case_index]
+    P, layer = case["position"], g["layer"]
+    full.reset()
+    k, v, ks, vs = W.attn_history(P, full.kv_heads * full.head_dim, port_quantizer(port))
+    full.kv_write(layer, 0, k, v, ks, vs)
+    res, ao, ctxv = full.attention_layer(layer, P, W.attn_input(full.hidden))
+    assert_close(ctxv, case["context"], what="context ctx=%d" % (P + 1))
+    assert_close(ao, case["attn_out"], what="attention output ctx=%d" % (P + 1))
+    assert_close(res, case["residual"], what="residual ctx=%d" % (P + 1))
+
+
+def test_config4_first_steps_match_reference(full):
+    g = gold("golden_full.json")["decode"]
+    full.reset()
+    tok = g[0]["input"]
+    for s, st in enumerate(g):
+        r = full.decode_step(tok, s, want_residual=True, want_experts=True)
+        assert r["token"] == st["token"], "step %d" % s
+        np.testing.assert_array_equal(r["experts"], np.asarray(st["experts"], np.uint32))
+        assert_close(r["routing"], np.asarray(st["routing"]).reshape(-1, 8), rel=1e-4, what="routing")
+        if st["residual"] is not None:
+            assert_close(r["residual"], st["residual"], what="final residual step %d" % s)
+        tok = r["token"]
+
+
+def test_config4_256_steps_teacher_forced(full, full_image, port):
+    """256 greedy steps on the device; then, at sampled positions, the CPU
+    checker continues from the engine's own KV and token and must pick the same
+    token and the same top-8 experts in every layer."""
+    full.reset()
+    toks = full.generate(W.START_TOKEN, 0, W.DECODE_STEPS)
+    assert len(set(toks.tolist())) > 1
+    P = port.open_image(full_image)
+    inputs = [W.START_TOKEN] + toks.tolist()
+    for s in (0, 17, 128, 255):
+        kv = P.new_kv(s + 1)
+        for layer in range(full.layers):
+            if s:
+                k, v, ks, vs = full.kv_read(layer, 0, s)
+                kv["k"][layer, :s], kv["v"][layer, :s], kv["ks"][layer, :s], kv["vs"][layer, :s] = k, v, ks, vs
+        r = P.decode_step(inputs[s], s, kv)
+        assert r["token"] == toks[s], "step %d" % s
+        full.reset()
+        for layer in range(full.layers):
+            if s:
+                full.kv_write(layer, 0, kv["k"][layer, :s], kv["v"][layer, :s], kv["ks"][layer, :s], kv["vs"][layer, :s])
+        e = full.decode_step(inputs[s], s, want_experts=True)
+        np.testing.assert_array_equal(e["experts"], r["experts"], err_msg="experts at step %d" % s)
+        assert e["token"] == r["token"]
