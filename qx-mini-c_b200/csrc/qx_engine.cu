@@ -31,7 +31,7 @@ struct Op {                  // one launch of the per-token sequence
 };
 
 enum OpKind { kEmbed, kQkv, kAttn, kOproj, kRouter, kGateup, kDown, kHead };
-const char* kOpNames[] = {"embed_q4k", "qkv_iq4xs", "attn_splitkv", "oproj_iq4xs",
+const char* kOpNames[] = {"embed_q4k", "qkv_iq4xs", "attn_int8kv", "oproj_iq4xs",
                           "router_top8", "gateup_iq2xs_swiglu", "down_iq3xxs_wsum", "head_q6k_argmax"};
 
 }  // namespace
@@ -169,7 +169,7 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         dm.q_heads % dm.kv_heads || dm.q_heads / dm.kv_heads > 8 || dm.head_dim != 128 || dm.q_dim() % 256 ||
         dm.q_dim() > 8192 || dm.vocab < 16 || dm.vocab % 16 || dm.experts < 8 || dm.experts > 256 ||
         model->experts_per_token != 8 || dm.moe_inter < 256 || dm.moe_inter % 256 || dm.moe_inter > 2048 ||
-        dm.ctx < 1 || dm.ctx > 65536) {
+        dm.ctx < 1 || dm.ctx > 65536 || !qx::geometry_supported(dm)) {
         set_err(err, n, "unsupported model geometry for the B200 engine");
         return 0;
     }
@@ -267,8 +267,7 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     d.tok_embd = W("token_embd.weight");
     d.out_norm = (const float*)W("output_norm.weight");
     d.head = W("output.weight");
-    d.nsplit = (dm.ctx + qx::kAttnChunk - 1) / qx::kAttnChunk;
-    d.head_grid = qx::head_grid_size(dev);
+    d.head_grid = qx::head_grid_size(dev, dm);
     const size_t L = dm.layers, C = dm.ctx, D = dm.head_dim;
     struct Slot { void** p; size_t bytes; };
     std::vector<Slot> slots;
@@ -283,7 +282,7 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     add((void**)&d.vcache, L * C * KV);
     add((void**)&d.kscale, L * C * 4);
     add((void**)&d.vscale, L * C * 4);
-    add((void**)&d.attn_part, (size_t)dm.q_heads * d.nsplit * (D + 2) * 4);
+    add((void**)&d.attn_scores, qx::attn_scores_bytes(dm));
     add((void**)&d.ctxv, Q * 4);
     add((void**)&d.attn_out, H * 4);
     add((void**)&d.moe_out, H * 4);

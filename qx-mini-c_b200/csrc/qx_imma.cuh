@@ -189,7 +189,10 @@ __device__ __forceinline__ uint32_t kv_lookup4(uint32_t n, const uint32_t K[4]) 
     const uint32_t sel = __byte_perm(packed, 0u, 0x0020);         // n0 | n1<<4 | n2<<8 | n3<<12
     const uint32_t lo = __byte_perm(K[0], K[1], sel), hi = __byte_perm(K[2], K[3], sel);
     const uint32_t hbit = (n & 0x08080808u) << 4;                  // bit 3 -> bit 7
-    const uint32_t mask = __byte_perm(hbit, 0u, 0xba98);          // replicate bit 7 over each byte
+    uint32_t mask;                                                // replicate bit 7 over each byte
+    // PTX prmt in its default mode honours the sign-replicate bit of each
+    // selector nibble (CUDA's __byte_perm ignores it).
+    asm("prmt.b32 %0, %1, 0, 0xba98;" : "=r"(mask) : "r"(hbit));
     return (hi & mask) | (lo & ~mask);
 }
 

@@ -1,10 +1,18 @@
-// sm_100a kernels of one greedy decode step.  Every weight matrix is read in
-// its native GGUF block layout: row tiles are streamed into shared memory with
-// cp.async and decoded there by one warp per row.  Accumulation is F32 for the
-// quantized matvecs; norms, the router, the softmax weights and SwiGLU use
-// double where the reference does (src/qx_format.c cited per kernel).
+// sm_100a kernels of one greedy decode step.
+//
+// Matvecs: weight row tiles (16 rows, native GGUF blocks) are streamed into
+// shared memory with cp.async, issued before the prologue so the DRAM latency
+// overlaps the activation preparation; each warp reduces a 16-row tile over a
+// range of blocks with exact integer tensor-core dots (qx_imma.cuh), partial
+// sums are combined in a fixed order, so every output is the correctly
+// rounded float of a double-accurate dot product, as in the reference's
+// double accumulation (src/qx_format.c:4266-4280, :4774-4783, :3683-3711).
+// Norms, RoPE, router softmax, SwiGLU and the attention softmax use double,
+// and the attention context is accumulated in float in position order, the
+// way qx_rope_gqa_attention_partial does it (src/qx_format.c:5127-5172).
 #include <cfloat>
 
+#include "qx_imma.cuh"
 #include "qx_kernels.h"
 
 namespace qx {
@@ -14,39 +22,43 @@ namespace qx {
 // ---------------------------------------------------------------------------
 
 // xs[i] = (float)((double)x[i] / rms) * w[i], rms = sqrt(sum x^2 / n + 1e-6)
-// computed in double (qx_apply_f32_rmsnorm, src/qx_format.c:3358-3371).
+// in double (qx_apply_f32_rmsnorm, src/qx_format.c:3358-3371).
 __device__ void rmsnorm_to_smem(const float* x, const float* w, float* xs, int n, double* scratch) {
     double ss = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = x[i];
-        xs[i] = v;
-        ss += (double)v * (double)v;
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(x + i);
+        *reinterpret_cast<float4*>(xs + i) = v;
+        ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y;
+        ss += (double)v.z * (double)v.z + (double)v.w * (double)v.w;
     }
     ss = block_sum_d(ss, scratch);
     const double rms = sqrt(ss / (double)n + 1.0e-6);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = (float)((double)xs[i] / rms) * w[i];
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
+        const float4 wv = *reinterpret_cast<const float4*>(w + i);
+        float4 v = *reinterpret_cast<float4*>(xs + i);
+        v.x = (float)((double)v.x / rms) * wv.x;
+        v.y = (float)((double)v.y / rms) * wv.y;
+        v.z = (float)((double)v.z / rms) * wv.z;
+        v.w = (float)((double)v.w / rms) * wv.w;
+        *reinterpret_cast<float4*>(xs + i) = v;
+    }
     __syncthreads();
 }
 
 __device__ void copy_to_smem(const float* x, float* xs, int n) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[i];
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
     __syncthreads();
 }
 
-// CTA copy of a table (bytes a multiple of 4, both 4-byte aligned); the caller syncs.
-__device__ __forceinline__ void copy_words(void* dst, const void* src, size_t bytes) {
-    for (size_t i = threadIdx.x; i < bytes / 4; i += blockDim.x)
-        reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
-}
-
-__device__ __forceinline__ float finite_or_zero(float v) { return isfinite(v) ? v : 0.0f; }
+__device__ __forceinline__ float finite_or_zero_d(double v) { return isfinite(v) ? (float)v : 0.0f; }
 
 __device__ __forceinline__ uint8_t* align16(uint8_t* p) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 15u) & ~(uintptr_t)15u);
 }
 
-// last-CTA ticket: returns true in exactly one CTA, after all `expected`
-// CTAs have made their global writes visible.
+// last-CTA ticket: true in exactly one CTA, after all `expected` CTAs made
+// their global writes visible.
 __device__ __forceinline__ bool last_cta(unsigned* counter, unsigned expected) {
     __shared__ bool is_last;
     __threadfence();
@@ -55,6 +67,46 @@ __device__ __forceinline__ bool last_cta(unsigned* counter, unsigned expected) {
     __syncthreads();
     if (is_last) __threadfence();
     return is_last;
+}
+
+// Shared-memory carve-up helper.
+struct Carve {
+    uint8_t* p;
+    __device__ explicit Carve(uint8_t* base) : p(base) {}
+    template <class T>
+    __device__ T* take(size_t count) {
+        p = align16(p);
+        T* r = reinterpret_cast<T*>(p);
+        p += count * sizeof(T);
+        return r;
+    }
+};
+
+__device__ __forceinline__ void load_kv_regs(const Tables* t, uint32_t K[4]) {
+    // IQ4_NL codebook as 16 signed bytes in 4 registers
+    for (int j = 0; j < 4; ++j) {
+        uint32_t w = 0;
+        for (int k = 0; k < 4; ++k) w |= ((uint32_t)(uint8_t)(int8_t)t->kvalues[4 * j + k]) << (8 * k);
+        K[j] = w;
+    }
+}
+
+// Sum the per-part tile partials in part order and return the row value.
+__device__ __forceinline__ double sum_parts(const double* part, int tile, int parts, int row) {
+    double v = 0.0;
+    for (int p = 0; p < parts; ++p) v += part[(tile * parts + p) * kTileRows + row];
+    return v;
+}
+
+// Store the two rows a warp finished (lane t = 0 of each group g).
+__device__ __forceinline__ void store_tile_rows(double* part, int warp, const Acc& acc) {
+    double lo, hi;
+    acc.finish(lo, hi);
+    const int lane = threadIdx.x & 31;
+    if ((lane & 3) == 0) {
+        part[warp * kTileRows + (lane >> 2)] = lo;
+        part[warp * kTileRows + (lane >> 2) + 8] = hi;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -68,8 +120,8 @@ __global__ void __launch_bounds__(256) k_embed(Dev d) {
     }
     const int nblk = d.dm.hidden / 256;
     const uint8_t* row = d.tok_embd + (size_t)tok * (size_t)(nblk * 144);
-    const int t = threadIdx.x;          // value index within each block
-    const int c = t >> 6, l = t & 63;   // 64-value chunk, position inside it
+    const int t = threadIdx.x;
+    const int c = t >> 6, l = t & 63;
     for (int b = 0; b < nblk; ++b) {
         const uint8_t* blk = row + b * 144;
         const float dd = h2f(ld16(blk)), dmin = h2f(ld16(blk + 2));
@@ -81,228 +133,238 @@ __global__ void __launch_bounds__(256) k_embed(Dev d) {
         const uint8_t qb = blk[16 + 32 * c + (l & 31)];
         const uint32_t q = l < 32 ? (qb & 15u) : (qb >> 4);
         // d*sc*q - dmin*m with each product rounded to float, no contraction
-        const float v = __fsub_rn(__fmul_rn(__fmul_rn(dd, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
-        d.x[b * 256 + t] = v;
+        d.x[b * 256 + t] = __fsub_rn(__fmul_rn(__fmul_rn(dd, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
     }
 }
 
 // ---------------------------------------------------------------------------
-// Q/K/V projections (qx_projection_matvec_fill_mode, src/qx_format.c:4207-4297)
-// with the attention RMSNorm (:6283-6290) fused in the prologue.
+// Q/K/V projections with the attention RMSNorm in the prologue
+// (qx_projection_matvec_fill_mode, src/qx_format.c:4207-4297; :6283-6290).
+// 2 tiles per CTA, 4 block-parts per tile.
 // ---------------------------------------------------------------------------
-constexpr int kSmallStages = 2;
+constexpr int kQkvTiles = 2;
 
 __global__ void __launch_bounds__(kThreads) k_qkv(Dev d, LayerW w) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ double scratch[kWarps];
-    __shared__ float kvals[16];
     const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
-    if (threadIdx.x < 16) kvals[threadIdx.x] = d.tables->kvalues[threadIdx.x];
-    float* xs = reinterpret_cast<float*>(smem);
-    uint8_t* ring = align16(smem + (size_t)H * 4);
-    rmsnorm_to_smem(d.x, w.attn_norm, xs, H, scratch);
     const int nblk = H / 256;
-    const uint32_t rb = (uint32_t)nblk * 136u, stage = (uint32_t)kTileRows * rb;
+    const uint32_t rb = (uint32_t)nblk * 136u, tb = (uint32_t)kTileRows * rb;
+    Carve cv(smem);
+    uint8_t* tiles = cv.take<uint8_t>(kQkvTiles * tb);
+    float* xs = cv.take<float>(H);
+    uint32_t* xb = cv.take<uint32_t>(H / 16 * 32);
+    int* sb = cv.take<int>(H / 256);
+    double* part = cv.take<double>(kWarps * kTileRows);
     const int ntiles = (Q + 2 * KV) / kTileRows;
+    for (int k = 0; k < kQkvTiles; ++k) {
+        const int t = blockIdx.x * kQkvTiles + k;
+        if (t >= ntiles) break;
+        const int r0 = t * kTileRows;
+        const uint8_t* src = r0 < Q ? w.wq + (size_t)r0 * rb
+                             : r0 < Q + KV ? w.wk + (size_t)(r0 - Q) * rb
+                                           : w.wv + (size_t)(r0 - Q - KV) * rb;
+        stage_copy(tiles + k * tb, src, tb);
+    }
+    cp_async_commit();
+    uint32_t K4[4];
+    load_kv_regs(d.tables, K4);
+    rmsnorm_to_smem(d.x, w.attn_norm, xs, H, scratch);
+    build_xq(xs, H, xb, sb);
+    cp_async_wait<0>();
+    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    tile_pipeline<kSmallStages>(
-        ntiles, stage, ring,
-        [&](int t, uint8_t* dst) {
-            const int r0 = t * kTileRows;
-            const uint8_t* src = r0 < Q ? w.wq + (size_t)r0 * rb
-                                 : r0 < Q + KV ? w.wk + (size_t)(r0 - Q) * rb
-                                               : w.wv + (size_t)(r0 - Q - KV) * rb;
-            stage_copy(dst, src, stage);
-        },
-        [&](int t, const uint8_t* s) {
-            for (int r = warp; r < kTileRows; r += kWarps) {
-                const float acc = dot_iq4_xs(s + r * rb, xs, nblk, kvals, lane);
-                if (lane == 0) d.qkv[t * kTileRows + r] = finite_or_zero(acc);
-            }
-        });
+    const int parts = kWarps / kQkvTiles, tile = warp / parts, p = warp % parts;
+    const int t = blockIdx.x * kQkvTiles + tile;
+    if (t < ntiles) {
+        const uint8_t* base = tiles + tile * tb;
+        Acc acc{};
+        const int g = lane >> 2;
+        dot_iq4_xs_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, K4,
+                       lane, acc);
+        store_tile_rows(part, warp, acc);
+    }
+    __syncthreads();
+    if (threadIdx.x < kQkvTiles * kTileRows) {
+        const int tl = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows;
+        const int tt = blockIdx.x * kQkvTiles + tl;
+        if (tt < ntiles) d.qkv[tt * kTileRows + r] = finite_or_zero_d(sum_parts(part, tl, parts, r));
+    }
 }
 
 // ---------------------------------------------------------------------------
-// Split-KV GQA attention over the INT8 cache, with the per-head Q/K RMSNorm
-// (:3740-3757), split-half RoPE (:4625-4641), the INT8 quantize-and-append of
-// the current K/V (:4449-4463, :6343-6400) and the softmax/context of
-// qx_rope_gqa_attention_partial (:5127-5172).  Grid: (kv_heads, nsplit); each
-// CTA handles the 8 query heads of one KV head over one 64-position chunk;
-// the last CTA of each KV head merges the chunks.
+// Attention for one query head per CTA (128 threads = head dims), exact
+// reference order: per-head Q/K RMSNorm (:3740-3757), split-half RoPE
+// (:4625-4641), INT8 quantize-and-append of the current K/V (:4449-4463,
+// :6343-6400), scores and softmax in double, context accumulated in float over
+// positions 0..pos in order (:5127-5172).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_attn(Dev d, LayerW w, int layer) {
-    const int D = d.dm.head_dim, KVH = d.dm.kv_heads, QH = d.dm.q_heads, group = QH / KVH;
+__device__ __forceinline__ double block_max_d(double v, double* scratch) {
+    for (int o = 16; o; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+    __syncthreads();
+    double m = scratch[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmax(m, scratch[i]);
+    return m;
+}
+
+__device__ __forceinline__ float block_max_f(float v, float* scratch) {
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float m = scratch[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, scratch[i]);
+    return m;
+}
+
+// Head RMSNorm (double) + RoPE (double, host table) of one 128-wide head held
+// in v[0..127] (shared memory); all 128 threads call.
+__device__ void head_norm_rope(float* v, const float* nw, const double* rope, double* scratch) {
+    const int i = threadIdx.x;
+    const double x = (double)v[i];
+    const double ss = block_sum_d(x * x, scratch);
+    const double inv = 1.0 / sqrt(ss / 128.0 + 1.0e-6);
+    const float y = (float)(x * inv * (double)nw[i]);
+    __syncthreads();
+    v[i] = y;
+    __syncthreads();
+    if (i < 64) {
+        const double c = rope[2 * i], s = rope[2 * i + 1];
+        const float x0 = v[i], x1 = v[i + 64];
+        v[i] = (float)((double)x0 * c - (double)x1 * s);
+        v[i + 64] = (float)((double)x0 * s + (double)x1 * c);
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
+    const int D = 128, KVH = d.dm.kv_heads, QH = d.dm.q_heads, group = QH / KVH;
     const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx;
-    const int g = blockIdx.x, split = blockIdx.y;
+    const int h = blockIdx.x, g = h / group, i = threadIdx.x;
     const int pos = *d.pos;
     if (pos < 0 || pos >= ctx) {
-        if (threadIdx.x == 0 && g == 0 && split == 0) atomicOr(d.err, kErrPosition);
+        if (i == 0 && h == 0) atomicOr(d.err, kErrPosition);
         return;
     }
-    if (split * kAttnChunk > pos) return;
-    const int nact = pos / kAttnChunk + 1;
-    extern __shared__ __align__(16) uint8_t smem[];
-    float* kcur = reinterpret_cast<float*>(smem);        // [KV]
-    float* vcur = kcur + KV;                               // [KV]
-    float* qs = vcur + KV;                                 // [group][D]
-    float* sc = qs + group * D;                            // [group][kAttnChunk]
-    int8_t* k8 = reinterpret_cast<int8_t*>(sc + group * kAttnChunk);   // [KV]
-    int8_t* v8 = k8 + KV;
-    __shared__ float red[2][kWarps];
-    __shared__ float scales[2];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const double* rope = d.rope + (size_t)pos * (D / 2) * 2;
-
-    for (int i = threadIdx.x; i < KV; i += blockDim.x) {
-        kcur[i] = d.qkv[Q + i];
-        vcur[i] = d.qkv[Q + KV + i];
+    __shared__ double scratch_d[4];
+    __shared__ float scratch_f[4];
+    __shared__ float qv[128];
+    __shared__ float kcur[1024];
+    __shared__ float vcur[1024];
+    __shared__ __align__(16) int8_t k8[1024];
+    __shared__ __align__(16) int8_t v8[1024];
+    const double* rope = d.rope + (size_t)pos * 128;
+    for (int j = i; j < KV; j += 128) {
+        kcur[j] = d.qkv[Q + j];
+        vcur[j] = d.qkv[Q + KV + j];
     }
-    for (int i = threadIdx.x; i < group * D; i += blockDim.x) qs[i] = d.qkv[(g * group) * D + i];
+    qv[i] = d.qkv[h * D + i];
     __syncthreads();
-    // head RMSNorm + RoPE: warps [0, KVH) take the K heads, the rest the Q heads of this group
-    for (int hh = warp; hh < KVH + group; hh += nw) {
-        float* v = hh < KVH ? kcur + hh * D : qs + (hh - KVH) * D;
-        const float* nwt = hh < KVH ? w.k_norm : w.q_norm;
-        double ss = 0.0;
-        for (int i = lane; i < D; i += 32) ss += (double)v[i] * (double)v[i];
-        ss = warp_sum_d(ss);
-        const double inv = 1.0 / sqrt(ss / (double)D + 1.0e-6);
-        for (int i = lane; i < D; i += 32) v[i] = (float)((double)v[i] * inv * (double)nwt[i]);
-        __syncwarp();
-        for (int i = lane; i < D / 2; i += 32) {
-            const double c = rope[2 * i], s = rope[2 * i + 1];
-            const float x0 = v[i], x1 = v[i + D / 2];
-            v[i] = (float)((double)x0 * c - (double)x1 * s);
-            v[i + D / 2] = (float)((double)x0 * s + (double)x1 * c);
-        }
-        __syncwarp();
-    }
-    __syncthreads();
-    // one INT8 scale for all KV values of this token (K and V separately)
+    for (int kh = 0; kh < KVH; ++kh) head_norm_rope(kcur + kh * D, w.k_norm, rope, scratch_d);
+    head_norm_rope(qv, w.q_norm, rope, scratch_d);
+    // one INT8 scale over all KV values of the token (K and V separately)
     float ka = 0.f, va = 0.f;
-    for (int i = threadIdx.x; i < KV; i += blockDim.x) {
-        ka = fmaxf(ka, isfinite(kcur[i]) ? fabsf(kcur[i]) : 0.f);
-        va = fmaxf(va, isfinite(vcur[i]) ? fabsf(vcur[i]) : 0.f);
+    for (int j = i; j < KV; j += 128) {
+        ka = fmaxf(ka, isfinite(kcur[j]) ? fabsf(kcur[j]) : 0.f);
+        va = fmaxf(va, isfinite(vcur[j]) ? fabsf(vcur[j]) : 0.f);
     }
-    for (int o = 16; o; o >>= 1) {
-        ka = fmaxf(ka, __shfl_xor_sync(0xffffffffu, ka, o));
-        va = fmaxf(va, __shfl_xor_sync(0xffffffffu, va, o));
-    }
-    if (lane == 0) { red[0][warp] = ka; red[1][warp] = va; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float a = 0.f, b = 0.f;
-        for (int i = 0; i < nw; ++i) { a = fmaxf(a, red[0][i]); b = fmaxf(b, red[1][i]); }
-        scales[0] = a > 0.f ? a / 127.0f : 1.0f;
-        scales[1] = b > 0.f ? b / 127.0f : 1.0f;
-    }
-    __syncthreads();
-    const float ksc = scales[0], vsc = scales[1];
-    for (int i = threadIdx.x; i < KV; i += blockDim.x) {
-        int qk = isfinite(kcur[i]) ? (int)lrintf(kcur[i] / ksc) : 0;
-        int qv = isfinite(vcur[i]) ? (int)lrintf(vcur[i] / vsc) : 0;
-        k8[i] = (int8_t)max(-127, min(127, qk));
-        v8[i] = (int8_t)max(-127, min(127, qv));
+    ka = block_max_f(ka, scratch_f);
+    va = block_max_f(va, scratch_f);
+    const float ksc = ka > 0.f ? ka / 127.0f : 1.0f, vsc = va > 0.f ? va / 127.0f : 1.0f;
+    for (int j = i; j < KV; j += 128) {
+        const int qk = isfinite(kcur[j]) ? (int)lrintf(kcur[j] / ksc) : 0;
+        const int qq = isfinite(vcur[j]) ? (int)lrintf(vcur[j] / vsc) : 0;
+        k8[j] = (int8_t)max(-127, min(127, qk));
+        v8[j] = (int8_t)max(-127, min(127, qq));
     }
     __syncthreads();
     const size_t slot = (size_t)layer * ctx + pos;
-    if (g == 0 && split == 0) {
-        for (int i = threadIdx.x; i < KV; i += blockDim.x) {
-            d.kcache[slot * KV + i] = k8[i];
-            d.vcache[slot * KV + i] = v8[i];
+    if (h == 0) {
+        for (int j = i; j < KV; j += 128) {
+            d.kcache[slot * KV + j] = k8[j];
+            d.vcache[slot * KV + j] = v8[j];
         }
-        if (threadIdx.x == 0) { d.kscale[slot] = ksc; d.vscale[slot] = vsc; }
+        if (i == 0) { d.kscale[slot] = ksc; d.vscale[slot] = vsc; }
     }
-    // scores for this chunk: warp h <-> query head g*group + h
-    const int t0 = split * kAttnChunk, n = min(kAttnChunk, pos + 1 - t0);
-    const float inv_sqrt_d = (float)(1.0 / sqrt((double)D));
-    for (int h = warp; h < group; h += nw) {
-        const float* q = qs + h * D;
-        for (int tt = 0; tt < n; ++tt) {
-            const int t = t0 + tt;
-            const size_t st = (size_t)layer * ctx + t;
-            const int8_t* kp = t == pos ? k8 + g * D : d.kcache + st * KV + g * D;
-            const float ks = t == pos ? ksc : d.kscale[st];
-            float s = 0.f;
-            for (int i = lane; i < D; i += 32) s = fmaf(q[i], (float)kp[i] * ks, s);
-            s = warp_sum(s) * inv_sqrt_d;
-            if (lane == 0) sc[h * kAttnChunk + tt] = isfinite(s) ? s : 0.f;
+    // scores: thread i takes positions i, i+128, ...; dot over d in order, double
+    double* sc = d.attn_scores + (size_t)h * ctx;
+    const int T = pos + 1;
+    const double sqrt_d = sqrt((double)D);
+    double mloc = -1.0e300;
+    for (int t = i; t < T; t += 128) {
+        const size_t st = (size_t)layer * ctx + t;
+        const int8_t* kp = t == pos ? k8 + g * D : d.kcache + st * KV + g * D;
+        const float ks = t == pos ? ksc : d.kscale[st];
+        double s = 0.0;
+        for (int j = 0; j < D; j += 16) {
+            const int4 raw = *reinterpret_cast<const int4*>(kp + j);
+            const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) s += (double)qv[j + u] * (double)((float)kb[u] * ks);
         }
+        s /= sqrt_d;
+        if (!isfinite(s)) s = 0.0;
+        sc[t] = s;
+        mloc = fmax(mloc, s);
     }
+    const double mx = block_max_d(mloc, scratch_d);
+    double dloc = 0.0;
+    for (int t = i; t < T; t += 128) {
+        const double e = exp(sc[t] - mx);
+        sc[t] = e;
+        dloc += e;
+    }
+    double den = block_sum_d(dloc, scratch_d);
+    if (!isfinite(den) || den <= 0.0) den = 1.0;
+    for (int t = i; t < T; t += 128) sc[t] = sc[t] / den;
     __syncthreads();
-    float* part = d.attn_part;
-    const int stride = D + 2;
-    for (int h = warp; h < group; h += nw) {
-        float m = -FLT_MAX;
-        for (int tt = lane; tt < n; tt += 32) m = fmaxf(m, sc[h * kAttnChunk + tt]);
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.f;
-        for (int tt = lane; tt < n; tt += 32) {
-            const float p = expf(sc[h * kAttnChunk + tt] - m);
-            sc[h * kAttnChunk + tt] = p;
-            l += p;
-        }
-        l = warp_sum(l);
-        __syncwarp();
-        float* out = part + ((size_t)(g * group + h) * d.nsplit + split) * stride;
-        for (int i = lane; i < D; i += 32) {
-            float acc = 0.f;
-            for (int tt = 0; tt < n; ++tt) {
-                const int t = t0 + tt;
-                const size_t st = (size_t)layer * ctx + t;
-                const int8_t* vp = t == pos ? v8 + g * D : d.vcache + st * KV + g * D;
-                const float vs = t == pos ? vsc : d.vscale[st];
-                acc = fmaf(sc[h * kAttnChunk + tt], (float)vp[i] * vs, acc);
-            }
-            out[2 + i] = acc;
-        }
-        if (lane == 0) { out[0] = m; out[1] = l; }
+    // context[d] += (float)(w_t * (double)vval_t) for t = 0..pos in order
+    float acc = 0.0f;
+    const int8_t* vbase = d.vcache + (size_t)layer * ctx * KV + g * D + i;
+    const float* vsb = d.vscale + (size_t)layer * ctx;
+    for (int t = 0; t < T; ++t) {
+        const float vv = t == pos ? (float)v8[g * D + i] * vsc : (float)vbase[(size_t)t * KV] * vsb[t];
+        acc += (float)(sc[t] * (double)vv);
     }
-    if (!last_cta(d.counters + kCntAttn + g, (unsigned)nact)) return;
-    // merge the chunks of this KV head's query heads
-    for (int h = warp; h < group; h += nw) {
-        const float* base = part + (size_t)(g * group + h) * d.nsplit * stride;
-        float M = -FLT_MAX;
-        for (int s = 0; s < nact; ++s) M = fmaxf(M, base[(size_t)s * stride]);
-        float L = 0.f;
-        for (int s = 0; s < nact; ++s) L += base[(size_t)s * stride + 1] * expf(base[(size_t)s * stride] - M);
-        for (int i = lane; i < D; i += 32) {
-            float acc = 0.f;
-            for (int s = 0; s < nact; ++s)
-                acc = fmaf(base[(size_t)s * stride + 2 + i], expf(base[(size_t)s * stride] - M), acc);
-            d.ctxv[(g * group + h) * D + i] = acc / L;
-        }
-    }
-    if (threadIdx.x == 0) d.counters[kCntAttn + g] = 0u;
+    d.ctxv[h * D + i] = acc;
 }
 
 // ---------------------------------------------------------------------------
-// O projection + residual add (:5183, :6420-6423)
+// O projection + residual add (:5183, :6420-6423).  One tile per CTA, 8 parts.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) k_oproj(Dev d, LayerW w) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ float kvals[16];
-    const int H = d.dm.hidden, Q = d.dm.q_dim();
-    if (threadIdx.x < 16) kvals[threadIdx.x] = d.tables->kvalues[threadIdx.x];
-    float* xs = reinterpret_cast<float*>(smem);
-    uint8_t* ring = align16(smem + (size_t)Q * 4);
-    copy_to_smem(d.ctxv, xs, Q);
+    const int Q = d.dm.q_dim();
     const int nblk = Q / 256;
-    const uint32_t rb = (uint32_t)nblk * 136u, stage = (uint32_t)kTileRows * rb;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    tile_pipeline<kSmallStages>(
-        H / kTileRows, stage, ring, [&](int t, uint8_t* dst) { stage_copy(dst, w.wo + (size_t)t * stage, stage); },
-        [&](int t, const uint8_t* s) {
-            for (int r = warp; r < kTileRows; r += kWarps) {
-                const float acc = dot_iq4_xs(s + r * rb, xs, nblk, kvals, lane);
-                if (lane == 0) {
-                    const int r0 = t * kTileRows + r;
-                    const float o = finite_or_zero(acc);
-                    d.attn_out[r0] = o;
-                    d.x[r0] = d.x[r0] + o;
-                }
-            }
-        });
+    const uint32_t rb = (uint32_t)nblk * 136u, tb = (uint32_t)kTileRows * rb;
+    Carve cv(smem);
+    uint8_t* tile = cv.take<uint8_t>(tb);
+    float* xs = cv.take<float>(Q);
+    uint32_t* xb = cv.take<uint32_t>(Q / 16 * 32);
+    int* sb = cv.take<int>(Q / 256);
+    double* part = cv.take<double>(kWarps * kTileRows);
+    stage_copy(tile, w.wo + (size_t)blockIdx.x * tb, tb);
+    cp_async_commit();
+    uint32_t K4[4];
+    load_kv_regs(d.tables, K4);
+    copy_to_smem(d.ctxv, xs, Q);
+    build_xq(xs, Q, xb, sb);
+    cp_async_wait<0>();
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+    Acc acc{};
+    dot_iq4_xs_mma(tile + g * rb, tile + (g + 8) * rb, warp * nblk / kWarps, (warp + 1) * nblk / kWarps, XQ{xb, sb},
+                   K4, lane, acc);
+    store_tile_rows(part, warp, acc);
+    __syncthreads();
+    if (threadIdx.x < kTileRows) {
+        const int r = blockIdx.x * kTileRows + threadIdx.x;
+        const float o = finite_or_zero_d(sum_parts(part, 0, kWarps, threadIdx.x));
+        d.attn_out[r] = o;
+        d.x[r] = d.x[r] + o;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -320,20 +382,34 @@ __global__ void __launch_bounds__(kThreads) k_router(Dev d, LayerW w, int layer)
     __shared__ int isel[8];
     const int H = d.dm.hidden, E = d.dm.experts;
     float* xs = reinterpret_cast<float*>(smem);
-    rmsnorm_to_smem(d.x, w.ffn_norm, xs, H, scratch);
-    if (blockIdx.x == 0)
-        for (int i = threadIdx.x; i < H; i += blockDim.x) d.xn[i] = xs[i];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * kRouterRowsPerCta + warp;
+    const float* row = w.router + (size_t)(e < E ? e : 0) * H;
+    // prefetch this warp's router row into registers while the norm runs
+    float4 wv[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int i = (k * 32 + lane) * 4;
+        wv[k] = i < H ? *reinterpret_cast<const float4*>(row + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    rmsnorm_to_smem(d.x, w.ffn_norm, xs, H, scratch);
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4)
+            *reinterpret_cast<float4*>(d.xn + i) = *reinterpret_cast<const float4*>(xs + i);
     if (e < E) {
-        const float* row = w.router + (size_t)e * H;
         double acc = 0.0;
-        for (int i = lane * 4; i < H; i += 128) {
-            const float4 wv = *reinterpret_cast<const float4*>(row + i);
-            acc += (double)wv.x * (double)xs[i];
-            acc += (double)wv.y * (double)xs[i + 1];
-            acc += (double)wv.z * (double)xs[i + 2];
-            acc += (double)wv.w * (double)xs[i + 3];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int i = (k * 32 + lane) * 4;
+            if (i < H) {
+                acc += (double)wv[k].x * (double)xs[i] + (double)wv[k].y * (double)xs[i + 1];
+                acc += (double)wv[k].z * (double)xs[i + 2] + (double)wv[k].w * (double)xs[i + 3];
+            }
+        }
+        for (int i = (16 * 32 + lane) * 4; i < H; i += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(row + i);
+            acc += (double)v.x * (double)xs[i] + (double)v.y * (double)xs[i + 1];
+            acc += (double)v.z * (double)xs[i + 2] + (double)v.w * (double)xs[i + 3];
         }
         acc = warp_sum_d(acc);
         if (lane == 0) d.router_logits[e] = acc;
@@ -341,7 +417,6 @@ __global__ void __launch_bounds__(kThreads) k_router(Dev d, LayerW w, int layer)
     if (!last_cta(d.counters + kCntRouter, gridDim.x)) return;
     const int t = threadIdx.x;
     const double lg = t < E ? d.router_logits[t] : -1.0e300;
-    // max
     double m = lg;
     for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
     __syncthreads();
@@ -354,7 +429,6 @@ __global__ void __launch_bounds__(kThreads) k_router(Dev d, LayerW w, int layer)
     if (t < 256) probs[t] = t < E ? ex / den : -1.0;
     __syncthreads();
     if (warp == 0) {
-        // 8 rounds of argmax with strict > (lowest index wins ties)
         for (int k = 0; k < 8; ++k) {
             double bv = -2.0;
             int bi = 0x7fffffff;
@@ -388,127 +462,175 @@ __global__ void __launch_bounds__(kThreads) k_router(Dev d, LayerW w, int layer)
 // ---------------------------------------------------------------------------
 // Fused gate/up IQ2_XS matvecs of the 8 selected experts with SwiGLU
 // (qx_packed_expert_matvec_mode :4739-4787, :5291-5297, qx_silu :2511).
-// Tile = 16 rows of gate and the same 16 rows of up for one expert.
+// CTA = (expert rank, 16-row tile): tile 0 = gate rows, tile 1 = up rows;
+// 4 block-parts each.
 // ---------------------------------------------------------------------------
+__device__ void load_iq_tables(IqTab* T, const Tables* G, bool want2, bool want3) {
+    if (want2)
+        for (int i = threadIdx.x; i < 512 * 2; i += blockDim.x) {
+            const float* g = G->iq2xs[i >> 1] + 4 * (i & 1);
+            T->grid2[i >> 1][i & 1] =
+                (uint32_t)g[0] | ((uint32_t)g[1] << 8) | ((uint32_t)g[2] << 16) | ((uint32_t)g[3] << 24);
+        }
+    if (want3)
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+            const float* g = G->iq3xxs[i];
+            T->grid3[i] = (uint32_t)g[0] | ((uint32_t)g[1] << 8) | ((uint32_t)g[2] << 16) | ((uint32_t)g[3] << 24);
+        }
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) T->ksigns[i] = G->ksigns[i];
+}
+
 __global__ void __launch_bounds__(kThreads) k_gateup(Dev d, LayerW w, int layer) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ float res[2][kTileRows];
     const int H = d.dm.hidden, I = d.dm.moe_inter;
-    Tables* T = reinterpret_cast<Tables*>(smem);
-    float* xs = reinterpret_cast<float*>(smem + sizeof(Tables));
-    uint8_t* ring = align16(reinterpret_cast<uint8_t*>(xs + H));
-    copy_words(T->iq2xs, d.tables->iq2xs, sizeof(T->iq2xs));
-    copy_words(T->ksigns, d.tables->ksigns, sizeof(T->ksigns));
-    copy_to_smem(d.xn, xs, H);
     const int nblk = H / 256;
-    const uint32_t rb = (uint32_t)nblk * 74u, half = (uint32_t)kTileRows * rb, stage = 2u * half;
-    const size_t slice = (size_t)I * rb;
+    const uint32_t rb = (uint32_t)nblk * 74u, tb = (uint32_t)kTileRows * rb;
+    Carve cv(smem);
+    uint8_t* tiles = cv.take<uint8_t>(2 * tb);
+    IqTab* T = cv.take<IqTab>(1);
+    float* xs = cv.take<float>(H);
+    uint32_t* xb = cv.take<uint32_t>(H / 16 * 32);
+    int* sb = cv.take<int>(H / 256);
+    double* part = cv.take<double>(kWarps * kTileRows);
     const int tiles_per_expert = I / kTileRows;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int* sel = d.sel + layer * 8;
-    tile_pipeline<kSmallStages>(
-        8 * tiles_per_expert, stage, ring,
-        [&](int t, uint8_t* dst) {
-            const int k = t / tiles_per_expert, i0 = (t % tiles_per_expert) * kTileRows;
-            const size_t off = (size_t)sel[k] * slice + (size_t)i0 * rb;
-            stage_copy(dst, w.gate + off, half);
-            stage_copy(dst + half, w.up + off, half);
-        },
-        [&](int t, const uint8_t* s) {
-            for (int r = warp; r < 2 * kTileRows; r += kWarps) {
-                const float v = dot_iq2_xs(s + (r / kTileRows) * half + (r % kTileRows) * rb, xs, nblk, *T, lane);
-                if (lane == 0) res[r / kTileRows][r % kTileRows] = finite_or_zero(v);
-            }
-            __syncthreads();
-            if (threadIdx.x < kTileRows) {
-                const int k = t / tiles_per_expert, i = (t % tiles_per_expert) * kTileRows + threadIdx.x;
-                const double g = (double)res[0][threadIdx.x];
-                d.hbuf[k * I + i] = (float)(g / (1.0 + exp(-g)) * (double)res[1][threadIdx.x]);
-            }
-        });
+    const int k = blockIdx.x / tiles_per_expert, i0 = (blockIdx.x % tiles_per_expert) * kTileRows;
+    const size_t off = (size_t)d.sel[layer * 8 + k] * ((size_t)I * rb) + (size_t)i0 * rb;
+    stage_copy(tiles, w.gate + off, tb);
+    stage_copy(tiles + tb, w.up + off, tb);
+    cp_async_commit();
+    load_iq_tables(T, d.tables, true, false);
+    copy_to_smem(d.xn, xs, H);
+    build_xq(xs, H, xb, sb);
+    cp_async_wait<0>();
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+    const int parts = kWarps / 2, tile = warp / parts, p = warp % parts;
+    const uint8_t* base = tiles + tile * tb;
+    Acc acc{};
+    dot_iq2_xs_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, *T, lane,
+                   acc);
+    store_tile_rows(part, warp, acc);
+    __syncthreads();
+    if (threadIdx.x < kTileRows) {
+        const float gv = finite_or_zero_d(sum_parts(part, 0, parts, threadIdx.x));
+        const float uv = finite_or_zero_d(sum_parts(part, 1, parts, threadIdx.x));
+        const double gd = (double)gv;
+        d.hbuf[k * I + i0 + threadIdx.x] = (float)(gd / (1.0 + exp(-gd)) * (double)uv);
+    }
 }
 
 // ---------------------------------------------------------------------------
 // IQ3_XXS down projections of the 8 experts with the rank-ordered weighted sum
-// and the residual add fused (:5298-5309).  Tile = rows [16t, 16t+16) of all
-// 8 selected experts, so each output row is finished inside one CTA.
+// and the residual add fused (:5298-5309).  CTA = rows [16c, 16c+16) of all 8
+// experts; warp k computes expert k on its own input h[k].
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) k_down(Dev d, LayerW w, int layer) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ float y[8][kTileRows];
     const int H = d.dm.hidden, I = d.dm.moe_inter;
-    Tables* T = reinterpret_cast<Tables*>(smem);
-    float* hs = reinterpret_cast<float*>(smem + sizeof(Tables));
-    uint8_t* ring = align16(reinterpret_cast<uint8_t*>(hs + 8 * I));
-    copy_words(T->iq3xxs, d.tables->iq3xxs, sizeof(T->iq3xxs));
-    copy_words(T->ksigns, d.tables->ksigns, sizeof(T->ksigns));
-    copy_to_smem(d.hbuf, hs, 8 * I);
     const int nblk = I / 256;
-    const uint32_t rb = (uint32_t)nblk * 98u, part = (uint32_t)kTileRows * rb, stage = 8u * part;
+    const uint32_t rb = (uint32_t)nblk * 98u, tb = (uint32_t)kTileRows * rb;
+    Carve cv(smem);
+    uint8_t* tiles = cv.take<uint8_t>(8 * tb);
+    IqTab* T = cv.take<IqTab>(1);
+    float* hs = cv.take<float>(8 * I);
+    uint32_t* xb = cv.take<uint32_t>(8 * (I / 16) * 32);
+    int* sb = cv.take<int>(8 * (I / 256));
+    double* part = cv.take<double>(kWarps * kTileRows);
     const size_t slice = (size_t)H * rb;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int* sel = d.sel + layer * 8;
-    tile_pipeline<kSmallStages>(
-        H / kTileRows, stage, ring,
-        [&](int t, uint8_t* dst) {
-            for (int k = 0; k < 8; ++k)
-                stage_copy(dst + k * part, w.down + (size_t)sel[k] * slice + (size_t)t * part, part);
-        },
-        [&](int t, const uint8_t* s) {
-            for (int r = warp; r < 8 * kTileRows; r += kWarps) {
-                const int k = r / kTileRows, rr = r % kTileRows;
-                const float v = dot_iq3_xxs(s + k * part + rr * rb, hs + k * I, nblk, *T, lane);
-                if (lane == 0) y[k][rr] = finite_or_zero(v);
-            }
-            __syncthreads();
-            if (threadIdx.x < kTileRows) {
-                const int r = t * kTileRows + threadIdx.x;
-                float moe = 0.0f;
-                for (int k = 0; k < 8; ++k) moe += (float)(d.selw_d[k] * (double)y[k][threadIdx.x]);
-                d.moe_out[r] = moe;
-                d.x[r] = d.x[r] + moe;
-            }
-        });
+    for (int k = 0; k < 8; ++k)
+        stage_copy(tiles + k * tb, w.down + (size_t)d.sel[layer * 8 + k] * slice + (size_t)blockIdx.x * tb, tb);
+    cp_async_commit();
+    load_iq_tables(T, d.tables, false, true);
+    copy_to_smem(d.hbuf, hs, 8 * I);
+    for (int k = 0; k < 8; ++k) build_xq(hs + k * I, I, xb + k * (I / 16) * 32, sb + k * (I / 256));
+    cp_async_wait<0>();
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+    const uint8_t* base = tiles + warp * tb;
+    Acc acc{};
+    dot_iq3_xxs_mma(base + g * rb, base + (g + 8) * rb, 0, nblk,
+                    XQ{xb + warp * (I / 16) * 32, sb + warp * (I / 256)}, *T, lane, acc);
+    store_tile_rows(part, warp, acc);
+    __syncthreads();
+    if (threadIdx.x < kTileRows) {
+        const int r = blockIdx.x * kTileRows + threadIdx.x;
+        float moe = 0.0f;
+        for (int k = 0; k < 8; ++k)
+            moe += (float)(d.selw_d[k] * (double)finite_or_zero_d(part[k * kTileRows + threadIdx.x]));
+        d.moe_out[r] = moe;
+        d.x[r] = d.x[r] + moe;
+    }
 }
 
 // ---------------------------------------------------------------------------
 // Final RMSNorm + Q6_K head + argmax (qx_compute_real_final_head,
-// src/qx_format.c:3554-3738; greedy pick :3045-3057).  Persistent grid; each
-// CTA keeps its best (value, lowest index); the last CTA picks the token,
-// records it at tokens_out[pos] and advances (token, pos) for the next step.
+// src/qx_format.c:3554-3738; greedy pick :3045-3057).  Persistent grid over
+// groups of 2 tiles; logits compared as doubles (ties to the lower index, as
+// the strict > scan does); the last CTA records the token and advances
+// (token, pos) for the next step.
 // ---------------------------------------------------------------------------
-constexpr int kHeadStages = 4;
+constexpr int kHeadStages = 3;
+constexpr int kHeadTiles = 2;
 
 __global__ void __launch_bounds__(kThreads) k_head(Dev d) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ double scratch[kWarps];
-    __shared__ float wbv[kWarps];
+    __shared__ double wbv[kWarps];
     __shared__ int wbi[kWarps];
     const int H = d.dm.hidden, V = d.dm.vocab;
-    float* xs = reinterpret_cast<float*>(smem);
-    uint8_t* ring = align16(smem + (size_t)H * 4);
-    rmsnorm_to_smem(d.x, d.out_norm, xs, H, scratch);
     const int nblk = H / 256;
-    const uint32_t rb = (uint32_t)nblk * 210u, stage = (uint32_t)kTileRows * rb;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float bv = -FLT_MAX;
+    const uint32_t rb = (uint32_t)nblk * 210u, tb = (uint32_t)kTileRows * rb, stage = kHeadTiles * tb;
+    Carve cv(smem);
+    uint8_t* ring = cv.take<uint8_t>(kHeadStages * stage);
+    float* xs = cv.take<float>(H);
+    uint32_t* xb = cv.take<uint32_t>(H / 16 * 32);
+    int* sb = cv.take<int>(H / 256);
+    double* part = cv.take<double>(kWarps * kTileRows);
+    const int ngroups = V / (kTileRows * kHeadTiles);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+    const int parts = kWarps / kHeadTiles, tile = warp / parts, p = warp % parts;
+    // the first stages are issued before the norm + x quantization run
+    const int first = blockIdx.x, step = gridDim.x;
+    const int mine = first < ngroups ? (ngroups - first + step - 1) / step : 0;
+    for (int s = 0; s < kHeadStages - 1; ++s) {
+        if (s < mine) stage_copy(ring + (uint32_t)s * stage, d.head + (size_t)(first + s * step) * stage, stage);
+        cp_async_commit();
+    }
+    rmsnorm_to_smem(d.x, d.out_norm, xs, H, scratch);
+    build_xq(xs, H, xb, sb);
+    __syncthreads();
+    double bv = -1.0e300;
     int bi = 0x7fffffff;
     bool bad = false;
-    tile_pipeline<kHeadStages>(
-        V / kTileRows, stage, ring, [&](int t, uint8_t* dst) { stage_copy(dst, d.head + (size_t)t * stage, stage); },
-        [&](int t, const uint8_t* s) {
-            for (int r = warp; r < kTileRows; r += kWarps) {
-                const float v = dot_q6_k(s + r * rb, xs, nblk, lane);
-                const int row = t * kTileRows + r;
-                if (lane == 0) {
-                    d.logits[row] = v;
-                    if (!isfinite(v)) bad = true;
-                    if (v > bv || (v == bv && row < bi)) { bv = v; bi = row; }
-                }
-            }
-        });
-    if (lane == 0) { wbv[warp] = bv; wbi[warp] = bi; }
+    for (int it = 0; it < mine; ++it) {
+        const int nx = it + kHeadStages - 1;
+        if (nx < mine)
+            stage_copy(ring + (uint32_t)(nx % kHeadStages) * stage, d.head + (size_t)(first + nx * step) * stage, stage);
+        cp_async_commit();
+        cp_async_wait<kHeadStages - 1>();
+        __syncthreads();
+        const uint8_t* base = ring + (uint32_t)(it % kHeadStages) * stage + tile * tb;
+        Acc acc{};
+        dot_q6_k_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, lane,
+                     acc);
+        store_tile_rows(part, warp, acc);
+        __syncthreads();
+        if (threadIdx.x < kHeadTiles * kTileRows) {
+            const int tl = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows;
+            const int row = (first + it * step) * kHeadTiles * kTileRows + tl * kTileRows + r;
+            const double v = sum_parts(part, tl, parts, r);
+            if (!isfinite(v)) bad = true;
+            d.logits[row] = (float)v;
+            if (v > bv || (v == bv && row < bi)) { bv = v; bi = row; }
+        }
+    }
     if (bad) atomicOr(d.err, kErrNonFinite);
+    for (int o = 16; o; o >>= 1) {
+        const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { wbv[warp] = bv; wbi[warp] = bi; }
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int i = 1; i < kWarps; ++i)
@@ -518,12 +640,12 @@ __global__ void __launch_bounds__(kThreads) k_head(Dev d) {
     }
     if (!last_cta(d.counters + kCntHead, gridDim.x)) return;
     if (threadIdx.x == 0) {
-        float v = d.best_val[0];
+        double v = d.best_val[0];
         int i = d.best_idx[0];
         for (int c = 1; c < (int)gridDim.x; ++c) {
-            const float cv = d.best_val[c];
+            const double cv2 = d.best_val[c];
             const int ci = d.best_idx[c];
-            if (cv > v || (cv == v && ci < i)) { v = cv; i = ci; }
+            if (cv2 > v || (cv2 == v && ci < i)) { v = cv2; i = ci; }
         }
         const int pos = *d.pos;
         if (pos >= 0 && pos < d.dm.ctx) d.tokens_out[pos] = i;
@@ -579,22 +701,27 @@ __global__ void __launch_bounds__(1024) k_topn(Dev d, int top_n, int* out_idx, f
 // ---------------------------------------------------------------------------
 // launch configuration
 // ---------------------------------------------------------------------------
-static size_t smem_qkv(const Dims& m) { return (size_t)m.hidden * 4 + 16 + kSmallStages * (size_t)kTileRows * (m.hidden / 256) * 136; }
-static size_t smem_oproj(const Dims& m) { return (size_t)m.q_dim() * 4 + 16 + kSmallStages * (size_t)kTileRows * (m.q_dim() / 256) * 136; }
-static size_t smem_attn(const Dims& m) {
-    const int group = m.q_heads / m.kv_heads;
-    return (size_t)(2 * m.kv_dim() + group * m.head_dim + group * kAttnChunk) * 4 + 2 * (size_t)m.kv_dim() + 16;
+namespace {
+size_t a16(size_t v) { return (v + 15) / 16 * 16; }
+size_t xq_bytes(int K) { return a16((size_t)K * 4) + a16((size_t)K / 16 * 32 * 4) + a16((size_t)K / 256 * 4); }
+size_t part_bytes() { return a16((size_t)kWarps * kTileRows * 8); }
+size_t smem_qkv(const Dims& m) { return 16 + a16((size_t)kQkvTiles * kTileRows * (m.hidden / 256) * 136) + xq_bytes(m.hidden) + part_bytes(); }
+size_t smem_oproj(const Dims& m) { return 16 + a16((size_t)kTileRows * (m.q_dim() / 256) * 136) + xq_bytes(m.q_dim()) + part_bytes(); }
+size_t smem_router(const Dims& m) { return (size_t)m.hidden * 4; }
+size_t smem_gateup(const Dims& m) { return 16 + a16(2 * (size_t)kTileRows * (m.hidden / 256) * 74) + a16(sizeof(IqTab)) + xq_bytes(m.hidden) + part_bytes(); }
+size_t smem_down(const Dims& m) {
+    return 16 + a16(8 * (size_t)kTileRows * (m.moe_inter / 256) * 98) + a16(sizeof(IqTab)) + a16((size_t)8 * m.moe_inter * 4) +
+           a16((size_t)8 * m.moe_inter / 16 * 32 * 4) + a16((size_t)8 * m.moe_inter / 256 * 4) + part_bytes();
 }
-static size_t smem_router(const Dims& m) { return (size_t)m.hidden * 4; }
-static size_t smem_gateup(const Dims& m) { return sizeof(Tables) + (size_t)m.hidden * 4 + 16 + kSmallStages * 2 * (size_t)kTileRows * (m.hidden / 256) * 74; }
-static size_t smem_down(const Dims& m) { return sizeof(Tables) + (size_t)8 * m.moe_inter * 4 + 16 + kSmallStages * 8 * (size_t)kTileRows * (m.moe_inter / 256) * 98; }
-static size_t smem_head(const Dims& m) { return (size_t)m.hidden * 4 + 16 + kHeadStages * (size_t)kTileRows * (m.hidden / 256) * 210; }
+size_t smem_head(const Dims& m) {
+    return 16 + a16((size_t)kHeadStages * kHeadTiles * kTileRows * (m.hidden / 256) * 210) + xq_bytes(m.hidden) + part_bytes();
+}
+}  // namespace
 
 cudaError_t configure_kernels() {
     int dev = 0, optin = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    // allow each kernel the opt-in maximum minus its static shared memory
     auto set = [&](const void* f) {
         cudaFuncAttributes a{};
         if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, f);
@@ -602,7 +729,6 @@ cudaError_t configure_kernels() {
             e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)a.sharedSizeBytes);
     };
     set((const void*)k_qkv);
-    set((const void*)k_attn);
     set((const void*)k_oproj);
     set((const void*)k_router);
     set((const void*)k_gateup);
@@ -612,26 +738,33 @@ cudaError_t configure_kernels() {
     return e;
 }
 
-int head_grid_size(int device) {
+int head_grid_size(int device, const Dims& m) {
     int sms = 0, per = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    Dims m{};
-    m.hidden = 2048;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_head, kThreads, smem_head(m));
     if (per < 1) per = 1;
-    return sms * per;
+    const int groups = m.vocab / (kTileRows * kHeadTiles);
+    const int grid = sms * per;
+    return grid < groups ? grid : groups;
+}
+
+size_t attn_scores_bytes(const Dims& m) { return (size_t)m.q_heads * m.ctx * sizeof(double); }
+
+bool geometry_supported(const Dims& m) {
+    return m.hidden % 256 == 0 && m.q_dim() % 256 == 0 && m.kv_dim() <= 1024 && m.head_dim == 128 &&
+           (m.q_dim() + 2 * m.kv_dim()) % (kQkvTiles * kTileRows) == 0 && m.moe_inter % 256 == 0 &&
+           m.vocab % (kTileRows * kHeadTiles) == 0 && smem_down(m) <= 227 * 1024 && smem_oproj(m) <= 227 * 1024;
 }
 
 void launch_embed(const Dev& d, cudaStream_t st) { k_embed<<<1, 256, 0, st>>>(d); }
 
 void launch_qkv(const Dev& d, const LayerW& w, cudaStream_t st) {
     const int nt = (d.dm.q_dim() + 2 * d.dm.kv_dim()) / kTileRows;
-    k_qkv<<<nt, kThreads, smem_qkv(d.dm), st>>>(d, w);
+    k_qkv<<<(nt + kQkvTiles - 1) / kQkvTiles, kThreads, smem_qkv(d.dm), st>>>(d, w);
 }
 
 void launch_attn(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
-    dim3 grid(d.dm.kv_heads, d.nsplit);
-    k_attn<<<grid, 256, smem_attn(d.dm), st>>>(d, w, layer);
+    k_attn<<<d.dm.q_heads, 128, 0, st>>>(d, w, layer);
 }
 
 void launch_oproj(const Dev& d, const LayerW& w, cudaStream_t st) {
@@ -644,17 +777,14 @@ void launch_router(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
 }
 
 void launch_gateup(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
-    const int nt = 8 * d.dm.moe_inter / kTileRows;
-    k_gateup<<<nt, kThreads, smem_gateup(d.dm), st>>>(d, w, layer);
+    k_gateup<<<8 * d.dm.moe_inter / kTileRows, kThreads, smem_gateup(d.dm), st>>>(d, w, layer);
 }
 
 void launch_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
     k_down<<<d.dm.hidden / kTileRows, kThreads, smem_down(d.dm), st>>>(d, w, layer);
 }
 
-void launch_head(const Dev& d, cudaStream_t st) {
-    k_head<<<d.head_grid, kThreads, smem_head(d.dm), st>>>(d);
-}
+void launch_head(const Dev& d, cudaStream_t st) { k_head<<<d.head_grid, kThreads, smem_head(d.dm), st>>>(d); }
 
 void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st) {
     k_final_norm<<<1, 256, (size_t)d.dm.hidden * 4, st>>>(d, normalized);

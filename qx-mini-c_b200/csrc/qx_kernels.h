@@ -5,6 +5,7 @@
 #include <cstdint>
 
 #include "qx_dev.cuh"
+#include "qx_imma.cuh"
 
 namespace qx {
 
@@ -44,7 +45,7 @@ struct Dev {
     int8_t* vcache;
     float* kscale;               // [L][ctx]
     float* vscale;
-    float* attn_part;            // split-KV partials [Hq][nsplit][D + 2]
+    double* attn_scores;         // softmax scratch [Hq][ctx] (double)
     float* ctxv;                 // attention context [Q]
     float* attn_out;             // O projection output [H] (stage API)
     float* moe_out;              // MoE output [H] (stage API)
@@ -62,12 +63,9 @@ struct Dev {
     int* tokens_out;             // [ctx] argmax written at index pos
     int* err;                    // error bits
     int head_grid;               // CTAs of the head kernel (partials length)
-    int nsplit;                  // split-KV chunks (ctx / kAttnChunk rounded up)
 };
 
-constexpr int kAttnChunk = 64;
-
-enum CounterSlot { kCntAttn = 0, kCntRouter = 8, kCntHead = 9, kCntTotal = 16 };
+enum CounterSlot { kCntRouter = 8, kCntHead = 9, kCntTotal = 16 };
 
 // Launchers.  All run on `st` and read pos/token from device memory, so they
 // can be captured once into a CUDA graph.
@@ -81,7 +79,9 @@ void launch_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
 void launch_head(const Dev& d, cudaStream_t st);
 void launch_topn(const Dev& d, int top_n, int* out_idx, float* out_val, cudaStream_t st);
 void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st);
-int head_grid_size(int device);
+int head_grid_size(int device, const Dims& m);
+size_t attn_scores_bytes(const Dims& m);
+bool geometry_supported(const Dims& m);
 cudaError_t configure_kernels();
 
 }  // namespace qx

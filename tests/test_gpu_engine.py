@@ -235,18 +235,17 @@ def test_config4_256_steps_teacher_forced(full, full_image, port):
     assert len(set(toks.tolist())) > 1
     P = port.open_image(full_image)
     inputs = [W.START_TOKEN] + toks.tolist()
+    snap = [full.kv_read(layer, 0, W.DECODE_STEPS) for layer in range(full.layers)]
     for s in (0, 17, 128, 255):
         kv = P.new_kv(s + 1)
-        for layer in range(full.layers):
-            if s:
-                k, v, ks, vs = full.kv_read(layer, 0, s)
-                kv["k"][layer, :s], kv["v"][layer, :s], kv["ks"][layer, :s], kv["vs"][layer, :s] = k, v, ks, vs
-        r = P.decode_step(inputs[s], s, kv)
-        assert r["token"] == toks[s], "step %d" % s
         full.reset()
         for layer in range(full.layers):
             if s:
-                full.kv_write(layer, 0, kv["k"][layer, :s], kv["v"][layer, :s], kv["ks"][layer, :s], kv["vs"][layer, :s])
+                k, v, ks, vs = (a[:s] for a in snap[layer])
+                kv["k"][layer, :s], kv["v"][layer, :s], kv["ks"][layer, :s], kv["vs"][layer, :s] = k, v, ks, vs
+                full.kv_write(layer, 0, k, v, ks, vs)
+        r = P.decode_step(inputs[s], s, kv)
+        assert r["token"] == toks[s], "step %d" % s
         e = full.decode_step(inputs[s], s, want_experts=True)
         np.testing.assert_array_equal(e["experts"], r["experts"], err_msg="experts at step %d" % s)
         assert e["token"] == r["token"]
