@@ -145,6 +145,25 @@ int qx_cuda_attention_layer(qx_cuda_engine *engine, uint32_t layer, uint32_t pos
  * without norm (src/qx_format.c:3759-3819, full-MoE mode :6261). */
 int qx_cuda_embed(qx_cuda_engine *engine, uint32_t token, float *out, char *err, uint64_t err_len);
 
+/* Final RMSNorm + Q6_K head + argmax that allocates no device memory.  No
+ * counterpart in the reference (it has no device code).  For callers that
+ * cannot call cudaMalloc themselves or have it called for them - a plugin
+ * inside a host that owns every allocation, or code that must not allocate
+ * between stream-ordered steps.  All pointers are device pointers the caller
+ * owns: residual[hidden], norm_weight[hidden] (output_norm.weight, F32),
+ * head (output.weight bytes, Q6_K, vocab rows), logits[vocab] (may be NULL),
+ * argmax (one uint32; 0xFFFFFFFF if a logit is not finite).  The work is
+ * queued on `stream` (cudaStream_t, NULL = default) and the call returns
+ * without waiting.  Its scratch (per-CTA partial maxima and a counter) is a
+ * fixed array inside this library, held by every GPU that loads it until the
+ * process exits, so: hidden must be a multiple of 256 and at most 2048, vocab
+ * a positive multiple of 32, and calls that overlap on the GPU (unordered
+ * streams) race on that array.  The first call on each device looks up the
+ * array's address; make it before any stream capture. */
+int qx_cuda_final_head_noalloc(const float *residual_dev, const float *norm_weight_dev, const void *head_q6k_dev,
+                               uint32_t hidden, uint32_t vocab, float *logits_dev, uint32_t *argmax_dev, void *stream,
+                               char *err, uint64_t err_len);
+
 /* ---- persistent KV ---------------------------------------------------- */
 
 /* Write / read `count` positions of layer `layer` starting at `first`:
