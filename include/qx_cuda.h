@@ -53,6 +53,7 @@ typedef struct qx_cuda_model {
 
 #define QX_CUDA_VERIFY_CHECKSUMS 0x1u   /* verify FNV checksums of every tensor once, at create */
 #define QX_CUDA_NO_GRAPH         0x2u   /* launch kernels one by one instead of replaying a CUDA graph */
+#define QX_CUDA_PER_STAGE        0x4u   /* decode with one kernel per stage instead of the one-launch step kernel */
 
 typedef struct qx_cuda_options {
     int32_t device;            /* CUDA ordinal; -1 = current device */
@@ -186,6 +187,13 @@ int qx_cuda_profile_get(const qx_cuda_engine *engine, qx_cuda_profile *out);
 int qx_cuda_time_kernels(qx_cuda_engine *engine, uint32_t token, uint32_t position, uint32_t steps,
                          char *names, uint64_t names_len, float *ms_avg, uint32_t *launches,
                          uint32_t max_kernels, uint32_t *kernel_count, char *err, uint64_t err_len);
+
+/* One decode step with a device timestamp (ns, %globaltimer) taken by CTA 0
+ * after each grid barrier of the persistent step kernel: stamps[0] = start,
+ * then embedding+QKV, attention, O projection, router, gate/up, down per
+ * layer, then the head.  A profiling aid (it allocates a small buffer). */
+int qx_cuda_phase_trace(qx_cuda_engine *engine, uint32_t token, uint32_t position, uint64_t *stamps_ns,
+                        uint32_t max_stamps, uint32_t *count, char *err, uint64_t err_len);
 
 /* The engine's CUDA stream (cudaStream_t) for callers that time with events. */
 void *qx_cuda_stream(const qx_cuda_engine *engine);

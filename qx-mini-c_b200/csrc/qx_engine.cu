@@ -30,9 +30,10 @@ struct Op {                  // one launch of the per-token sequence
     int kind;
 };
 
-enum OpKind { kEmbed, kQkv, kAttn, kOproj, kRouter, kGateup, kDown, kHead };
+enum OpKind { kEmbed, kQkv, kAttn, kOproj, kRouter, kGateup, kDown, kHead, kStep };
 const char* kOpNames[] = {"embed_q4k", "qkv_iq4xs", "attn_int8kv", "oproj_iq4xs",
-                          "router_top8", "gateup_iq2xs_swiglu", "down_iq3xxs_wsum", "head_q6k_argmax"};
+                          "router_top8", "gateup_iq2xs_swiglu", "down_iq3xxs_wsum", "head_q6k_argmax",
+                          "decode_step_persistent"};
 
 }  // namespace
 
@@ -52,6 +53,8 @@ struct qx_cuda_engine {
     cudaGraphExec_t graph = nullptr;
     bool use_graph = true;
     std::vector<Op> ops;
+    LayerW* layers_dev = nullptr;   // device copy of the layer table (persistent step kernel)
+    int mega_grid = 0;               // 0 = per-stage kernels
     int* d_topi = nullptr;
     float* d_topv = nullptr;
     float* d_norm = nullptr;
@@ -84,11 +87,16 @@ void run_op(qx_cuda_engine* E, const Op& op) {
         case kGateup: qx::launch_gateup(d, E->layers[op.layer], op.layer, st); break;
         case kDown: qx::launch_down(d, E->layers[op.layer], op.layer, st); break;
         case kHead: qx::launch_head(d, st); break;
+        case kStep: qx::launch_decode_step(d, E->layers_dev, E->mega_grid, st); break;
     }
 }
 
 void build_ops(qx_cuda_engine* E) {
     E->ops.clear();
+    if (E->mega_grid) {
+        E->ops.push_back({kOpNames[kStep], -1, kStep});
+        return;
+    }
     E->ops.push_back({kOpNames[kEmbed], -1, kEmbed});
     for (int l = 0; l < E->dm.layers; ++l)
         for (int k = kQkv; k <= kDown; ++k) E->ops.push_back({kOpNames[k], l, k});
@@ -103,7 +111,7 @@ bool run_step(qx_cuda_engine* E, char* err, uint64_t n) {
         for (const Op& op : E->ops) run_op(E, op);
         if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return false;
     }
-    E->prof.kernel_launches += E->ops.size();
+    E->prof.kernel_launches += E->mega_grid ? 1 : E->ops.size();
     E->prof.decode_steps++;
     return true;
 }
@@ -146,6 +154,7 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->graph) cudaGraphExecDestroy(E->graph);
     if (E->weights) cudaFree(E->weights);
     if (E->work) cudaFree(E->work);
+    if (E->layers_dev) cudaFree(E->layers_dev);
     if (E->h_io) cudaFreeHost(E->h_io);
     if (E->own_stream && E->stream) cudaStreamDestroy(E->stream);
     cudaSetDevice(prev);
@@ -337,6 +346,14 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     if (ce != cudaSuccess) return fail(ce, "upload tables");
     ce = cudaHostAlloc((void**)&E->h_io, 64, cudaHostAllocDefault);
     if (ce != cudaSuccess) return fail(ce, "cudaHostAlloc");
+    if (!(o.flags & QX_CUDA_PER_STAGE) && qx::mega_setup(dev, dm, &E->mega_grid)) {
+        ce = cudaMalloc((void**)&E->layers_dev, E->layers.size() * sizeof(LayerW));
+        if (ce == cudaSuccess)
+            ce = cudaMemcpy(E->layers_dev, E->layers.data(), E->layers.size() * sizeof(LayerW), cudaMemcpyHostToDevice);
+        if (ce != cudaSuccess) return fail(ce, "layer table");
+    } else {
+        E->mega_grid = 0;
+    }
     build_ops(E);
 
     if (E->use_graph) {
@@ -417,6 +434,7 @@ bool finish(qx_cuda_engine* E, char* err, uint64_t n) {
     if (bits & qx::kErrPosition) { set_err(err, n, "steps exceed ctx"); return false; }
     if (bits & qx::kErrNonFinite) { set_err(err, n, "non-finite final logit"); return false; }
     if (bits & qx::kErrRouter) { set_err(err, n, "invalid selected router weights"); return false; }
+    if (bits & qx::kErrTimeout) { set_err(err, n, "device grid barrier timed out"); return false; }
     return true;
 }
 
@@ -641,4 +659,27 @@ QX_API int qx_cuda_time_kernels(qx_cuda_engine* E, uint32_t token, uint32_t posi
     if (names && names_len) snprintf(names, (size_t)names_len, "%s", joined.c_str());
     E->prof.kernel_launches += nops * steps;
     return 1;
+}
+
+QX_API int qx_cuda_phase_trace(qx_cuda_engine* E, uint32_t token, uint32_t position, uint64_t* stamps_ns,
+                               uint32_t max_stamps, uint32_t* count, char* err, uint64_t n) {
+    if (!E || !stamps_ns || !count || !max_stamps) { set_err(err, n, "invalid argument"); return 0; }
+    if (!E->mega_grid) { set_err(err, n, "phase trace needs the persistent step kernel"); return 0; }
+    if (position >= (uint32_t)E->dm.ctx || token >= (uint32_t)E->dm.vocab) { set_err(err, n, "invalid argument"); return 0; }
+    DeviceGuard g(E->device);
+    const uint32_t nst = 2u + 6u * (uint32_t)E->dm.layers + 1u;
+    unsigned long long* tr = nullptr;
+    if (!cuda_ok(cudaMalloc((void**)&tr, nst * 8), "cudaMalloc(trace)", err, n)) return 0;
+    cudaMemsetAsync(tr, 0, nst * 8, E->stream);
+    bool ok = set_scalars(E, token, position, err, n);
+    if (ok) {
+        Dev d = E->dev;
+        d.trace = tr;
+        ok = cuda_ok(qx::launch_decode_step(d, E->layers_dev, E->mega_grid, E->stream), "launch", err, n) && finish(E, err, n);
+    }
+    const uint32_t c = nst < max_stamps ? nst : max_stamps;
+    if (ok) ok = cuda_ok(cudaMemcpy(stamps_ns, tr, c * 8, cudaMemcpyDeviceToHost), "trace d2h", err, n);
+    cudaFree(tr);
+    if (ok) *count = c;
+    return ok ? 1 : 0;
 }

@@ -12,102 +12,9 @@
 // way qx_rope_gqa_attention_partial does it (src/qx_format.c:5127-5172).
 #include <cfloat>
 
-#include "qx_imma.cuh"
-#include "qx_kernels.h"
+#include "qx_common.cuh"
 
 namespace qx {
-
-// ---------------------------------------------------------------------------
-// shared helpers
-// ---------------------------------------------------------------------------
-
-// xs[i] = (float)((double)x[i] / rms) * w[i], rms = sqrt(sum x^2 / n + 1e-6)
-// in double (qx_apply_f32_rmsnorm, src/qx_format.c:3358-3371).
-__device__ void rmsnorm_to_smem(const float* x, const float* w, float* xs, int n, double* scratch) {
-    double ss = 0.0;
-    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(x + i);
-        *reinterpret_cast<float4*>(xs + i) = v;
-        ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y;
-        ss += (double)v.z * (double)v.z + (double)v.w * (double)v.w;
-    }
-    ss = block_sum_d(ss, scratch);
-    const double rms = sqrt(ss / (double)n + 1.0e-6);
-    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
-        const float4 wv = *reinterpret_cast<const float4*>(w + i);
-        float4 v = *reinterpret_cast<float4*>(xs + i);
-        v.x = (float)((double)v.x / rms) * wv.x;
-        v.y = (float)((double)v.y / rms) * wv.y;
-        v.z = (float)((double)v.z / rms) * wv.z;
-        v.w = (float)((double)v.w / rms) * wv.w;
-        *reinterpret_cast<float4*>(xs + i) = v;
-    }
-    __syncthreads();
-}
-
-__device__ void copy_to_smem(const float* x, float* xs, int n) {
-    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
-        *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
-    __syncthreads();
-}
-
-__device__ __forceinline__ float finite_or_zero_d(double v) { return isfinite(v) ? (float)v : 0.0f; }
-
-__device__ __forceinline__ uint8_t* align16(uint8_t* p) {
-    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 15u) & ~(uintptr_t)15u);
-}
-
-// last-CTA ticket: true in exactly one CTA, after all `expected` CTAs made
-// their global writes visible.
-__device__ __forceinline__ bool last_cta(unsigned* counter, unsigned expected) {
-    __shared__ bool is_last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(counter, 1u) == expected - 1u;
-    __syncthreads();
-    if (is_last) __threadfence();
-    return is_last;
-}
-
-// Shared-memory carve-up helper.
-struct Carve {
-    uint8_t* p;
-    __device__ explicit Carve(uint8_t* base) : p(base) {}
-    template <class T>
-    __device__ T* take(size_t count) {
-        p = align16(p);
-        T* r = reinterpret_cast<T*>(p);
-        p += count * sizeof(T);
-        return r;
-    }
-};
-
-__device__ __forceinline__ void load_kv_regs(const Tables* t, uint32_t K[4]) {
-    // IQ4_NL codebook as 16 signed bytes in 4 registers
-    for (int j = 0; j < 4; ++j) {
-        uint32_t w = 0;
-        for (int k = 0; k < 4; ++k) w |= ((uint32_t)(uint8_t)(int8_t)t->kvalues[4 * j + k]) << (8 * k);
-        K[j] = w;
-    }
-}
-
-// Sum the per-part tile partials in part order and return the row value.
-__device__ __forceinline__ double sum_parts(const double* part, int tile, int parts, int row) {
-    double v = 0.0;
-    for (int p = 0; p < parts; ++p) v += part[(tile * parts + p) * kTileRows + row];
-    return v;
-}
-
-// Store the two rows a warp finished (lane t = 0 of each group g).
-__device__ __forceinline__ void store_tile_rows(double* part, int warp, const Acc& acc) {
-    double lo, hi;
-    acc.finish(lo, hi);
-    const int lane = threadIdx.x & 31;
-    if ((lane & 3) == 0) {
-        part[warp * kTileRows + (lane >> 2)] = lo;
-        part[warp * kTileRows + (lane >> 2) + 8] = hi;
-    }
-}
 
 // ---------------------------------------------------------------------------
 // embedding: Q4_K row gather (src/qx_format.c:2089-2110, :3759-3819)
@@ -199,46 +106,6 @@ __global__ void __launch_bounds__(kThreads) k_qkv(Dev d, LayerW w) {
 // :6343-6400), scores and softmax in double, context accumulated in float over
 // positions 0..pos in order (:5127-5172).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ double block_max_d(double v, double* scratch) {
-    for (int o = 16; o; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
-    __syncthreads();
-    double m = scratch[0];
-    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmax(m, scratch[i]);
-    return m;
-}
-
-__device__ __forceinline__ float block_max_f(float v, float* scratch) {
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float m = scratch[0];
-    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, scratch[i]);
-    return m;
-}
-
-// Head RMSNorm (double) + RoPE (double, host table) of one 128-wide head held
-// in v[0..127] (shared memory); all 128 threads call.
-__device__ void head_norm_rope(float* v, const float* nw, const double* rope, double* scratch) {
-    const int i = threadIdx.x;
-    const double x = (double)v[i];
-    const double ss = block_sum_d(x * x, scratch);
-    const double inv = 1.0 / sqrt(ss / 128.0 + 1.0e-6);
-    const float y = (float)(x * inv * (double)nw[i]);
-    __syncthreads();
-    v[i] = y;
-    __syncthreads();
-    if (i < 64) {
-        const double c = rope[2 * i], s = rope[2 * i + 1];
-        const float x0 = v[i], x1 = v[i + 64];
-        v[i] = (float)((double)x0 * c - (double)x1 * s);
-        v[i + 64] = (float)((double)x0 * s + (double)x1 * c);
-    }
-    __syncthreads();
-}
-
 __global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
     const int D = 128, KVH = d.dm.kv_heads, QH = d.dm.q_heads, group = QH / KVH;
     const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx;
@@ -262,8 +129,11 @@ __global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
     }
     qv[i] = d.qkv[h * D + i];
     __syncthreads();
-    for (int kh = 0; kh < KVH; ++kh) head_norm_rope(kcur + kh * D, w.k_norm, rope, scratch_d);
-    head_norm_rope(qv, w.q_norm, rope, scratch_d);
+    for (int hh = i >> 5; hh <= KVH; hh += 4) {
+        if (hh < KVH) warp_norm_rope(kcur + hh * D, w.k_norm, rope, i & 31);
+        else warp_norm_rope(qv, w.q_norm, rope, i & 31);
+    }
+    __syncthreads();
     // one INT8 scale over all KV values of the token (K and V separately)
     float ka = 0.f, va = 0.f;
     for (int j = i; j < KV; j += 128) {
@@ -310,13 +180,8 @@ __global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
         mloc = fmax(mloc, s);
     }
     const double mx = block_max_d(mloc, scratch_d);
-    double dloc = 0.0;
-    for (int t = i; t < T; t += 128) {
-        const double e = exp(sc[t] - mx);
-        sc[t] = e;
-        dloc += e;
-    }
-    double den = block_sum_d(dloc, scratch_d);
+    for (int t = i; t < T; t += 128) sc[t] = exp(sc[t] - mx);
+    double den = fixed_order_sum(sc, T, scratch_d);
     if (!isfinite(den) || den <= 0.0) den = 1.0;
     for (int t = i; t < T; t += 128) sc[t] = sc[t] / den;
     __syncthreads();
@@ -465,21 +330,6 @@ __global__ void __launch_bounds__(kThreads) k_router(Dev d, LayerW w, int layer)
 // CTA = (expert rank, 16-row tile): tile 0 = gate rows, tile 1 = up rows;
 // 4 block-parts each.
 // ---------------------------------------------------------------------------
-__device__ void load_iq_tables(IqTab* T, const Tables* G, bool want2, bool want3) {
-    if (want2)
-        for (int i = threadIdx.x; i < 512 * 2; i += blockDim.x) {
-            const float* g = G->iq2xs[i >> 1] + 4 * (i & 1);
-            T->grid2[i >> 1][i & 1] =
-                (uint32_t)g[0] | ((uint32_t)g[1] << 8) | ((uint32_t)g[2] << 16) | ((uint32_t)g[3] << 24);
-        }
-    if (want3)
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-            const float* g = G->iq3xxs[i];
-            T->grid3[i] = (uint32_t)g[0] | ((uint32_t)g[1] << 8) | ((uint32_t)g[2] << 16) | ((uint32_t)g[3] << 24);
-        }
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) T->ksigns[i] = G->ksigns[i];
-}
-
 __global__ void __launch_bounds__(kThreads) k_gateup(Dev d, LayerW w, int layer) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int H = d.dm.hidden, I = d.dm.moe_inter;

@@ -63,9 +63,10 @@ struct Dev {
     int* tokens_out;             // [ctx] argmax written at index pos
     int* err;                    // error bits
     int head_grid;               // CTAs of the head kernel (partials length)
+    unsigned long long* trace;   // optional: global-timer stamp per grid barrier (CTA 0)
 };
 
-enum CounterSlot { kCntRouter = 8, kCntHead = 9, kCntTotal = 16 };
+enum CounterSlot { kCntRouter = 8, kCntHead = 9, kCntBarrier = 10, kCntTotal = 16 };
 
 // Launchers.  All run on `st` and read pos/token from device memory, so they
 // can be captured once into a CUDA graph.
@@ -83,5 +84,8 @@ int head_grid_size(int device, const Dims& m);
 size_t attn_scores_bytes(const Dims& m);
 bool geometry_supported(const Dims& m);
 cudaError_t configure_kernels();
+// Persistent one-launch decode step (qx_mega.cu).
+int mega_setup(int device, const Dims& m, int* grid_out);
+cudaError_t launch_decode_step(const Dev& d, const LayerW* layers_dev, int grid, cudaStream_t st);
 
 }  // namespace qx

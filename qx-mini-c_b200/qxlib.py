@@ -121,6 +121,7 @@ ENGINE_SYMBOLS = [
 
 VERIFY_CHECKSUMS = 0x1
 NO_GRAPH = 0x2
+PER_STAGE = 0x4
 
 
 def cuda():
