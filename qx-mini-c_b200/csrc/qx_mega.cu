@@ -567,7 +567,7 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     const int XS = std::max(std::max(H, Q), 8 * I);
     MegaLayout L{};
     uint32_t off = 0;
-    L.xs = off; off += a16u((size_t)XS * 4);
+    L.xs = off; off += a16u(std::max((size_t)XS * 4, (size_t)kVChunk * 132));
     L.xb = off; off += a16u((size_t)XS / 16 * 32 * 4);
     L.sb = off; off += a16u((size_t)XS / 256 * 4 + 32);
     L.tab = off; off += a16u(sizeof(IqTab));
