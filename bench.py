@@ -171,18 +171,34 @@ def run_reference_arm(args, rank, world):
 
 
 # --------------------------------------------------------------------------- GPU arm
-def kernel_bytes(cfg, name, position):
-    """Algorithmic HBM bytes of one launch of each kernel (weights + KV it must read)."""
+def phase_bytes(cfg, position):
+    """Algorithmic HBM bytes each phase of one layer must read at `position`
+    (weights of that phase, the INT8 KV history for attention)."""
     H, Q, KV, I = cfg.hidden, cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.moe_intermediate
     return {
-        "embed_q4k": (H // 256) * 144,
-        "qkv_iq4xs": (Q + 2 * KV) * (H // 256) * 136 + 2 * H * 4,
-        "attn_splitkv": (position + 1) * (2 * KV + 8),
-        "oproj_iq4xs": H * (Q // 256) * 136 + Q * 4,
-        "router_top8": cfg.experts * H * 4 + H * 4,
-        "gateup_iq2xs_swiglu": 8 * 2 * I * (H // 256) * 74,
-        "down_iq3xxs_wsum": 8 * H * (I // 256) * 98,
-        "head_q6k_argmax": cfg.vocab * (H // 256) * 210 + H * 4,
+        "qkv": (Q + 2 * KV) * (H // 256) * 136 + 2 * H * 4,
+        "attn": (position + 1) * (2 * KV + 8),
+        "oproj": H * (Q // 256) * 136,
+        "router": cfg.experts * H * 4 + H * 4,
+        "gateup": 8 * 2 * I * (H // 256) * 74,
+        "down": 8 * H * (I // 256) * 98,
+        "head": cfg.vocab * (H // 256) * 210 + H * 4,
+    }
+
+
+def kernel_bytes(cfg, name, position):
+    """Algorithmic HBM bytes of one launch of each kernel (weights + KV it must read)."""
+    pb = phase_bytes(cfg, position)
+    return {
+        "embed_q4k": (cfg.hidden // 256) * 144,
+        "qkv_iq4xs": pb["qkv"],
+        "attn_splitkv": pb["attn"],
+        "oproj_iq4xs": pb["oproj"] + cfg.q_heads * cfg.head_dim * 4,
+        "router_top8": pb["router"],
+        "gateup_iq2xs_swiglu": pb["gateup"],
+        "down_iq3xxs_wsum": pb["down"],
+        "head_q6k_argmax": pb["head"],
+        "decode_step_persistent": W.weight_bytes_per_token(cfg) + W.kv_bytes_per_token(cfg, position),
     }.get(name, 0)
 
 
@@ -193,6 +209,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling case only: the same model with fewer layers (default: all 48)")
     args = ap.parse_args()
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
@@ -204,6 +222,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     cfg = W.model_config(full=True)
+    if args.layers:
+        cfg.layers = args.layers
     img = qxlib.build_image(cfg)
     stream = torch.cuda.Stream()
     eng = qxlib.Engine(img, ctx=W.DECODE_STEPS + 8, device=local, stream=stream.cuda_stream)
@@ -265,13 +285,16 @@ def main():
     h2d = (q1["host_to_device_bytes"] - q0["host_to_device_bytes"]) // args.steps
     d2h = (q1["device_to_host_bytes"] - q0["device_to_host_bytes"]) // args.steps
 
-    # per-kernel device time (CUDA events between launches, outside the timed region)
-    kt = eng.time_kernels(W.START_TOKEN, 0, 16)
-    per_token = {k: v[0] * v[1] / 16.0 for k, v in kt.items()}
+    # per-kernel device time (CUDA events between launches, outside the timed
+    # region) at positions 120..135, the middle of the 256-token workload; the
+    # KV history there is the one the generation above left behind
+    tpos, tn = 120, 16
+    kt = eng.time_kernels(W.START_TOKEN, tpos, tn)
+    per_token = {k: v[0] * v[1] / tn for k, v in kt.items()}
     total_ms = sum(per_token.values())
     dom = max(per_token, key=per_token.get)
     dom_ms, dom_n = kt[dom][0], kt[dom][1]
-    dom_bytes = kernel_bytes(cfg, dom, 8)
+    dom_bytes = kernel_bytes(cfg, dom, tpos + (tn - 1) / 2.0)
     peak, peak_kind = peaks()
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
     traffic = None
@@ -281,6 +304,17 @@ def main():
             traffic = json.load(open(tpath)).get(dom)
         except Exception:
             traffic = None
+    # per-phase breakdown of the persistent step (grid-barrier timestamps)
+    phases = None
+    if dom == "decode_step_persistent":
+        tr = eng.phase_trace(W.START_TOKEN, 128)
+        pb = phase_bytes(cfg, 128)
+        phases = {}
+        for name in eng.PHASES:
+            us = float(np.median(tr[name]))
+            phases[name] = {"us_per_layer": round(us, 2), "GB/s": round(pb[name] / us / 1e3, 1)}
+        phases["head"] = {"us": round(tr["head"], 2), "GB/s": round(pb["head"] / tr["head"] / 1e3, 1)}
+        phases["step_us"] = round(tr["total"], 1)
     step_bytes = W.weight_bytes_per_token(cfg) + sum(W.kv_bytes_per_token(cfg, p) for p in range(steps_tok)) / steps_tok
     step_gbs = step_bytes * value / world / 1e9
 
@@ -289,7 +323,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-quant model and inputs; no real checkpoint available)",
-        "config": {"workload": WORKLOAD, "tokens_per_step": steps_tok, "batch": 1,
+        "config": {"workload": WORKLOAD if not args.layers else "profiling case: %d layers" % cfg.layers,
+                   "tokens_per_step": steps_tok, "batch": 1,
                    "parallelism": "single GPU" if world == 1 else "%d independent replicas" % world,
                    "l2": "inputs larger than L2 (10.25 GB of weights streamed per token)"},
         "hbm_gbs_per_gpu": step_gbs, "hbm_frac_of_measured": step_gbs / peak,
@@ -297,6 +332,7 @@ def main():
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
                      "bytes_per_launch": dom_bytes, "avg_launch_ms": dom_ms, "share_of_step": per_token[dom] / total_ms},
+        "phases_at_position_128": phases,
         "kernels_ms_per_token": {k: round(v, 5) for k, v in sorted(per_token.items(), key=lambda kv: -kv[1])},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},

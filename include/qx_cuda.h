@@ -188,10 +188,17 @@ int qx_cuda_time_kernels(qx_cuda_engine *engine, uint32_t token, uint32_t positi
                          char *names, uint64_t names_len, float *ms_avg, uint32_t *launches,
                          uint32_t max_kernels, uint32_t *kernel_count, char *err, uint64_t err_len);
 
-/* One decode step with a device timestamp (ns, %globaltimer) taken by CTA 0
- * after each grid barrier of the persistent step kernel: stamps[0] = start,
- * then embedding+QKV, attention, O projection, router, gate/up, down per
- * layer, then the head.  A profiling aid (it allocates a small buffer). */
+/* One decode step of the persistent step kernel with device timestamps (ns,
+ * %globaltimer).  With n = 3 + 6 * layers and G the kernel's CTA count, the
+ * full record has n * (9 + G) stamps (fewer are written if max_stamps is
+ * smaller; *count says how many):
+ *   [0, n)       stamps[0] = start, then CTA 0's exit from each grid barrier:
+ *                embedding+QKV, attention, O projection, router, gate/up,
+ *                down per layer, then the head (last slot unused);
+ *   [n, 9n)      eight in-phase markers of CTA 0 per barrier epoch e at
+ *                n + 8e + k (0 where the phase sets no marker k);
+ *   [9n, 9n+nG)  each CTA's arrival at barrier e at 9n + e*G + cta.
+ * A profiling aid (it allocates a buffer); not part of the reference API. */
 int qx_cuda_phase_trace(qx_cuda_engine *engine, uint32_t token, uint32_t position, uint64_t *stamps_ns,
                         uint32_t max_stamps, uint32_t *count, char *err, uint64_t err_len);
 

@@ -668,16 +668,17 @@ QX_API int qx_cuda_phase_trace(qx_cuda_engine* E, uint32_t token, uint32_t posit
     if (position >= (uint32_t)E->dm.ctx || token >= (uint32_t)E->dm.vocab) { set_err(err, n, "invalid argument"); return 0; }
     DeviceGuard g(E->device);
     const uint32_t nst = 2u + 6u * (uint32_t)E->dm.layers + 1u;
+    const uint32_t total = nst * (9u + (uint32_t)E->mega_grid);
     unsigned long long* tr = nullptr;
-    if (!cuda_ok(cudaMalloc((void**)&tr, nst * 8), "cudaMalloc(trace)", err, n)) return 0;
-    cudaMemsetAsync(tr, 0, nst * 8, E->stream);
+    if (!cuda_ok(cudaMalloc((void**)&tr, (size_t)total * 8), "cudaMalloc(trace)", err, n)) return 0;
+    cudaMemsetAsync(tr, 0, (size_t)total * 8, E->stream);
     bool ok = set_scalars(E, token, position, err, n);
     if (ok) {
         Dev d = E->dev;
         d.trace = tr;
         ok = cuda_ok(qx::launch_decode_step(d, E->layers_dev, E->mega_grid, E->stream), "launch", err, n) && finish(E, err, n);
     }
-    const uint32_t c = nst < max_stamps ? nst : max_stamps;
+    const uint32_t c = total < max_stamps ? total : max_stamps;
     if (ok) ok = cuda_ok(cudaMemcpy(stamps_ns, tr, c * 8, cudaMemcpyDeviceToHost), "trace d2h", err, n);
     cudaFree(tr);
     if (ok) *count = c;

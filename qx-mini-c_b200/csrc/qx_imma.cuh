@@ -27,29 +27,36 @@ namespace qx {
 constexpr int kLimbs = 7;           // 56-bit fixed point
 constexpr int kOffsetBits = 55;
 
-// B operand in shared memory: for each 16-value group G, 32 words in lane
-// order; lane 4n+t holds limb n of values 16G+4t .. 16G+4t+3 (one byte each,
-// value order).  Lane group n = 7 holds the constant 1 (offset column).
+// B operand in shared memory: for each 16-value group G, kXG words of which
+// the first 32 are in lane order; lane 4n+t holds limb n of values
+// 16G+4t .. 16G+4t+3 (one byte each, value order).  Lane group n = 7 holds the
+// constant 1 (offset column).  The stride of 36 words (not 32) makes the
+// quantizer's stores conflict-free: the 8 groups a warp writes at once start
+// in banks 0, 4, ..., 28.
+constexpr int kXG = 36;
+__host__ __device__ constexpr size_t xq_words(int K) { return (size_t)K / 16 * kXG; }
+
 struct XQ {
-    const uint32_t* b;   // [K/16][32]
+    const uint32_t* b;   // [K/16][kXG]
     const int* s;        // [K/256] block exponents S_b
 };
 
+// Exact 2^e as a double for -1022 <= e <= 1023.
+__device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(1023 + e) << 52); }
+
 // ---- activation quantization ------------------------------------------------
 
-// X' = round(|x| * 2^S) * sign + 2^55, split in two words.
+// X' = round(x * 2^S) + 2^55 (halfway cases away from zero), split in two
+// words.  S = 54 - E(block max) lies in [-73, 180]; the scale is applied as two
+// exact power-of-two factors in [2^-37, 2^90], so y = x * 2^S is exact (a
+// product that underflows has |x * 2^S| < 2^-126 and rounds to 0 either way)
+// and |y| < 2^55 converts to int64 exactly.  Rounding: truncate, then step
+// away from zero when the (exact) dropped fraction is at least 1/2.
 __device__ __forceinline__ void to_fixed(float x, int S, uint32_t& hi, uint32_t& lo) {
-    const uint32_t bits = __float_as_uint(x);
-    int e = (int)((bits >> 23) & 255u);
-    uint32_t m = bits & 0x7fffffu;
-    if (e) m |= 0x800000u; else e = 1;
-    const int sh = e - 150 + S;           // |x| * 2^S = m * 2^sh, sh <= 31 by the choice of S
-    uint64_t mag = 0;
-    if (m) {
-        if (sh >= 0) mag = (uint64_t)m << sh;
-        else if (sh > -40) mag = ((uint64_t)m + ((1ull << (-sh)) >> 1)) >> (-sh);
-    }
-    const int64_t X = (bits >> 31) ? -(int64_t)mag : (int64_t)mag;
+    const int s1 = S >> 1, s2 = S - s1;
+    const float y = __fmul_rn(__fmul_rn(x, __int_as_float((s1 + 127) << 23)), __int_as_float((s2 + 127) << 23));
+    long long X = __float2ll_rz(y);
+    if (fabsf(__fsub_rn(y, truncf(y))) >= 0.5f) X += y < 0.f ? -1 : 1;
     const uint64_t Xp = (uint64_t)(X + (1ll << kOffsetBits));
     hi = (uint32_t)(Xp >> 32);
     lo = (uint32_t)Xp;
@@ -65,40 +72,36 @@ __device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, u
     out[3] = __byte_perm(t1, t3, 0x7632);
 }
 
-// Quantize xs[0..K) (shared memory floats, K a multiple of 256) into the B
-// layout.  Every warp of the CTA must call it (warp-wide max per block).
+// Quantize xs[0..K) (shared memory floats, 16-byte aligned, K a multiple of
+// 256) into the B layout.  One warp per 256-value block: lane 4*gl + t
+// converts values 16G+4t..+3 of groups G = gl and gl + 8 of the block.
 __device__ __forceinline__ void build_xq(const float* xs, int K, uint32_t* xb, int* sb) {
-    const int lane = threadIdx.x & 31;
-    for (int base = threadIdx.x * 8; base - lane * 8 < K; base += blockDim.x * 8) {
-        const bool active = base < K;
-        float v[8];
-        float mx = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            v[i] = active ? xs[base + i] : 0.f;
-            mx = fmaxf(mx, fabsf(v[i]));
-        }
+    const int lane = threadIdx.x & 31, t = lane & 3, gl = lane >> 2;
+    for (int blk = threadIdx.x >> 5; blk < K / 256; blk += blockDim.x >> 5) {
+        const float4 u = reinterpret_cast<const float4*>(xs + blk * 256)[lane];
+        const float4 v = reinterpret_cast<const float4*>(xs + blk * 256 + 128)[lane];
+        float mx = fmaxf(fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))),
+                         fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (!active) continue;
         const int E = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 255u) - 127 : -126;
         const int S = 54 - (E < -126 ? -126 : E);
-        if (lane == 0) sb[base / 256] = S;
-        uint32_t hi[8], lo[8];
+        if (lane == 0) sb[blk] = S;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) to_fixed(v[i], S, hi[i], lo[i]);
-        const int G = base / 16, t0 = (base % 16) / 4;
-        uint32_t w[4];
-        uint32_t* dst = xb + G * 32;
+        for (int h = 0; h < 2; ++h) {
+            const float4 q = h ? v : u;
+            uint32_t hi[4], lo[4], w[4];
+            to_fixed(q.x, S, hi[0], lo[0]);
+            to_fixed(q.y, S, hi[1], lo[1]);
+            to_fixed(q.z, S, hi[2], lo[2]);
+            to_fixed(q.w, S, hi[3], lo[3]);
+            uint32_t* dst = xb + (size_t)(blk * 16 + 8 * h + gl) * kXG + t;
+            transpose4(lo[0], lo[1], lo[2], lo[3], w);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {           // values base+4h .. base+4h+3 -> lane t0+h
-            const int t = t0 + h;
-            transpose4(lo[4 * h], lo[4 * h + 1], lo[4 * h + 2], lo[4 * h + 3], w);
+            for (int n = 0; n < 4; ++n) dst[4 * n] = w[n];
+            transpose4(hi[0], hi[1], hi[2], hi[3], w);
 #pragma unroll
-            for (int n = 0; n < 4; ++n) dst[n * 4 + t] = w[n];
-            transpose4(hi[4 * h], hi[4 * h + 1], hi[4 * h + 2], hi[4 * h + 3], w);
-#pragma unroll
-            for (int n = 0; n < 3; ++n) dst[(4 + n) * 4 + t] = w[n];
-            dst[28 + t] = 0x01010101u;
+            for (int n = 0; n < 3; ++n) dst[4 * (4 + n)] = w[n];
+            dst[28] = 0x01010101u;
         }
     }
 }
@@ -108,7 +111,7 @@ __device__ __forceinline__ void build_xq(const float* xs, int K, uint32_t* xb, i
 // 6 in the int32 domain before conversion (Acc::flush), so its weight is 0.
 __device__ __forceinline__ double limb_weight(int lane, int r) {
     const int n = 2 * (lane & 3) + (r & 1);
-    return n < kLimbs ? ldexp(1.0, 8 * n) : 0.0;
+    return n < kLimbs ? pow2d(8 * n) : 0.0;
 }
 
 // ---- tensor-core primitives -------------------------------------------------
@@ -181,19 +184,17 @@ __device__ __forceinline__ uint32_t signed_bytes(uint32_t mag, uint32_t nib) {
 // One warp; rows r0 (= g) and r1 (= g+8) of a 16-row tile staged in shared
 // memory; blocks [b0, b1) of the row.  Accumulates into acc.
 
-// IQ4_NL codebook lookup of the four nibbles held in bits 0-3 of each byte
-// of n (bytes 0..15), via byte permutes of the 16-byte table K[0..3].
-__device__ __forceinline__ uint32_t kv_lookup4(uint32_t n, const uint32_t K[4]) {
-    const uint32_t i3 = n & 0x07070707u;
-    const uint32_t packed = i3 | (i3 >> 4);                       // byte0 = n0|n1<<4, byte2 = n2|n3<<4
-    const uint32_t sel = __byte_perm(packed, 0u, 0x0020);         // n0 | n1<<4 | n2<<8 | n3<<12
-    const uint32_t lo = __byte_perm(K[0], K[1], sel), hi = __byte_perm(K[2], K[3], sel);
-    const uint32_t hbit = (n & 0x08080808u) << 4;                  // bit 3 -> bit 7
-    uint32_t mask;                                                // replicate bit 7 over each byte
-    // PTX prmt in its default mode honours the sign-replicate bit of each
-    // selector nibble (CUDA's __byte_perm ignores it).
-    asm("prmt.b32 %0, %1, 0, 0xba98;" : "=r"(mask) : "r"(hbit));
-    return (hi & mask) | (lo & ~mask);
+// Codebook lookup of all eight nibbles of q: lo = entries of the low nibbles
+// of bytes 0..3, hi = entries of the high nibbles.  __byte_perm reads only the
+// low 3 bits of each selector nibble, so the first two permutes fetch entries
+// n & 7 from the lower and upper halves of the 16-byte table; a third picks
+// the half by bit 3 of each nibble; two more split low and high nibbles.
+__device__ __forceinline__ void kv_lookup8(uint32_t q, const uint32_t K[4], uint32_t& lo, uint32_t& hi) {
+    const uint32_t pick = ((q & 0x88888888u) >> 1) | 0x32103210u;   // nibble k -> byte k or 4 + k
+    const uint32_t r0 = __byte_perm(__byte_perm(K[0], K[1], q), __byte_perm(K[2], K[3], q), pick);
+    const uint32_t r1 = __byte_perm(__byte_perm(K[0], K[1], q >> 16), __byte_perm(K[2], K[3], q >> 16), pick >> 16);
+    lo = __byte_perm(r0, r1, 0x6420);
+    hi = __byte_perm(r0, r1, 0x7531);
 }
 
 // IQ4_XS: m16n8k32, natural order (lane t: bytes 4t..4t+3 of each 16-byte
@@ -215,14 +216,15 @@ __device__ __forceinline__ void dot_iq4_xs_mma(const uint8_t* r0, const uint8_t*
             const int ls1 = ((sl1 >> (4 * ib)) & 15) | (((sh1 >> (2 * ib)) & 3) << 4);
             const uint32_t q0 = *reinterpret_cast<const uint32_t*>(p0 + 8 + 16 * ib + 4 * t);
             const uint32_t q1 = *reinterpret_cast<const uint32_t*>(p1 + 8 + 16 * ib + 4 * t);
-            const uint32_t a0 = kv_lookup4(q0, K), a2 = kv_lookup4(q0 >> 4, K);
-            const uint32_t a1 = kv_lookup4(q1, K), a3 = kv_lookup4(q1 >> 4, K);
+            uint32_t a0, a1, a2, a3;
+            kv_lookup8(q0, K, a0, a2);
+            kv_lookup8(q1, K, a1, a3);
             const int G = b * 16 + 2 * ib;
             int D[4];
-            mma_k32(D, a0, a1, a2, a3, x.b[G * 32 + lane], x.b[(G + 1) * 32 + lane]);
+            mma_k32(D, a0, a1, a2, a3, x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
             acc.add(D, ls0 - 32, ls1 - 32);
         }
-        const double sc = ldexp(1.0, -x.s[b]);
+        const double sc = pow2d(-x.s[b]);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -247,10 +249,10 @@ __device__ __forceinline__ void dot_iq2_xs_mma(const uint8_t* r0, const uint8_t*
             const int sc0 = 1 + 2 * ((p0[66 + (gq >> 1)] >> (4 * (gq & 1))) & 15);
             const int sc1 = 1 + 2 * ((p1[66 + (gq >> 1)] >> (4 * (gq & 1))) & 15);
             int D[4];
-            mma_k16(D, a0, a1, x.b[(b * 16 + gq) * 32 + lane]);
+            mma_k16(D, a0, a1, x.b[(b * 16 + gq) * kXG + lane]);
             acc.add(D, sc0, sc1);
         }
-        const double sc = ldexp(1.0, -x.s[b]) * 0.125;
+        const double sc = pow2d(-x.s[b] - 3);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -276,10 +278,10 @@ __device__ __forceinline__ void dot_iq3_xxs_mma(const uint8_t* r0, const uint8_t
             const uint32_t a3 = signed_bytes(T.grid3[p1[2 + 8 * ib + 4 + t]], sB1 >> (4 * half));
             const int G = b * 16 + 2 * ib;
             int D[4];
-            mma_k32(D, a0, a1, a2, a3, x.b[G * 32 + lane], x.b[(G + 1) * 32 + lane]);
+            mma_k32(D, a0, a1, a2, a3, x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
             acc.add(D, 1 + 2 * (int)(aux0 >> 28), 1 + 2 * (int)(aux1 >> 28));
         }
-        const double sc = ldexp(1.0, -x.s[b]) * 0.25;
+        const double sc = pow2d(-x.s[b] - 2);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -317,13 +319,13 @@ __device__ __forceinline__ void dot_q6_k_mma(const uint8_t* r0, const uint8_t* r
                     const uint32_t a1 = q6_word((s & 1) ? qlB1 : qlA1, qh1, s);
                     const int gq = 8 * h + 2 * s + lh;      // 16-value group index in the block
                     int D[4];
-                    mma_k16(D, a0, a1, x.b[(b * 16 + gq) * 32 + lane]);
+                    mma_k16(D, a0, a1, x.b[(b * 16 + gq) * kXG + lane]);
                     const int si = 8 * h + lh + 2 * s;
                     acc.add(D, (int)c0[si], (int)c1[si]);
                 }
             }
         }
-        const double sc = ldexp(1.0, -x.s[b]);
+        const double sc = pow2d(-x.s[b]);
         acc.flush((double)h2f(ld16(p0 + 208)) * sc, (double)h2f(ld16(p1 + 208)) * sc, lw);
     }
 }

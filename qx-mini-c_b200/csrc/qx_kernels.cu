@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(Dev d, LayerW w) {
     Carve cv(smem);
     uint8_t* tiles = cv.take<uint8_t>(kQkvTiles * tb);
     float* xs = cv.take<float>(H);
-    uint32_t* xb = cv.take<uint32_t>(H / 16 * 32);
+    uint32_t* xb = cv.take<uint32_t>(xq_words(H));
     int* sb = cv.take<int>(H / 256);
     double* part = cv.take<double>(kWarps * kTileRows);
     const int ntiles = (Q + 2 * KV) / kTileRows;
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dev d, LayerW w) {
     Carve cv(smem);
     uint8_t* tile = cv.take<uint8_t>(tb);
     float* xs = cv.take<float>(Q);
-    uint32_t* xb = cv.take<uint32_t>(Q / 16 * 32);
+    uint32_t* xb = cv.take<uint32_t>(xq_words(Q));
     int* sb = cv.take<int>(Q / 256);
     double* part = cv.take<double>(kWarps * kTileRows);
     stage_copy(tile, w.wo + (size_t)blockIdx.x * tb, tb);
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dev d, LayerW w, int layer)
     uint8_t* tiles = cv.take<uint8_t>(2 * tb);
     IqTab* T = cv.take<IqTab>(1);
     float* xs = cv.take<float>(H);
-    uint32_t* xb = cv.take<uint32_t>(H / 16 * 32);
+    uint32_t* xb = cv.take<uint32_t>(xq_words(H));
     int* sb = cv.take<int>(H / 256);
     double* part = cv.take<double>(kWarps * kTileRows);
     const int tiles_per_expert = I / kTileRows;
@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(kThreads) k_down(Dev d, LayerW w, int layer) {
     uint8_t* tiles = cv.take<uint8_t>(8 * tb);
     IqTab* T = cv.take<IqTab>(1);
     float* hs = cv.take<float>(8 * I);
-    uint32_t* xb = cv.take<uint32_t>(8 * (I / 16) * 32);
+    uint32_t* xb = cv.take<uint32_t>(xq_words(8 * I));
     int* sb = cv.take<int>(8 * (I / 256));
     double* part = cv.take<double>(kWarps * kTileRows);
     const size_t slice = (size_t)H * rb;
@@ -392,14 +392,14 @@ __global__ void __launch_bounds__(kThreads) k_down(Dev d, LayerW w, int layer) {
     cp_async_commit();
     load_iq_tables(T, d.tables, false, true);
     copy_to_smem(d.hbuf, hs, 8 * I);
-    for (int k = 0; k < 8; ++k) build_xq(hs + k * I, I, xb + k * (I / 16) * 32, sb + k * (I / 256));
+    build_xq(hs, 8 * I, xb, sb);   // expert k's groups start at k * I / 16 (I % 256 == 0)
     cp_async_wait<0>();
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
     const uint8_t* base = tiles + warp * tb;
     Acc acc{};
     dot_iq3_xxs_mma(base + g * rb, base + (g + 8) * rb, 0, nblk,
-                    XQ{xb + warp * (I / 16) * 32, sb + warp * (I / 256)}, *T, lane, acc);
+                    XQ{xb + warp * xq_words(I), sb + warp * (I / 256)}, *T, lane, acc);
     store_tile_rows(part, warp, acc);
     __syncthreads();
     if (threadIdx.x < kTileRows) {
@@ -433,7 +433,7 @@ __global__ void __launch_bounds__(kThreads) k_head(Dev d) {
     Carve cv(smem);
     uint8_t* ring = cv.take<uint8_t>(kHeadStages * stage);
     float* xs = cv.take<float>(H);
-    uint32_t* xb = cv.take<uint32_t>(H / 16 * 32);
+    uint32_t* xb = cv.take<uint32_t>(xq_words(H));
     int* sb = cv.take<int>(H / 256);
     double* part = cv.take<double>(kWarps * kTileRows);
     const int ngroups = V / (kTileRows * kHeadTiles);
@@ -553,7 +553,7 @@ __global__ void __launch_bounds__(1024) k_topn(Dev d, int top_n, int* out_idx, f
 // ---------------------------------------------------------------------------
 namespace {
 size_t a16(size_t v) { return (v + 15) / 16 * 16; }
-size_t xq_bytes(int K) { return a16((size_t)K * 4) + a16((size_t)K / 16 * 32 * 4) + a16((size_t)K / 256 * 4); }
+size_t xq_bytes(int K) { return a16((size_t)K * 4) + a16(xq_words(K) * 4) + a16((size_t)K / 256 * 4); }
 size_t part_bytes() { return a16((size_t)kWarps * kTileRows * 8); }
 size_t smem_qkv(const Dims& m) { return 16 + a16((size_t)kQkvTiles * kTileRows * (m.hidden / 256) * 136) + xq_bytes(m.hidden) + part_bytes(); }
 size_t smem_oproj(const Dims& m) { return 16 + a16((size_t)kTileRows * (m.q_dim() / 256) * 136) + xq_bytes(m.q_dim()) + part_bytes(); }
@@ -561,7 +561,7 @@ size_t smem_router(const Dims& m) { return (size_t)m.hidden * 4; }
 size_t smem_gateup(const Dims& m) { return 16 + a16(2 * (size_t)kTileRows * (m.hidden / 256) * 74) + a16(sizeof(IqTab)) + xq_bytes(m.hidden) + part_bytes(); }
 size_t smem_down(const Dims& m) {
     return 16 + a16(8 * (size_t)kTileRows * (m.moe_inter / 256) * 98) + a16(sizeof(IqTab)) + a16((size_t)8 * m.moe_inter * 4) +
-           a16((size_t)8 * m.moe_inter / 16 * 32 * 4) + a16((size_t)8 * m.moe_inter / 256 * 4) + part_bytes();
+           a16(xq_words(8 * m.moe_inter) * 4) + a16((size_t)8 * m.moe_inter / 256 * 4) + part_bytes();
 }
 size_t smem_head(const Dims& m) {
     return 16 + a16((size_t)kHeadStages * kHeadTiles * kTileRows * (m.hidden / 256) * 210) + xq_bytes(m.hidden) + part_bytes();

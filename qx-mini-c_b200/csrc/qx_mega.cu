@@ -26,7 +26,7 @@ namespace {
 constexpr int kMT = 256;                 // threads per CTA
 constexpr int kMW = kMT / 32;
 constexpr int kMaxTasks = 96;            // (tile, block) tasks per CTA per phase
-constexpr long long kSpinLimit = 1ll << 26;
+constexpr long long kSpinLimit = 1ll << 24;   // ~1e7 L2 round trips: seconds
 enum { QXH_IQ4_XS_F = 23, QXH_IQ2_XS_F = 17, QXH_IQ3_XXS_F = 18, QXH_Q6_K_F = 14 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -42,19 +42,30 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-__device__ __forceinline__ void grid_sync(unsigned* bar, unsigned& epoch, int* err, unsigned long long* trace) {
+// Trace buffer (optional, profiling only): [0, n) exit stamp of each barrier
+// taken by CTA 0 (slot 0 = kernel start), [n, 9n) eight in-phase markers of
+// CTA 0 per barrier epoch, [9n, 9n + n*grid) each CTA's arrival at each
+// barrier; n = 3 + 6 * layers.
+__device__ __forceinline__ size_t trace_n(const Dev& d) { return 3 + 6 * (size_t)d.dm.layers; }
+
+__device__ __forceinline__ void mark(const Dev& d, unsigned epoch, int k) {
+    if (d.trace && blockIdx.x == 0 && threadIdx.x == 0) d.trace[trace_n(d) + (size_t)(epoch + 1) * 8 + k] = global_ns();
+}
+
+__device__ __forceinline__ void grid_sync(unsigned* bar, unsigned& epoch, const Dev& d) {
+    int* err = d.err;
+    unsigned long long* trace = d.trace;
     __syncthreads();
     epoch += 1;
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
+        if (trace) trace[9 * trace_n(d) + (size_t)epoch * gridDim.x + blockIdx.x] = global_ns();
+        // the CTA's writes are ordered before this release by the bar.sync above
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         const unsigned target = epoch * gridDim.x;
         long long it = 0;
         while (ld_acquire(bar) < target) {
             if (++it > kSpinLimit) { atomicOr(err, kErrTimeout); break; }
-            __nanosleep(64);
         }
-        __threadfence();
         if (trace && blockIdx.x == 0) trace[epoch] = global_ns();
     }
     __syncthreads();
@@ -166,7 +177,7 @@ constexpr int kVChunk = 128;   // positions of V staged per pass
 // Attention of query head h (all 256 threads).  w_s: >= pos+1 doubles of
 // shared scratch; v_s: kVChunk*128 bytes + kVChunk floats of shared scratch.
 __device__ void attn_head(const Dev& d, const LayerW& w, int layer, int h, int pos, AttnSmem& S, double* w_s,
-                          uint8_t* v_s) {
+                          uint8_t* v_s, unsigned epoch) {
     const int D = 128, KVH = d.dm.kv_heads, group = d.dm.q_heads / KVH;
     const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx, g = h / group, i = threadIdx.x;
     const int warp = i >> 5, lane = i & 31;
@@ -182,6 +193,7 @@ __device__ void attn_head(const Dev& d, const LayerW& w, int layer, int h, int p
         else warp_norm_rope(S.qv, w.q_norm, rope, lane);
     }
     __syncthreads();
+    mark(d, epoch, 0);
     float ka = 0.f, va = 0.f;
     for (int j = i; j < KV; j += kMT) {
         ka = fmaxf(ka, isfinite(S.kcur[j]) ? fabsf(S.kcur[j]) : 0.f);
@@ -197,6 +209,7 @@ __device__ void attn_head(const Dev& d, const LayerW& w, int layer, int h, int p
         S.v8[j] = (int8_t)max(-127, min(127, qq));
     }
     __syncthreads();
+    mark(d, epoch, 1);
     const size_t slot = (size_t)layer * ctx + pos;
     if (h == 0) {
         for (int j = i; j < KV; j += kMT) {
@@ -229,10 +242,12 @@ __device__ void attn_head(const Dev& d, const LayerW& w, int layer, int h, int p
         mloc = fmax(mloc, s);
     }
     const double mx = block_max_d(mloc, S.sd);
+    mark(d, epoch, 2);
     for (int t = i; t < T; t += kMT) w_s[t] = exp(w_s[t] - mx);
     double den = fixed_order_sum(w_s, T, S.sd);
     if (!isfinite(den) || den <= 0.0) den = 1.0;
     for (int t = i; t < T; t += kMT) w_s[t] = w_s[t] / den;
+    mark(d, epoch, 3);
     // context: V of head g staged kVChunk positions at a time; thread i < 128
     // accumulates dim i over t in order, as the reference does.
     int8_t* vch = reinterpret_cast<int8_t*>(v_s);
@@ -369,41 +384,51 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             const double rms = sqrt(ss / (double)H + 1.0e-6);
             for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * w.attn_norm[i];
             __syncthreads();
+            mark(d, epoch, 0);
             build_xq(xs, H, xb, sb);
             issue_oproj(d, w, buf[1 - qb]);
             cp_async_commit();
+            __syncthreads();
+            mark(d, epoch, 1);
             cp_async_wait<1>();
             __syncthreads();
+            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(H / 256) * 136u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items((Q + 2 * KV) / kTileRows), nblk = H / 256;
             run_tasks<QXH_IQ4_XS_F>(buf[qb], tb, rb, mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
+            mark(d, epoch, 3);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT)
                 d.qkv[item_id(r / kTileRows) * kTileRows + r % kTileRows] =
                     finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
-            grid_sync(bar, epoch, d.err, d.trace);
+            grid_sync(bar, epoch, d);
         }
         // ---------------- attention (CTAs 0..Hq-1) ----------------
         issue_router(d, w, buf[qb]);
         cp_async_commit();
         for (int h = blockIdx.x; h < m.q_heads; h += gridDim.x)
-            attn_head(d, w, layer, h, pos, attn, reinterpret_cast<double*>(smem + L.xb), smem + L.xs);
-        grid_sync(bar, epoch, d.err, d.trace);
+            attn_head(d, w, layer, h, pos, attn, reinterpret_cast<double*>(smem + L.xb), smem + L.xs, epoch);
+        grid_sync(bar, epoch, d);
         // ---------------- O projection (weights in buf[1-qb]) ----------------
         {
             copy_to_smem(d.ctxv, xs, Q);
+            mark(d, epoch, 0);
             build_xq(xs, Q, xb, sb);
+            __syncthreads();
+            mark(d, epoch, 1);
             cp_async_wait<1>();
             __syncthreads();
+            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(Q / 256) * 136u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = Q / 256;
             run_tasks<QXH_IQ4_XS_F>(buf[1 - qb], tb, rb, mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
+            mark(d, epoch, 3);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
                 const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
                 const float o = finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
                 d.attn_out[row] = o;
                 d.x[row] = d.x[row] + o;
             }
-            grid_sync(bar, epoch, d.err, d.trace);
+            grid_sync(bar, epoch, d);
         }
         // ---------------- router (weights in buf[qb]) ----------------
         {
@@ -416,8 +441,10 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             __syncthreads();
             if (blockIdx.x == 0)
                 for (int i = threadIdx.x; i < H; i += kMT) d.xn[i] = xs[i];
+            mark(d, epoch, 0);
             cp_async_wait<0>();
             __syncthreads();
+            mark(d, epoch, 1);
             const int mine = my_items(E);
             const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
             for (int k = 0; k < mine; ++k) {
@@ -431,21 +458,26 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 acc = block_sum_d(acc, scratch);
                 if (threadIdx.x == 0) d.router_logits[item_id(k)] = acc;
             }
-            grid_sync(bar, epoch, d.err, d.trace);
+            grid_sync(bar, epoch, d);
         }
         // ---------------- top-8 + gate/up (weights in buf[1-qb]) ----------------
         {
             top8(d, layer, sel, wsel, probs, scratch);
+            mark(d, epoch, 0);
             issue_gateup(d, w, sel, buf[1 - qb]);
             cp_async_commit();
             issue_down(d, w, sel, buf[qb]);
             cp_async_commit();
             build_xq(xs, H, xb, sb);            // xs still holds the FFN-normed input
+            __syncthreads();
+            mark(d, epoch, 1);
             cp_async_wait<1>();
             __syncthreads();
+            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(8 * (I / kTileRows)), nblk = H / 256;
             run_tasks<QXH_IQ2_XS_F>(buf[1 - qb], tb, rb, 2 * mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
+            mark(d, epoch, 3);
             const int tpe = I / kTileRows;
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
                 const int k = r / kTileRows, rr = r % kTileRows, it = item_id(k);
@@ -454,22 +486,27 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const double gd = (double)gv;
                 d.hbuf[(it / tpe) * I + (it % tpe) * kTileRows + rr] = (float)(gd / (1.0 + exp(-gd)) * (double)uv);
             }
-            grid_sync(bar, epoch, d.err, d.trace);
+            grid_sync(bar, epoch, d);
         }
         // ---------------- down (weights in buf[qb]) ----------------
         {
             copy_to_smem(d.hbuf, xs, 8 * I);
-            for (int e = 0; e < 8; ++e) build_xq(xs + e * I, I, xb + e * (I / 16) * 32, sb + e * (I / 256));
+            mark(d, epoch, 0);
+            build_xq(xs, 8 * I, xb, sb);     // expert e's groups start at e * I / 16 (I % 256 == 0)
             if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb]);
             else if ((int)blockIdx.x < m.vocab / (kTileRows * kHeadGroupTiles)) issue_head_group(d, blockIdx.x, buf[1 - qb]);
             cp_async_commit();
+            __syncthreads();
+            mark(d, epoch, 1);
             cp_async_wait<1>();
             __syncthreads();
+            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = I / 256;
             run_tasks<QXH_IQ3_XXS_F>(buf[qb], tb, rb, 8 * mine, nblk,
-                                     [&](int i) { return XQ{xb + (i % 8) * (I / 16) * 32, sb + (i % 8) * (I / 256)}; },
+                                     [&](int i) { return XQ{xb + (i % 8) * xq_words(I), sb + (i % 8) * (I / 256)}; },
                                      K4, T, part);
+            mark(d, epoch, 3);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
                 const int k = r / kTileRows, rr = r % kTileRows, row = item_id(k) * kTileRows + rr;
                 float moe = 0.0f;
@@ -478,7 +515,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 d.moe_out[row] = moe;
                 d.x[row] = d.x[row] + moe;
             }
-            grid_sync(bar, epoch, d.err, d.trace);
+            grid_sync(bar, epoch, d);
         }
         qb = 1 - qb;
     }
@@ -529,7 +566,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             d.best_val[blockIdx.x] = bv;
             d.best_idx[blockIdx.x] = bi;
         }
-        grid_sync(bar, epoch, d.err, d.trace);
+        grid_sync(bar, epoch, d);
         if (blockIdx.x == 0 && threadIdx.x == 0) {
             double v = d.best_val[0];
             int i = d.best_idx[0];
@@ -568,7 +605,7 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     MegaLayout L{};
     uint32_t off = 0;
     L.xs = off; off += a16u(std::max((size_t)XS * 4, (size_t)kVChunk * 132));
-    L.xb = off; off += a16u((size_t)XS / 16 * 32 * 4);
+    L.xb = off; off += a16u(xq_words(XS) * 4);
     L.sb = off; off += a16u((size_t)XS / 256 * 4 + 32);
     L.tab = off; off += a16u(sizeof(IqTab));
     L.part = off; off += a16u((size_t)kMaxTasks * kTileRows * 8);

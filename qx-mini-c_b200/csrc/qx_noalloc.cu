@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(kThreads) k_head_noalloc(const float* x, const
     uint8_t* ring = align16(smem);
     float* xs = reinterpret_cast<float*>(align16(ring + (size_t)kStages * stage));
     uint32_t* xb = reinterpret_cast<uint32_t*>(align16(reinterpret_cast<uint8_t*>(xs + H)));
-    int* sb = reinterpret_cast<int*>(align16(reinterpret_cast<uint8_t*>(xb + H / 16 * 32)));
+    int* sb = reinterpret_cast<int*>(align16(reinterpret_cast<uint8_t*>(xb + xq_words(H))));
     double* part = reinterpret_cast<double*>(align16(reinterpret_cast<uint8_t*>(sb + H / 256)));
     const int ngroups = V / (kTileRows * kTiles);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kThreads) k_head_noalloc(const float* x, const
 size_t smem_bytes(int H) {
     auto a16 = [](size_t v) { return (v + 15) / 16 * 16; };
     return 16 + a16((size_t)kStages * kTiles * kTileRows * (H / 256) * 210) + a16((size_t)H * 4) +
-           a16((size_t)H / 16 * 32 * 4) + a16((size_t)H / 256 * 4) + a16((size_t)kWarps * kTileRows * 8);
+           a16(xq_words(H) * 4) + a16((size_t)H / 256 * 4) + a16((size_t)kWarps * kTileRows * 8);
 }
 
 void set_err(char* err, uint64_t n, const char* m) {

@@ -116,7 +116,7 @@ ENGINE_SYMBOLS = [
     "qx_cuda_engine_create", "qx_cuda_engine_create_from_qxf", "qx_cuda_engine_create_from_image",
     "qx_cuda_engine_destroy", "qx_cuda_reset", "qx_cuda_decode_step", "qx_cuda_generate", "qx_cuda_final_head",
     "qx_cuda_moe_layer", "qx_cuda_attention_layer", "qx_cuda_embed", "qx_cuda_kv_write", "qx_cuda_kv_read",
-    "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_stream",
+    "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_phase_trace", "qx_cuda_stream",
 ]
 
 VERIFY_CHECKSUMS = 0x1
@@ -145,6 +145,7 @@ def cuda():
             "qx_cuda_kv_read": [P, U32, U32, U32, P, P, P, P, E, U64],
             "qx_cuda_profile_get": [P, C.POINTER(CudaProfile)],
             "qx_cuda_time_kernels": [P, U32, U32, U32, C.c_char_p, U64, P, P, U32, P, E, U64],
+            "qx_cuda_phase_trace": [P, U32, U32, P, U32, P, E, U64],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)
@@ -278,6 +279,36 @@ class Engine:
         self._call("qx_cuda_time_kernels", token, position, steps, names, len(names), _p(ms), _p(ln), 64, _p(cnt))
         keys = names.value.decode().split(";")
         return {k: (float(ms[i]), int(ln[i])) for i, k in enumerate(keys[:int(cnt[0])])}
+
+    PHASES = ("qkv", "attn", "oproj", "router", "gateup", "down")
+
+    def phase_trace(self, token, position, detail=False):
+        """Run one persistent decode step with %globaltimer stamps at every grid
+        barrier; returns {"qkv": [us per layer], ..., "head": us, "total": us}.
+        The "qkv" phase of layer 0 includes the embedding lookup.  With
+        detail=True also "markers" (epochs x 8 in-phase stamps of CTA 0, us from
+        the previous barrier exit, NaN where unset) and "arrivals" (epochs x
+        CTAs, us from the previous barrier exit)."""
+        n = 3 + 6 * self.layers
+        cap = n * (9 + 1024)
+        st = np.zeros(cap, np.uint64)
+        cnt = np.zeros(1, np.uint32)
+        self._call("qx_cuda_phase_trace", token, position, _p(st), cap, _p(cnt))
+        st = st[:int(cnt[0])].astype(np.int64)
+        ex = st[:n - 1]
+        d = np.diff(ex) / 1000.0
+        out = {name: d[i:6 * self.layers:6].tolist() for i, name in enumerate(self.PHASES)}
+        out["head"] = float(d[6 * self.layers:].sum())
+        out["total"] = float(d.sum())
+        if detail:
+            grid = (len(st) - 9 * n) // n
+            prev = np.concatenate([[ex[0]], ex[:-1]])[:, None]          # exit of epoch e-1
+            mk = st[n:9 * n].reshape(n, 8)[:n - 1].astype(np.float64)
+            mk = np.where(mk > 0, (mk - prev) / 1000.0, np.nan)
+            ar = st[9 * n:].reshape(n, grid)[:n - 1].astype(np.float64)
+            ar = np.where(ar > 0, (ar - prev) / 1000.0, np.nan)
+            out["markers"], out["arrivals"] = mk, ar
+        return out
 
     def stream(self):
         return self.lib.qx_cuda_stream(self.h)
