@@ -177,7 +177,8 @@ def phase_bytes(cfg, position):
     H, Q, KV, I = cfg.hidden, cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.moe_intermediate
     return {
         "qkv": (Q + 2 * KV) * (H // 256) * 136 + 2 * H * 4,
-        "attn": (position + 1) * (2 * KV + 8),
+        "scores": (position + 1) * (KV + 4),
+        "context": (position + 1) * (KV + 4),
         "oproj": H * (Q // 256) * 136,
         "router": cfg.experts * H * 4 + H * 4,
         "gateup": 8 * 2 * I * (H // 256) * 74,
@@ -192,7 +193,7 @@ def kernel_bytes(cfg, name, position):
     return {
         "embed_q4k": (cfg.hidden // 256) * 144,
         "qkv_iq4xs": pb["qkv"],
-        "attn_splitkv": pb["attn"],
+        "attn_splitkv": pb["scores"] + pb["context"],
         "oproj_iq4xs": pb["oproj"] + cfg.q_heads * cfg.head_dim * 4,
         "router_top8": pb["router"],
         "gateup_iq2xs_swiglu": pb["gateup"],

@@ -176,6 +176,24 @@ __device__ __forceinline__ void warp_norm_rope(float* v, const float* nw, const 
     }
 }
 
+// Attention score of one cached INT8 key row (128 dims) against a query head
+// held as doubles: the dot product in dimension order in double, exactly as the
+// reference accumulates it (src/qx_format.c:5127-5150): each product of two
+// floats is exact in double, so the fused multiply-add rounds like the
+// reference's multiply-then-add.  Divided by sqrt(128); non-finite -> 0.
+__device__ __forceinline__ double score_row(const double* qd, const int8_t* kp, float ks, double sqrt_d) {
+    double s = 0.0;
+#pragma unroll 2
+    for (int j = 0; j < 128; j += 16) {
+        const int4 raw = *reinterpret_cast<const int4*>(kp + j);
+        const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) s = fma(qd[j + u], (double)((float)kb[u] * ks), s);
+    }
+    s /= sqrt_d;
+    return isfinite(s) ? s : 0.0;
+}
+
 // Sum of w[0..n) in a fixed order that does not depend on the CTA size:
 // lane l adds w[l], w[l+32], ... then the 32 lane sums are combined by a
 // butterfly.  All threads call; the result is broadcast.

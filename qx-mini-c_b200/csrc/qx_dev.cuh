@@ -183,6 +183,11 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+
 // Copy `bytes` (multiple of 16, both pointers 16-byte aligned) with the whole CTA.
 __device__ __forceinline__ void stage_copy(uint8_t* dst, const uint8_t* src, uint32_t bytes) {
     for (uint32_t c = threadIdx.x; c < bytes / 16u; c += blockDim.x) cp_async16(dst + 16u * c, src + 16u * c);

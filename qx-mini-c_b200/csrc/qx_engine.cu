@@ -667,7 +667,7 @@ QX_API int qx_cuda_phase_trace(qx_cuda_engine* E, uint32_t token, uint32_t posit
     if (!E->mega_grid) { set_err(err, n, "phase trace needs the persistent step kernel"); return 0; }
     if (position >= (uint32_t)E->dm.ctx || token >= (uint32_t)E->dm.vocab) { set_err(err, n, "invalid argument"); return 0; }
     DeviceGuard g(E->device);
-    const uint32_t nst = 2u + 6u * (uint32_t)E->dm.layers + 1u;
+    const uint32_t nst = 2u + (uint32_t)qx::kPhasesPerLayer * (uint32_t)E->dm.layers + 1u;
     const uint32_t total = nst * (9u + (uint32_t)E->mega_grid);
     unsigned long long* tr = nullptr;
     if (!cuda_ok(cudaMalloc((void**)&tr, (size_t)total * 8), "cudaMalloc(trace)", err, n)) return 0;

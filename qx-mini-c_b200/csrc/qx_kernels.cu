@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
     __shared__ double scratch_d[4];
     __shared__ float scratch_f[4];
     __shared__ float qv[128];
+    __shared__ double qd[128];
     __shared__ float kcur[1024];
     __shared__ float vcur[1024];
     __shared__ __align__(16) int8_t k8[1024];
@@ -158,6 +159,8 @@ __global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
         }
         if (i == 0) { d.kscale[slot] = ksc; d.vscale[slot] = vsc; }
     }
+    qd[i] = (double)qv[i];
+    __syncthreads();
     // scores: thread i takes positions i, i+128, ...; dot over d in order, double
     double* sc = d.attn_scores + (size_t)h * ctx;
     const int T = pos + 1;
@@ -167,15 +170,7 @@ __global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
         const size_t st = (size_t)layer * ctx + t;
         const int8_t* kp = t == pos ? k8 + g * D : d.kcache + st * KV + g * D;
         const float ks = t == pos ? ksc : d.kscale[st];
-        double s = 0.0;
-        for (int j = 0; j < D; j += 16) {
-            const int4 raw = *reinterpret_cast<const int4*>(kp + j);
-            const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
-#pragma unroll
-            for (int u = 0; u < 16; ++u) s += (double)qv[j + u] * (double)((float)kb[u] * ks);
-        }
-        s /= sqrt_d;
-        if (!isfinite(s)) s = 0.0;
+        const double s = score_row(qd, kp, ks, sqrt_d);
         sc[t] = s;
         mloc = fmax(mloc, s);
     }

@@ -82,6 +82,9 @@ void launch_topn(const Dev& d, int top_n, int* out_idx, float* out_val, cudaStre
 void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st);
 int head_grid_size(int device, const Dims& m);
 size_t attn_scores_bytes(const Dims& m);
+// Grid barriers per layer of the persistent step kernel: QKV, attention
+// scores, attention context, O projection, router, gate/up, down.
+constexpr int kPhasesPerLayer = 7;
 bool geometry_supported(const Dims& m);
 cudaError_t configure_kernels();
 // Persistent one-launch decode step (qx_mega.cu).

@@ -15,15 +15,20 @@
 
 #include "qx_common.cuh"
 
+#ifndef QX_MEGA_THREADS
+#define QX_MEGA_THREADS 512
+#endif
+
 namespace qx {
 
 struct MegaLayout {                      // byte offsets into dynamic shared memory
     uint32_t xs, xb, sb, tab, part, buf0, buf1, total, buf_bytes;
+    uint32_t norm;                       // offset inside a weight buffer of the RMSNorm vector
 };
 
 namespace {
 
-constexpr int kMT = 256;                 // threads per CTA
+constexpr int kMT = QX_MEGA_THREADS;     // threads per CTA (a multiple of 256)
 constexpr int kMW = kMT / 32;
 constexpr int kMaxTasks = 96;            // (tile, block) tasks per CTA per phase
 constexpr long long kSpinLimit = 1ll << 24;   // ~1e7 L2 round trips: seconds
@@ -45,8 +50,8 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Trace buffer (optional, profiling only): [0, n) exit stamp of each barrier
 // taken by CTA 0 (slot 0 = kernel start), [n, 9n) eight in-phase markers of
 // CTA 0 per barrier epoch, [9n, 9n + n*grid) each CTA's arrival at each
-// barrier; n = 3 + 6 * layers.
-__device__ __forceinline__ size_t trace_n(const Dev& d) { return 3 + 6 * (size_t)d.dm.layers; }
+// barrier; n = 3 + kPhasesPerLayer * layers.
+__device__ __forceinline__ size_t trace_n(const Dev& d) { return 3 + kPhasesPerLayer * (size_t)d.dm.layers; }
 
 __device__ __forceinline__ void mark(const Dev& d, unsigned epoch, int k) {
     if (d.trace && blockIdx.x == 0 && threadIdx.x == 0) d.trace[trace_n(d) + (size_t)(epoch + 1) * 8 + k] = global_ns();
@@ -106,8 +111,11 @@ __device__ __forceinline__ double tile_row(const double* part, int i, int nblk, 
 }
 
 // ---- weight-tile issue per phase -------------------------------------------
-__device__ void issue_qkv(const Dev& d, const LayerW& w, uint8_t* buf) {
+// The QKV and router groups also carry the layer's RMSNorm weights (H floats)
+// to offset `norm` of the buffer, behind every tile of those phases.
+__device__ void issue_qkv(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm) {
     const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
+    stage_copy(buf + norm, reinterpret_cast<const uint8_t*>(w.attn_norm), (uint32_t)H * 4u);
     const uint32_t rb = (uint32_t)(H / 256) * 136u, tb = (uint32_t)kTileRows * rb;
     const int n = (Q + 2 * KV) / kTileRows, mine = my_items(n);
     for (int k = 0; k < mine; ++k) {
@@ -125,8 +133,9 @@ __device__ void issue_oproj(const Dev& d, const LayerW& w, uint8_t* buf) {
     for (int k = 0; k < mine; ++k) stage_copy(buf + (size_t)k * tb, w.wo + (size_t)item_id(k) * tb, tb);
 }
 
-__device__ void issue_router(const Dev& d, const LayerW& w, uint8_t* buf) {
+__device__ void issue_router(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm) {
     const uint32_t rowb = (uint32_t)d.dm.hidden * 4u;
+    stage_copy(buf + norm, reinterpret_cast<const uint8_t*>(w.ffn_norm), rowb);
     const int mine = my_items(d.dm.experts);
     for (int k = 0; k < mine; ++k)
         stage_copy(buf + (size_t)k * rowb, reinterpret_cast<const uint8_t*>(w.router) + (size_t)item_id(k) * rowb, rowb);
@@ -161,46 +170,134 @@ __device__ void issue_head_group(const Dev& d, int grp, uint8_t* buf) {
     stage_copy(buf, d.head + (size_t)grp * stage, stage);
 }
 
-// ---- attention for one query head with 256 threads ----------------------------
+// ---- attention over every CTA ---------------------------------------------
 struct AttnSmem {
     double sd[kMW];
     float sf[kMW];
-    float qv[128];
     float kcur[1024];
     float vcur[1024];
     __align__(16) int8_t k8[1024];
     __align__(16) int8_t v8[1024];
 };
 
-constexpr int kVChunk = 128;   // positions of V staged per pass
+constexpr int kVChunk = 128;   // positions per context pass
+constexpr int kCtxSlices = 4;  // 32-dim slices of a head's context
+constexpr int kQdStride = 130; // doubles per staged query head (conflict-free rows)
 
-// Attention of query head h (all 256 threads).  w_s: >= pos+1 doubles of
-// shared scratch; v_s: kVChunk*128 bytes + kVChunk floats of shared scratch.
-__device__ void attn_head(const Dev& d, const LayerW& w, int layer, int h, int pos, AttnSmem& S, double* w_s,
-                          uint8_t* v_s, unsigned epoch) {
+// Shared-memory staging of the attention phases (the activation region, free
+// while attention runs).  Scores: RoPE row, Q/K norm vectors, this CTA's cached
+// K rows and scales.  Context: softmax weights w_s[ctx], then the item's V
+// slices (32 bytes per position) and V scales.  Rows beyond the capacity are
+// read from global memory.
+struct AttnStage {
+    double* rope;
+    float* qn;
+    float* kn;
+    float* kscl;
+    int8_t* krows;
+    int kcap;
+    double* w_s;
+    int8_t* vrows;
+    float* vscl;
+    int vcap;
+};
+
+__device__ __forceinline__ int attn_cpg(const Dev& d) { return (int)gridDim.x / d.dm.kv_heads; }
+
+__device__ AttnStage attn_stage(const Dev& d, int pos, uint8_t* base, uint32_t bytes) {
+    AttnStage st;
+    const int cpg = attn_cpg(d);
+    st.rope = reinterpret_cast<double*>(base);
+    st.qn = reinterpret_cast<float*>(base + 1024);
+    st.kn = reinterpret_cast<float*>(base + 1536);
+    const int krows = (pos + cpg - 1) / cpg;                  // most positions < pos one CTA scores
+    const int kfit = ((int)bytes - 2048 - 16) / 132;
+    st.kcap = max(0, min(krows, kfit));
+    st.kscl = reinterpret_cast<float*>(base + 2048);
+    st.krows = reinterpret_cast<int8_t*>(base + 2048 + ((st.kcap * 4 + 15) & ~15));
+    const uint32_t ws = (uint32_t)((d.dm.ctx * 8 + 15) & ~15);
+    st.w_s = reinterpret_cast<double*>(base);
+    st.vcap = max(0, min(pos + 1, ((int)bytes - (int)ws) / 36));
+    st.vrows = reinterpret_cast<int8_t*>(base + ws);
+    st.vscl = reinterpret_cast<float*>(base + ws + st.vcap * 32);
+    return st;
+}
+
+__device__ void issue_attn_scores(const Dev& d, const LayerW& w, int layer, int pos, const AttnStage& st) {
+    const int KVH = d.dm.kv_heads, cpg = attn_cpg(d), KV = d.dm.kv_dim(), ctx = d.dm.ctx;
+    if ((int)blockIdx.x >= cpg * KVH) return;
+    const int g = blockIdx.x / cpg, r = blockIdx.x % cpg;
+    stage_copy(reinterpret_cast<uint8_t*>(st.rope), reinterpret_cast<const uint8_t*>(d.rope + (size_t)pos * 128), 1024);
+    stage_copy(reinterpret_cast<uint8_t*>(st.qn), reinterpret_cast<const uint8_t*>(w.q_norm), 512);
+    stage_copy(reinterpret_cast<uint8_t*>(st.kn), reinterpret_cast<const uint8_t*>(w.k_norm), 512);
+    const int rows = r < pos ? min(st.kcap, (pos - r + cpg - 1) / cpg) : 0;
+    for (int c = threadIdx.x; c < rows * 8; c += kMT) {
+        const int mrow = c >> 3, part = c & 7, t = r + mrow * cpg;
+        cp_async16(st.krows + mrow * 128 + part * 16, d.kcache + ((size_t)layer * ctx + t) * KV + g * 128 + part * 16);
+    }
+    for (int mrow = threadIdx.x; mrow < rows; mrow += kMT)
+        cp_async4(st.kscl + mrow, d.kscale + (size_t)layer * ctx + r + mrow * cpg);
+}
+
+__device__ void issue_attn_context(const Dev& d, int layer, int pos, const AttnStage& st) {
+    const int D = 128, SW = D / kCtxSlices, group = d.dm.q_heads / d.dm.kv_heads;
+    const int KV = d.dm.kv_dim(), ctx = d.dm.ctx, item = blockIdx.x;
+    if (item >= d.dm.q_heads * kCtxSlices) return;
+    const int h = item / kCtxSlices, sl = item % kCtxSlices, g = h / group;
+    const int8_t* vb = d.vcache + (size_t)layer * ctx * KV + g * D + sl * SW;
+    for (int c = threadIdx.x; c < st.vcap * 2; c += kMT)
+        cp_async16(st.vrows + (c >> 1) * SW + (c & 1) * 16, vb + (size_t)(c >> 1) * KV + (c & 1) * 16);
+    for (int t = threadIdx.x; t < st.vcap; t += kMT) cp_async4(st.vscl + t, d.vscale + (size_t)layer * ctx + t);
+    (void)pos;
+}
+
+// Scores.  The CTAs form kv_heads groups of G/kv_heads; group g serves the
+// query heads of KV head g, CTA r of the group positions r, r + cpg, ...;
+// thread i scores query head i % group at one of those positions.  Every CTA
+// of a group repeats the per-head Q/K RMSNorm + RoPE of its heads and the INT8
+// quantization of the current K/V (one scale per token over all KV values,
+// src/qx_format.c:4449-4463); CTA 0 appends them to the cache.  qd: shared
+// scratch of group * kQdStride doubles.  The staged group must be the second
+// most recent cp.async group.
+__device__ void attn_scores(const Dev& d, int layer, int pos, AttnSmem& S, double* qd, const AttnStage& st,
+                            unsigned epoch) {
     const int D = 128, KVH = d.dm.kv_heads, group = d.dm.q_heads / KVH;
-    const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx, g = h / group, i = threadIdx.x;
-    const int warp = i >> 5, lane = i & 31;
-    const double* rope = d.rope + (size_t)pos * 128;
+    const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx, i = threadIdx.x;
+    const int warp = i >> 5, lane = i & 31, cpg = attn_cpg(d);
+    if ((int)blockIdx.x >= cpg * KVH) return;
+    const int g = blockIdx.x / cpg, r = blockIdx.x % cpg;
+    float* qf = reinterpret_cast<float*>(qd);             // group * 128 floats, widened below
     for (int j = i; j < KV; j += kMT) {
         S.kcur[j] = d.qkv[Q + j];
         S.vcur[j] = d.qkv[Q + KV + j];
     }
-    if (i < 128) S.qv[i] = d.qkv[h * D + i];
+    for (int j = i; j < group * D; j += kMT) qf[j] = d.qkv[(size_t)g * group * D + j];
+    cp_async_wait<1>();
     __syncthreads();
-    for (int hh = warp; hh <= KVH; hh += kMW) {
-        if (hh < KVH) warp_norm_rope(S.kcur + hh * D, w.k_norm, rope, lane);
-        else warp_norm_rope(S.qv, w.q_norm, rope, lane);
+    for (int hh = warp; hh < KVH + group; hh += kMW) {
+        if (hh < KVH) warp_norm_rope(S.kcur + hh * D, st.kn, st.rope, lane);
+        else warp_norm_rope(qf + (hh - KVH) * D, st.qn, st.rope, lane);
     }
     __syncthreads();
-    mark(d, epoch, 0);
     float ka = 0.f, va = 0.f;
     for (int j = i; j < KV; j += kMT) {
         ka = fmaxf(ka, isfinite(S.kcur[j]) ? fabsf(S.kcur[j]) : 0.f);
         va = fmaxf(va, isfinite(S.vcur[j]) ? fabsf(S.vcur[j]) : 0.f);
     }
+    // widen the query heads (exact) into padded double rows; every float is
+    // read into registers before the first double is written over them
+    float qreg[8];
+    const int nq = group * D;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) qreg[k] = (i + k * kMT < nq) ? qf[i + k * kMT] : 0.f;
     ka = block_max_f(ka, S.sf);
     va = block_max_f(va, S.sf);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int j = i + k * kMT;
+        if (j < nq) qd[(j / D) * kQdStride + j % D] = (double)qreg[k];
+    }
+    mark(d, epoch, 0);
     const float ksc = ka > 0.f ? ka / 127.0f : 1.0f, vsc = va > 0.f ? va / 127.0f : 1.0f;
     for (int j = i; j < KV; j += kMT) {
         const int qk = isfinite(S.kcur[j]) ? (int)lrintf(S.kcur[j] / ksc) : 0;
@@ -209,109 +306,119 @@ __device__ void attn_head(const Dev& d, const LayerW& w, int layer, int h, int p
         S.v8[j] = (int8_t)max(-127, min(127, qq));
     }
     __syncthreads();
-    mark(d, epoch, 1);
     const size_t slot = (size_t)layer * ctx + pos;
-    if (h == 0) {
+    if (blockIdx.x == 0) {
         for (int j = i; j < KV; j += kMT) {
             d.kcache[slot * KV + j] = S.k8[j];
             d.vcache[slot * KV + j] = S.v8[j];
         }
         if (i == 0) { d.kscale[slot] = ksc; d.vscale[slot] = vsc; }
     }
-    // scores (double, dims in order) for positions i, i+256, ...
-    const int T = pos + 1;
+    mark(d, epoch, 1);
+    const int T = pos + 1, per = kMT / group, hj = i % group;
     const double sqrt_d = sqrt((double)D);
-    double mloc = -1.0e300;
-    for (int t = i; t < T; t += kMT) {
-        const size_t st = (size_t)layer * ctx + t;
-        const int8_t* kp = t == pos ? S.k8 + g * D : d.kcache + st * KV + g * D;
-        const float ks = t == pos ? ksc : d.kscale[st];
-        int4 raw[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) raw[j] = reinterpret_cast<const int4*>(kp)[j];
-        double s = 0.0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int8_t* kb = reinterpret_cast<const int8_t*>(&raw[j]);
-#pragma unroll
-            for (int u = 0; u < 16; ++u) s += (double)S.qv[16 * j + u] * (double)((float)kb[u] * ks);
-        }
-        s /= sqrt_d;
-        if (!isfinite(s)) s = 0.0;
-        w_s[t] = s;
-        mloc = fmax(mloc, s);
+    const double* q = qd + hj * kQdStride;
+    double* out = d.attn_scores + (size_t)(g * group + hj) * ctx;
+    for (int mrow = i / group; r + mrow * cpg < T; mrow += per) {
+        const int t = r + mrow * cpg;
+        const size_t stt = (size_t)layer * ctx + t;
+        // pick the row first so the lanes of a warp run one chain together
+        const int8_t* kp = t == pos ? S.k8 + g * D : mrow < st.kcap ? st.krows + mrow * 128 : d.kcache + stt * KV + g * D;
+        const float ks = t == pos ? ksc : mrow < st.kcap ? st.kscl[mrow] : d.kscale[stt];
+        out[t] = score_row(q, kp, ks, sqrt_d);
     }
-    const double mx = block_max_d(mloc, S.sd);
+    __syncthreads();
     mark(d, epoch, 2);
-    for (int t = i; t < T; t += kMT) w_s[t] = exp(w_s[t] - mx);
-    double den = fixed_order_sum(w_s, T, S.sd);
-    if (!isfinite(den) || den <= 0.0) den = 1.0;
-    for (int t = i; t < T; t += kMT) w_s[t] = w_s[t] / den;
-    mark(d, epoch, 3);
-    // context: V of head g staged kVChunk positions at a time; thread i < 128
-    // accumulates dim i over t in order, as the reference does.
-    int8_t* vch = reinterpret_cast<int8_t*>(v_s);
-    float* vsc_s = reinterpret_cast<float*>(v_s + kVChunk * 128);
-    float acc = 0.0f;
-    for (int t0 = 0; t0 < T; t0 += kVChunk) {
-        const int n = min(kVChunk, T - t0);
-        __syncthreads();
-        for (int j = i; j < n * 8; j += kMT) {          // 8 x 16 bytes per position
-            const int t = t0 + j / 8, part = j % 8;
-            const int4* src = t == pos ? reinterpret_cast<const int4*>(S.v8 + g * D)
-                                       : reinterpret_cast<const int4*>(d.vcache + ((size_t)layer * ctx + t) * KV + g * D);
-            reinterpret_cast<int4*>(vch + (size_t)(j / 8) * 128)[part] = src[part];
+}
+
+// Softmax and context.  Item (h, slice) = 32 context dims of query head h:
+// the head's softmax in double (max, exp, fixed-order sum, divide), then the
+// products (float)(w_t * v_t) by every thread into prod, then one warp adds
+// them per dimension in position order in float (src/qx_format.c:5152-5172).
+// prod: kVChunk * 32 floats of shared scratch.  The staged V group must be the
+// most recent cp.async group.
+__device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, float* prod, const AttnStage& st,
+                             unsigned epoch) {
+    const int D = 128, SW = D / kCtxSlices, group = d.dm.q_heads / d.dm.kv_heads;
+    const int KV = d.dm.kv_dim(), ctx = d.dm.ctx, T = pos + 1, i = threadIdx.x;
+    double* w_s = st.w_s;
+    for (int item = blockIdx.x; item < d.dm.q_heads * kCtxSlices; item += gridDim.x) {
+        const int h = item / kCtxSlices, sl = item % kCtxSlices, g = h / group;
+        const bool staged = item == (int)blockIdx.x;
+        const double* sc = d.attn_scores + (size_t)h * ctx;
+        double mloc = -1.0e300;
+        for (int t = i; t < T; t += kMT) {
+            const double s = sc[t];
+            w_s[t] = s;
+            mloc = fmax(mloc, s);
         }
-        for (int j = i; j < n; j += kMT) vsc_s[j] = t0 + j == pos ? vsc : d.vscale[(size_t)layer * ctx + t0 + j];
-        __syncthreads();
-        if (i < 128) {
+        const double mx = block_max_d(mloc, S.sd);
+        for (int t = i; t < T; t += kMT) w_s[t] = exp(w_s[t] - mx);
+        double den = fixed_order_sum(w_s, T, S.sd);
+        if (!isfinite(den) || den <= 0.0) den = 1.0;
+        for (int t = i; t < T; t += kMT) w_s[t] = w_s[t] / den;
+        cp_async_wait<0>();
+        mark(d, epoch, 0);
+        const int8_t* vb = d.vcache + (size_t)layer * ctx * KV + g * D + sl * SW;
+        const float* vs = d.vscale + (size_t)layer * ctx;
+        const int vcap = staged ? st.vcap : 0;
+        float acc = 0.0f;
+        for (int t0 = 0; t0 < T; t0 += kVChunk) {
+            const int n = min(kVChunk, T - t0);
+            __syncthreads();
+            for (int idx = i; idx < n * SW; idx += kMT) {
+                const int t = t0 + idx / SW, dd = idx % SW;
+                const float vv = t < vcap ? (float)st.vrows[t * SW + dd] * st.vscl[t]
+                                          : (float)vb[(size_t)t * KV + dd] * vs[t];
+                prod[idx] = (float)(w_s[t] * (double)vv);
+            }
+            __syncthreads();
+            if (i < SW) {
 #pragma unroll 8
-            for (int j = 0; j < n; ++j) {
-                const float vv = (float)vch[j * 128 + i] * vsc_s[j];
-                acc += (float)(w_s[t0 + j] * (double)vv);
+                for (int tt = 0; tt < n; ++tt) acc += prod[tt * SW + i];
             }
         }
+        if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
+        mark(d, epoch, 1);
+        __syncthreads();
     }
-    if (i < 128) d.ctxv[h * D + i] = acc;
-    __syncthreads();
 }
 
 // Router softmax + top-8 over the logits in global memory (every CTA; the
-// result is identical everywhere).  sel/w in shared memory.
+// result is identical everywhere).  sel/w in shared memory.  The reference
+// picks the 8 largest probabilities one at a time, ties to the lower expert
+// index (src/qx_format.c:5272-5285); the same list comes from ranking every
+// expert by (probability descending, index ascending) in parallel.
 __device__ void top8(const Dev& d, int layer, int* sel, double* wsel, double* probs, double* scratch) {
-    const int E = d.dm.experts, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int E = d.dm.experts, t = threadIdx.x;
     const double lg = t < E ? d.router_logits[t] : -1.0e300;
     const double m = block_max_d(lg, scratch);
     const double ex = t < E ? exp(lg - m) : 0.0;
     const double den = block_sum_d(ex, scratch);
-    probs[t] = t < E ? ex / den : -1.0;
+    const double p = t < E ? ex / den : -1.0;
+    probs[t] = p;
     __syncthreads();
-    if (warp == 0) {
-        for (int k = 0; k < 8; ++k) {
-            double bv = -2.0;
-            int bi = 0x7fffffff;
-            for (int i = lane; i < E; i += 32) {
-                const double p = probs[i];
-                if (p > bv || (p == bv && i < bi)) { bv = p; bi = i; }
-            }
-            for (int o = 16; o; o >>= 1) {
-                const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            if (lane == 0) { sel[k] = bi; wsel[k] = bv; probs[bi] = -1.0; }
-            __syncwarp();
+    if (t < E) {
+        int rank = 0;
+        for (int u = 0; u < E; ++u) {
+            const double q = probs[u];
+            rank += (q > p) | ((q == p) & (u < t));
         }
-        if (lane == 0) {
-            double sum = 0.0;
-            for (int k = 0; k < 8; ++k) sum += wsel[k];
-            if (!(sum > 0.0) || !isfinite(sum)) atomicOr(d.err, kErrRouter);
-            for (int k = 0; k < 8; ++k) {
-                wsel[k] = wsel[k] / sum;
-                if (blockIdx.x == 0) {
-                    d.sel[layer * 8 + k] = sel[k];
-                    d.selw[layer * 8 + k] = (float)wsel[k];
-                }
+        if (rank < 8) {
+            sel[rank] = t;
+            wsel[rank] = p;
+        }
+    }
+    __syncthreads();
+    if (t == 0) {
+        double sum = 0.0;
+        for (int k = 0; k < 8; ++k) sum += wsel[k];
+        if (!(sum > 0.0) || !isfinite(sum)) atomicOr(d.err, kErrRouter);
+        for (int k = 0; k < 8; ++k) {
+            wsel[k] = wsel[k] / sum;
+            if (blockIdx.x == 0) {
+                d.sel[layer * 8 + k] = sel[k];
+                d.selw[layer * 8 + k] = (float)wsel[k];
             }
         }
     }
@@ -323,7 +430,7 @@ __device__ void top8(const Dev& d, int layer, int* sel, double* wsel, double* pr
 __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __restrict__ layers, MegaLayout L) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ double scratch[kMW];
-    __shared__ double probs[256];
+    __shared__ double probs[kMT];
     __shared__ double wsel[8];
     __shared__ int sel[8];
     __shared__ AttnSmem attn;
@@ -349,14 +456,14 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     load_kv_regs(d.tables, K4);
     load_iq_tables(T, d.tables, true, true);
     int qb = 0;
-    issue_qkv(d, layers[0], buf[qb]);
+    issue_qkv(d, layers[0], buf[qb], L.norm);
     cp_async_commit();
     // embedding (every CTA into its own xs; CTA 0 also writes the residual)
     {
         const int nblk = H / 256;
         const uint8_t* row = d.tok_embd + (size_t)tok * (size_t)(nblk * 144);
-        const int t = threadIdx.x, c = t >> 6, l = t & 63;
-        for (int b = 0; b < nblk; ++b) {
+        const int t = threadIdx.x & 255, c = t >> 6, l = t & 63;
+        for (int b = threadIdx.x >> 8; b < nblk; b += kMT / 256) {
             const uint8_t* blk = row + b * 144;
             const float dd = h2f(ld16(blk)), dmin = h2f(ld16(blk + 2));
             const uint8_t* s = blk + 4;
@@ -376,13 +483,16 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         const LayerW& w = layers[layer];
         // ---------------- QKV (weights in buf[qb]) ----------------
         {
+            cp_async_wait<0>();                  // this phase's tiles and norm vector
             if (layer > 0) copy_to_smem(d.x, xs, H);
+            else __syncthreads();
             // attention RMSNorm of xs in place
+            const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
             double ss = 0.0;
             for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
             ss = block_sum_d(ss, scratch);
             const double rms = sqrt(ss / (double)H + 1.0e-6);
-            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * w.attn_norm[i];
+            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
             __syncthreads();
             mark(d, epoch, 0);
             build_xq(xs, H, xb, sb);
@@ -403,10 +513,16 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             grid_sync(bar, epoch, d);
         }
         // ---------------- attention (CTAs 0..Hq-1) ----------------
-        issue_router(d, w, buf[qb]);
+        const AttnStage stg = attn_stage(d, pos, smem + L.xb, L.sb - L.xb);
+        issue_attn_scores(d, w, layer, pos, stg);
         cp_async_commit();
-        for (int h = blockIdx.x; h < m.q_heads; h += gridDim.x)
-            attn_head(d, w, layer, h, pos, attn, reinterpret_cast<double*>(smem + L.xb), smem + L.xs, epoch);
+        issue_router(d, w, buf[qb], L.norm);
+        cp_async_commit();
+        attn_scores(d, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, epoch);
+        grid_sync(bar, epoch, d);
+        issue_attn_context(d, layer, pos, stg);
+        cp_async_commit();
+        attn_context(d, layer, pos, attn, reinterpret_cast<float*>(smem + L.xs), stg, epoch);
         grid_sync(bar, epoch, d);
         // ---------------- O projection (weights in buf[1-qb]) ----------------
         {
@@ -432,12 +548,14 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         }
         // ---------------- router (weights in buf[qb]) ----------------
         {
+            cp_async_wait<0>();                  // router rows and norm vector
             copy_to_smem(d.x, xs, H);
+            const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
             double ss = 0.0;
             for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
             ss = block_sum_d(ss, scratch);
             const double rms = sqrt(ss / (double)H + 1.0e-6);
-            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * w.ffn_norm[i];
+            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
             __syncthreads();
             if (blockIdx.x == 0)
                 for (int i = threadIdx.x; i < H; i += kMT) d.xn[i] = xs[i];
@@ -493,7 +611,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             copy_to_smem(d.hbuf, xs, 8 * I);
             mark(d, epoch, 0);
             build_xq(xs, 8 * I, xb, sb);     // expert e's groups start at e * I / 16 (I % 256 == 0)
-            if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb]);
+            if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm);
             else if ((int)blockIdx.x < m.vocab / (kTileRows * kHeadGroupTiles)) issue_head_group(d, blockIdx.x, buf[1 - qb]);
             cp_async_commit();
             __syncthreads();
@@ -587,6 +705,18 @@ MegaLayout g_layout;
 uint32_t a16u(size_t v) { return (uint32_t)((v + 15) / 16 * 16); }
 }  // namespace
 
+// (tile, block) tasks one CTA runs in its largest dot phase.
+static int mega_max_tasks(const Dims& m, int grid) {
+    auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
+    const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter;
+    const int t[] = {cdiv((Q + 2 * KV) / kTileRows, grid) * (H / 256), cdiv(H / kTileRows, grid) * (Q / 256),
+                     cdiv(8 * (I / kTileRows), grid) * 2 * (H / 256), cdiv(H / kTileRows, grid) * 8 * (I / 256),
+                     kHeadGroupTiles * (H / 256)};
+    int mx = 0;
+    for (int v : t) mx = std::max(mx, v);
+    return mx;
+}
+
 // Shared-memory layout for the model geometry on `grid` CTAs.
 static MegaLayout mega_layout(const Dims& m, int grid) {
     auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
@@ -595,9 +725,9 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     const size_t t_gu = (size_t)kTileRows * (H / 256) * 74, t_dn = (size_t)kTileRows * (I / 256) * 98;
     const size_t t_hd = (size_t)kHeadGroupTiles * kTileRows * (H / 256) * 210;
     size_t bufb = 0;
-    bufb = std::max(bufb, cdiv((Q + 2 * KV) / kTileRows, grid) * t_qkv);
+    bufb = std::max(bufb, cdiv((Q + 2 * KV) / kTileRows, grid) * t_qkv + (size_t)H * 4);
     bufb = std::max(bufb, cdiv(H / kTileRows, grid) * t_o);
-    bufb = std::max(bufb, (size_t)cdiv(m.experts, grid) * H * 4);
+    bufb = std::max(bufb, (size_t)cdiv(m.experts, grid) * H * 4 + (size_t)H * 4);
     bufb = std::max(bufb, cdiv(8 * (I / kTileRows), grid) * 2 * t_gu);
     bufb = std::max(bufb, cdiv(H / kTileRows, grid) * 8 * t_dn);
     bufb = std::max(bufb, t_hd);
@@ -608,25 +738,17 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     L.xb = off; off += a16u(xq_words(XS) * 4);
     L.sb = off; off += a16u((size_t)XS / 256 * 4 + 32);
     L.tab = off; off += a16u(sizeof(IqTab));
-    L.part = off; off += a16u((size_t)kMaxTasks * kTileRows * 8);
+    L.part = off; off += a16u((size_t)mega_max_tasks(m, grid) * kTileRows * 8);
     L.buf_bytes = a16u(bufb);
+    L.norm = L.buf_bytes - (uint32_t)H * 4u;
     L.buf0 = off; off += L.buf_bytes;
     L.buf1 = off; off += L.buf_bytes;
     L.total = off;
     return L;
 }
 
-// Tasks per CTA must fit the partial buffer.
-static bool mega_tasks_fit(const Dims& m, int grid) {
-    auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
-    const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter;
-    const int t[] = {cdiv((Q + 2 * KV) / kTileRows, grid) * (H / 256), cdiv(H / kTileRows, grid) * (Q / 256),
-                     cdiv(8 * (I / kTileRows), grid) * 2 * (H / 256), cdiv(H / kTileRows, grid) * 8 * (I / 256),
-                     kHeadGroupTiles * (H / 256)};
-    for (int v : t)
-        if (v > kMaxTasks) return false;
-    return m.experts <= 256;
-}
+// Tasks per CTA must fit the per-task bookkeeping.
+static bool mega_tasks_fit(const Dims& m, int grid) { return mega_max_tasks(m, grid) <= kMaxTasks && m.experts <= kMT; }
 
 int mega_setup(int device, const Dims& m, int* grid_out) {
     int sms = 0, optin = 0;
@@ -637,6 +759,9 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
     const MegaLayout L = mega_layout(m, sms);
     if (L.total + a.sharedSizeBytes > (size_t)optin || !mega_tasks_fit(m, sms)) return 0;
     if ((size_t)m.ctx * 8 > L.sb - L.xb || (size_t)kVChunk * 132 > L.xb - L.xs) return 0;
+    const int group = m.q_heads / m.kv_heads;
+    if (kMT % group || group * 128 > 8 * kMT || (size_t)group * kQdStride * 8 > L.xb - L.xs || sms < m.kv_heads)
+        return 0;
     if (cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total) != cudaSuccess)
         return 0;
     int per = 0;

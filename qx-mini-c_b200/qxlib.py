@@ -280,7 +280,7 @@ class Engine:
         keys = names.value.decode().split(";")
         return {k: (float(ms[i]), int(ln[i])) for i, k in enumerate(keys[:int(cnt[0])])}
 
-    PHASES = ("qkv", "attn", "oproj", "router", "gateup", "down")
+    PHASES = ("qkv", "scores", "context", "oproj", "router", "gateup", "down")
 
     def phase_trace(self, token, position, detail=False):
         """Run one persistent decode step with %globaltimer stamps at every grid
@@ -289,7 +289,8 @@ class Engine:
         detail=True also "markers" (epochs x 8 in-phase stamps of CTA 0, us from
         the previous barrier exit, NaN where unset) and "arrivals" (epochs x
         CTAs, us from the previous barrier exit)."""
-        n = 3 + 6 * self.layers
+        P = len(self.PHASES)
+        n = 3 + P * self.layers
         cap = n * (9 + 1024)
         st = np.zeros(cap, np.uint64)
         cnt = np.zeros(1, np.uint32)
@@ -297,8 +298,8 @@ class Engine:
         st = st[:int(cnt[0])].astype(np.int64)
         ex = st[:n - 1]
         d = np.diff(ex) / 1000.0
-        out = {name: d[i:6 * self.layers:6].tolist() for i, name in enumerate(self.PHASES)}
-        out["head"] = float(d[6 * self.layers:].sum())
+        out = {name: d[i:P * self.layers:P].tolist() for i, name in enumerate(self.PHASES)}
+        out["head"] = float(d[P * self.layers:].sum())
         out["total"] = float(d.sum())
         if detail:
             grid = (len(st) - 9 * n) // n

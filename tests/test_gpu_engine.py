@@ -212,6 +212,16 @@ def test_config3_attention_with_history(full, port, case_index):
     assert_close(res, case["residual"], what="residual ctx=%d" % (P + 1))
 
 
+def test_full_model_runs_the_one_launch_step(full):
+    """The full geometry fits the persistent kernel's shared-memory layout: a
+    decode step is one launch, not the per-stage sequence."""
+    full.reset()
+    p0 = full.profile()["kernel_launches"]
+    full.decode_step(W.START_TOKEN, 0)
+    assert full.profile()["kernel_launches"] - p0 == 1
+    assert full.phase_trace(W.START_TOKEN, 1)["total"] > 0
+
+
 def test_config4_first_steps_match_reference(full):
     g = gold("golden_full.json")["decode"]
     full.reset()
