@@ -203,6 +203,23 @@ def kernel_bytes(cfg, name, position):
     }.get(name, 0)
 
 
+def ncu_traffic(kernel, algorithmic_bytes):
+    """DRAM bytes per launch from the committed ncu summary of `kernel`: the
+    summary records dram__bytes_read.sum + dram__bytes_write.sum over the
+    algorithmic bytes of the captured (smaller) launch, in a line
+    `traffic_ratio <kernel> <ratio>`; traffic grows with the weights streamed,
+    so the full launch's traffic is that ratio times its algorithmic bytes."""
+    for name in sorted(os.listdir(os.path.join(ROOT, "profiles"))) if os.path.isdir(os.path.join(ROOT, "profiles")) else []:
+        if not name.endswith(".txt"):
+            continue
+        with open(os.path.join(ROOT, "profiles", name)) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 3 and parts[0] == "traffic_ratio" and parts[1] == kernel:
+                    return float(parts[2]) * algorithmic_bytes
+    return None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -298,13 +315,7 @@ def main():
     dom_bytes = kernel_bytes(cfg, dom, tpos + (tn - 1) / 2.0)
     peak, peak_kind = peaks()
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
-    if os.path.exists(tpath):
-        try:
-            traffic = json.load(open(tpath)).get(dom)
-        except Exception:
-            traffic = None
+    traffic = ncu_traffic(dom, dom_bytes)
     # per-phase breakdown of the persistent step (grid-barrier timestamps)
     phases = None
     if dom == "decode_step_persistent":

@@ -259,26 +259,39 @@ __device__ void issue_attn_context(const Dev& d, int layer, int pos, const AttnS
 // src/qx_format.c:4449-4463); CTA 0 appends them to the cache.  qd: shared
 // scratch of group * kQdStride doubles.  The staged group must be the second
 // most recent cp.async group.
-__device__ void attn_scores(const Dev& d, int layer, int pos, AttnSmem& S, double* qd, const AttnStage& st,
-                            unsigned epoch) {
+__device__ void attn_scores(const Dev& d, const LayerW& w, int layer, int pos, AttnSmem& S, double* qd,
+                            const AttnStage& st, uint8_t* router_buf, uint32_t norm, unsigned epoch) {
     const int D = 128, KVH = d.dm.kv_heads, group = d.dm.q_heads / KVH;
     const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx, i = threadIdx.x;
     const int warp = i >> 5, lane = i & 31, cpg = attn_cpg(d);
-    if ((int)blockIdx.x >= cpg * KVH) return;
-    const int g = blockIdx.x / cpg, r = blockIdx.x % cpg;
+    const bool active = (int)blockIdx.x < cpg * KVH;
+    const int g = blockIdx.x / max(cpg, 1), r = blockIdx.x % max(cpg, 1);
     float* qf = reinterpret_cast<float*>(qd);             // group * 128 floats, widened below
-    for (int j = i; j < KV; j += kMT) {
-        S.kcur[j] = d.qkv[Q + j];
-        S.vcur[j] = d.qkv[Q + KV + j];
+    if (active) {
+        for (int j = i; j < KV; j += kMT) {
+            S.kcur[j] = d.qkv[Q + j];
+            S.vcur[j] = d.qkv[Q + KV + j];
+        }
+        for (int j = i; j < group * D; j += kMT) qf[j] = d.qkv[(size_t)g * group * D + j];
     }
-    for (int j = i; j < group * D; j += kMT) qf[j] = d.qkv[(size_t)g * group * D + j];
+    __syncthreads();
+    mark(d, epoch, 3);
+    // the staging and router copies start once the phase's inputs are in, so
+    // they do not queue ahead of those loads
+    issue_attn_scores(d, w, layer, pos, st);
+    cp_async_commit();
+    issue_router(d, w, router_buf, norm);
+    cp_async_commit();
+    if (!active) return;
     cp_async_wait<1>();
     __syncthreads();
+    mark(d, epoch, 4);
     for (int hh = warp; hh < KVH + group; hh += kMW) {
         if (hh < KVH) warp_norm_rope(S.kcur + hh * D, st.kn, st.rope, lane);
         else warp_norm_rope(qf + (hh - KVH) * D, st.qn, st.rope, lane);
     }
     __syncthreads();
+    mark(d, epoch, 5);
     float ka = 0.f, va = 0.f;
     for (int j = i; j < KV; j += kMT) {
         ka = fmaxf(ka, isfinite(S.kcur[j]) ? fabsf(S.kcur[j]) : 0.f);
@@ -353,10 +366,18 @@ __device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, floa
             mloc = fmax(mloc, s);
         }
         const double mx = block_max_d(mloc, S.sd);
+        mark(d, epoch, 3);
+        if (staged) {                      // V slices start once the scores are in
+            issue_attn_context(d, layer, pos, st);
+            cp_async_commit();
+        }
         for (int t = i; t < T; t += kMT) w_s[t] = exp(w_s[t] - mx);
         double den = fixed_order_sum(w_s, T, S.sd);
+        mark(d, epoch, 4);
         if (!isfinite(den) || den <= 0.0) den = 1.0;
         for (int t = i; t < T; t += kMT) w_s[t] = w_s[t] / den;
+        __syncthreads();
+        mark(d, epoch, 5);
         cp_async_wait<0>();
         mark(d, epoch, 0);
         const int8_t* vb = d.vcache + (size_t)layer * ctx * KV + g * D + sl * SW;
@@ -514,14 +535,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         }
         // ---------------- attention (CTAs 0..Hq-1) ----------------
         const AttnStage stg = attn_stage(d, pos, smem + L.xb, L.sb - L.xb);
-        issue_attn_scores(d, w, layer, pos, stg);
-        cp_async_commit();
-        issue_router(d, w, buf[qb], L.norm);
-        cp_async_commit();
-        attn_scores(d, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, epoch);
+        attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, buf[qb], L.norm, epoch);
         grid_sync(bar, epoch, d);
-        issue_attn_context(d, layer, pos, stg);
-        cp_async_commit();
         attn_context(d, layer, pos, attn, reinterpret_cast<float*>(smem + L.xs), stg, epoch);
         grid_sync(bar, epoch, d);
         // ---------------- O projection (weights in buf[1-qb]) ----------------
