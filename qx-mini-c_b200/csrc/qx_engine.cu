@@ -301,8 +301,13 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     add((void**)&d.selw_d, 8 * 8);
     add((void**)&d.hbuf, 8 * I * 4);
     add((void**)&d.logits, (size_t)dm.vocab * 4);
-    add((void**)&d.best_val, (size_t)d.head_grid * 4);
-    add((void**)&d.best_idx, (size_t)d.head_grid * 4);
+    // argmax partials: one per CTA of the per-stage head or of the persistent
+    // step kernel (one CTA per SM), whichever is larger
+    int sm_count = 0;
+    cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    const size_t partials = (size_t)std::max(d.head_grid, sm_count);
+    add((void**)&d.best_val, partials * sizeof(double));
+    add((void**)&d.best_idx, partials * 4);
     add((void**)&d.counters, qx::kCntTotal * 4);
     add((void**)&d.token, 4);
     add((void**)&d.pos, 4);

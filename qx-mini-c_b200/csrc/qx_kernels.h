@@ -55,7 +55,7 @@ struct Dev {
     double* selw_d;              // [8] weights of the current layer (double)
     float* hbuf;                 // SwiGLU outputs [8][I]
     float* logits;               // [V]
-    float* best_val;             // per-CTA argmax partials
+    double* best_val;            // per-CTA argmax partials (double logits, as the reference compares)
     int* best_idx;
     unsigned* counters;          // ticket counters for last-CTA reductions
     int* token;                  // current input token (device scalar)
