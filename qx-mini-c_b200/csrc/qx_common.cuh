@@ -194,6 +194,21 @@ __device__ __forceinline__ double score_row(const double* qd, const int8_t* kp, 
     return isfinite(s) ? s : 0.0;
 }
 
+// score_row over a key row whose 16-byte chunk j is stored at chunk j ^ key
+// (a shared-memory swizzle; key 0 = plain row).  Same arithmetic and order.
+__device__ __forceinline__ double score_row_sw(const double* qd, const int8_t* kp, int key, float ks, double sqrt_d) {
+    double s = 0.0;
+#pragma unroll 2
+    for (int j = 0; j < 8; ++j) {
+        const int4 raw = *reinterpret_cast<const int4*>(kp + 16 * (j ^ key));
+        const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) s = fma(qd[16 * j + u], (double)((float)kb[u] * ks), s);
+    }
+    s /= sqrt_d;
+    return isfinite(s) ? s : 0.0;
+}
+
 // Sum of w[0..n) in a fixed order that does not depend on the CTA size:
 // lane l adds w[l], w[l+32], ... then the 32 lane sums are combined by a
 // butterfly.  All threads call; the result is broadcast.

@@ -31,7 +31,8 @@ namespace {
 constexpr int kMT = QX_MEGA_THREADS;     // threads per CTA (a multiple of 256)
 constexpr int kMW = kMT / 32;
 constexpr int kMaxTasks = 96;            // (tile, block) tasks per CTA per phase
-constexpr long long kSpinLimit = 1ll << 24;   // ~1e7 L2 round trips: seconds
+constexpr long long kSpinLimit = 1ll << 26;             // polls of one barrier wait, at most
+constexpr unsigned long long kBarrierTimeoutNs = 2000000000ull;   // 2 s; a healthy wait is microseconds
 enum { QXH_IQ4_XS_F = 23, QXH_IQ2_XS_F = 17, QXH_IQ3_XXS_F = 18, QXH_Q6_K_F = 14 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -57,23 +58,42 @@ __device__ __forceinline__ void mark(const Dev& d, unsigned epoch, int k) {
     if (d.trace && blockIdx.x == 0 && threadIdx.x == 0) d.trace[trace_n(d) + (size_t)(epoch + 1) * 8 + k] = global_ns();
 }
 
-__device__ __forceinline__ void grid_sync(unsigned* bar, unsigned& epoch, const Dev& d) {
+// `epoch` numbers phases (trace slots); `nsync` counts the barriers actually
+// entered, which sets the arrival target.  A CTA waits at most
+// kBarrierTimeoutNs (or kSpinLimit polls); then it sets kErrTimeout and
+// returns, and every later barrier returns at once when it sees that flag, so
+// a broken step ends quickly with an error the host reports.
+__device__ __forceinline__ void grid_sync(unsigned* bar, unsigned& epoch, unsigned& nsync, const Dev& d) {
     int* err = d.err;
     unsigned long long* trace = d.trace;
     __syncthreads();
     epoch += 1;
+    nsync += 1;
     if (threadIdx.x == 0) {
         if (trace) trace[9 * trace_n(d) + (size_t)epoch * gridDim.x + blockIdx.x] = global_ns();
         // the CTA's writes are ordered before this release by the bar.sync above
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
-        const unsigned target = epoch * gridDim.x;
-        long long it = 0;
-        while (ld_acquire(bar) < target) {
-            if (++it > kSpinLimit) { atomicOr(err, kErrTimeout); break; }
+        const unsigned target = nsync * gridDim.x;
+        const unsigned long long t0 = global_ns();
+        for (long long it = 0; ld_acquire(bar) < target; ++it) {
+            if ((it & 63) == 63) {
+                if (*reinterpret_cast<volatile int*>(err) & kErrTimeout) break;
+                if (global_ns() - t0 > kBarrierTimeoutNs || it > kSpinLimit) {
+                    atomicOr(err, kErrTimeout);
+                    break;
+                }
+            }
         }
         if (trace && blockIdx.x == 0) trace[epoch] = global_ns();
     }
     __syncthreads();
+}
+
+// Advance the barrier numbering without synchronising (a phase that is
+// merged into the previous one); the trace records a zero-length phase.
+__device__ __forceinline__ void skip_sync(unsigned& epoch, const Dev& d) {
+    epoch += 1;
+    if (d.trace && blockIdx.x == 0 && threadIdx.x == 0) d.trace[epoch] = global_ns();
 }
 
 // Items of a phase owned by this CTA: blockIdx.x, blockIdx.x + G, ...
@@ -405,6 +425,166 @@ __device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, floa
     }
 }
 
+// ---- single-phase attention (history fits in shared memory) ----------------
+// Item (h, slice) computes every score of query head h itself (the 4 slice
+// CTAs of a head repeat the same exact arithmetic), then its 32 context dims;
+// no scores round trip through global memory and one grid barrier fewer.
+// Staged at the end of the QKV phase into the activation region: RoPE row,
+// Q/K norm vectors, K rows of the item's KV head (16-byte chunk j of row t at
+// chunk j ^ (t & 7), so lanes scoring consecutive positions read different
+// banks), K scales, the item's 32-byte V slices and V scales.
+struct FusedStage {
+    double* rope;
+    float* qn;
+    float* kn;
+    double* qd;
+    double* w_s;
+    float* kscl;
+    float* vscl;
+    int8_t* krows;
+    int8_t* vrows;
+};
+
+constexpr uint32_t kFusedFixed = 1024 + 512 + 512 + 1040;        // rope, norms, qd (bytes, 16-aligned)
+constexpr uint32_t kFusedPerPos = 8 + 4 + 4 + 128 + 32;          // w_s, scales, K row, V slice
+
+__device__ __forceinline__ int fused_cap(uint32_t bytes) {
+    return bytes > kFusedFixed + 64 ? min(1024, (int)((bytes - kFusedFixed - 64) / kFusedPerPos)) : 0;
+}
+
+__device__ FusedStage fused_stage(uint8_t* base, uint32_t bytes) {
+    const int cap = fused_cap(bytes);
+    FusedStage f;
+    f.rope = reinterpret_cast<double*>(base);
+    f.qn = reinterpret_cast<float*>(base + 1024);
+    f.kn = reinterpret_cast<float*>(base + 1536);
+    f.qd = reinterpret_cast<double*>(base + 2048);
+    uint8_t* p = base + kFusedFixed;
+    f.w_s = reinterpret_cast<double*>(p);
+    p += ((size_t)cap * 8 + 15) & ~(size_t)15;
+    f.kscl = reinterpret_cast<float*>(p);
+    p += ((size_t)cap * 4 + 15) & ~(size_t)15;
+    f.vscl = reinterpret_cast<float*>(p);
+    p += ((size_t)cap * 4 + 15) & ~(size_t)15;
+    f.krows = reinterpret_cast<int8_t*>(p);
+    p += (size_t)cap * 128;
+    f.vrows = reinterpret_cast<int8_t*>(p);
+    return f;
+}
+
+// Copies for the fused phase of `layer` at `pos` (history rows t < pos).
+__device__ void issue_attn_fused(const Dev& d, const LayerW& w, int layer, int pos, const FusedStage& f) {
+    const int D = 128, SW = D / kCtxSlices, group = d.dm.q_heads / d.dm.kv_heads;
+    const int KV = d.dm.kv_dim(), ctx = d.dm.ctx, item = blockIdx.x;
+    if (item >= d.dm.q_heads * kCtxSlices) return;
+    const int h = item / kCtxSlices, sl = item % kCtxSlices, g = h / group;
+    stage_copy(reinterpret_cast<uint8_t*>(f.rope), reinterpret_cast<const uint8_t*>(d.rope + (size_t)pos * 128), 1024);
+    stage_copy(reinterpret_cast<uint8_t*>(f.qn), reinterpret_cast<const uint8_t*>(w.q_norm), 512);
+    stage_copy(reinterpret_cast<uint8_t*>(f.kn), reinterpret_cast<const uint8_t*>(w.k_norm), 512);
+    const int8_t* kb = d.kcache + (size_t)layer * ctx * KV + g * D;
+    const int8_t* vb = d.vcache + (size_t)layer * ctx * KV + g * D + sl * SW;
+    for (int c = threadIdx.x; c < pos * 8; c += kMT) {
+        const int t = c >> 3, j = c & 7;
+        cp_async16(f.krows + t * 128 + 16 * (j ^ (t & 7)), kb + (size_t)t * KV + 16 * j);
+    }
+    for (int c = threadIdx.x; c < pos * 2; c += kMT)
+        cp_async16(f.vrows + (c >> 1) * SW + (c & 1) * 16, vb + (size_t)(c >> 1) * KV + (c & 1) * 16);
+    for (int t = threadIdx.x; t < pos; t += kMT) {
+        cp_async4(f.kscl + t, d.kscale + (size_t)layer * ctx + t);
+        cp_async4(f.vscl + t, d.vscale + (size_t)layer * ctx + t);
+    }
+}
+
+// The fused phase.  The staged group must be the second most recent
+// cp.async group once the router copies are issued here.
+__device__ void attn_fused(const Dev& d, const LayerW& w, int layer, int pos, AttnSmem& S, const FusedStage& f,
+                           float* prod, uint8_t* router_buf, uint32_t norm, unsigned epoch) {
+    const int D = 128, SW = D / kCtxSlices, KVH = d.dm.kv_heads, group = d.dm.q_heads / KVH;
+    const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx, i = threadIdx.x;
+    const int warp = i >> 5, lane = i & 31, item = blockIdx.x, T = pos + 1;
+    const bool active = item < d.dm.q_heads * kCtxSlices;
+    const int h = item / kCtxSlices, sl = item % kCtxSlices, g = h / group;
+    float* qf = reinterpret_cast<float*>(prod);                   // 128 floats of scratch
+    if (active) {
+        for (int j = i; j < KV; j += kMT) {
+            S.kcur[j] = d.qkv[Q + j];
+            S.vcur[j] = d.qkv[Q + KV + j];
+        }
+        if (i < D) qf[i] = d.qkv[h * D + i];
+    }
+    __syncthreads();
+    issue_router(d, w, router_buf, norm);
+    cp_async_commit();
+    if (!active) return;
+    cp_async_wait<1>();
+    __syncthreads();
+    mark(d, epoch, 3);
+    if (warp <= KVH) {
+        if (warp < KVH) warp_norm_rope(S.kcur + warp * D, f.kn, f.rope, lane);
+        else warp_norm_rope(qf, f.qn, f.rope, lane);
+    }
+    __syncthreads();
+    float ka = 0.f, va = 0.f;
+    for (int j = i; j < KV; j += kMT) {
+        ka = fmaxf(ka, isfinite(S.kcur[j]) ? fabsf(S.kcur[j]) : 0.f);
+        va = fmaxf(va, isfinite(S.vcur[j]) ? fabsf(S.vcur[j]) : 0.f);
+    }
+    if (i < D) f.qd[i] = (double)qf[i];
+    ka = block_max_f(ka, S.sf);
+    va = block_max_f(va, S.sf);
+    const float ksc = ka > 0.f ? ka / 127.0f : 1.0f, vsc = va > 0.f ? va / 127.0f : 1.0f;
+    for (int j = i; j < KV; j += kMT) {
+        const int qk = isfinite(S.kcur[j]) ? (int)lrintf(S.kcur[j] / ksc) : 0;
+        const int qq = isfinite(S.vcur[j]) ? (int)lrintf(S.vcur[j] / vsc) : 0;
+        S.k8[j] = (int8_t)max(-127, min(127, qk));
+        S.v8[j] = (int8_t)max(-127, min(127, qq));
+    }
+    __syncthreads();
+    if (item == 0) {
+        const size_t slot = (size_t)layer * ctx + pos;
+        for (int j = i; j < KV; j += kMT) {
+            d.kcache[slot * KV + j] = S.k8[j];
+            d.vcache[slot * KV + j] = S.v8[j];
+        }
+        if (i == 0) { d.kscale[slot] = ksc; d.vscale[slot] = vsc; }
+    }
+    mark(d, epoch, 0);
+    // scores of every position (the current one from the fresh INT8 row)
+    const double sqrt_d = sqrt((double)D);
+    double mloc = -1.0e300;
+    for (int t = i; t < T; t += kMT) {
+        const bool cur = t == pos;
+        const double s = score_row_sw(f.qd, cur ? S.k8 + g * D : f.krows + t * 128, cur ? 0 : (t & 7),
+                                      cur ? ksc : f.kscl[t], sqrt_d);
+        f.w_s[t] = s;
+        mloc = fmax(mloc, s);
+    }
+    const double mx = block_max_d(mloc, S.sd);
+    mark(d, epoch, 1);
+    for (int t = i; t < T; t += kMT) f.w_s[t] = exp(f.w_s[t] - mx);
+    double den = fixed_order_sum(f.w_s, T, S.sd);
+    if (!isfinite(den) || den <= 0.0) den = 1.0;
+    for (int t = i; t < T; t += kMT) f.w_s[t] = f.w_s[t] / den;
+    mark(d, epoch, 2);
+    float acc = 0.0f;
+    for (int t0 = 0; t0 < T; t0 += kVChunk) {
+        const int n = min(kVChunk, T - t0);
+        __syncthreads();
+        for (int idx = i; idx < n * SW; idx += kMT) {
+            const int t = t0 + idx / SW, dd = idx % SW;
+            const float vv = t == pos ? (float)S.v8[g * D + sl * SW + dd] * vsc : (float)f.vrows[t * SW + dd] * f.vscl[t];
+            prod[idx] = (float)(f.w_s[t] * (double)vv);
+        }
+        __syncthreads();
+        if (i < SW) {
+#pragma unroll 8
+            for (int tt = 0; tt < n; ++tt) acc += prod[tt * SW + i];
+        }
+    }
+    if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
+    __syncthreads();
+}
+
 // Router softmax + top-8 over the logits in global memory (every CTA; the
 // result is identical everywhere).  sel/w in shared memory.  The reference
 // picks the 8 largest probabilities one at a time, ties to the lower expert
@@ -417,13 +597,18 @@ __device__ void top8(const Dev& d, int layer, int* sel, double* wsel, double* pr
     const double ex = t < E ? exp(lg - m) : 0.0;
     const double den = block_sum_d(ex, scratch);
     const double p = t < E ? ex / den : -1.0;
-    probs[t] = p;
+    // probabilities are >= 0, so their bit patterns order like the values:
+    // rank with integer compares (a NaN makes the weight sum NaN, which is
+    // reported as an error whatever the order)
+    long long* pb = reinterpret_cast<long long*>(probs);
+    const long long key = __double_as_longlong(p);
+    pb[t] = key;
     __syncthreads();
     if (t < E) {
         int rank = 0;
         for (int u = 0; u < E; ++u) {
-            const double q = probs[u];
-            rank += (q > p) | ((q == p) & (u < t));
+            const long long q = pb[u];
+            rank += (q > key) | ((q == key) & (u < t));
         }
         if (rank < 8) {
             sel[rank] = t;
@@ -431,16 +616,16 @@ __device__ void top8(const Dev& d, int layer, int* sel, double* wsel, double* pr
         }
     }
     __syncthreads();
-    if (t == 0) {
+    if (t < 8) {                                  // same sum order on each of the 8 threads
         double sum = 0.0;
         for (int k = 0; k < 8; ++k) sum += wsel[k];
-        if (!(sum > 0.0) || !isfinite(sum)) atomicOr(d.err, kErrRouter);
-        for (int k = 0; k < 8; ++k) {
-            wsel[k] = wsel[k] / sum;
-            if (blockIdx.x == 0) {
-                d.sel[layer * 8 + k] = sel[k];
-                d.selw[layer * 8 + k] = (float)wsel[k];
-            }
+        if (t == 0 && (!(sum > 0.0) || !isfinite(sum))) atomicOr(d.err, kErrRouter);
+        const double wk = wsel[t] / sum;
+        __syncwarp(0xffu);
+        wsel[t] = wk;
+        if (blockIdx.x == 0) {
+            d.sel[layer * 8 + t] = sel[t];
+            d.selw[layer * 8 + t] = (float)wk;
         }
     }
     __syncthreads();
@@ -465,7 +650,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     uint8_t* buf[2] = {smem + L.buf0, smem + L.buf1};
     const Dims& m = d.dm;
     const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter, E = m.experts;
-    unsigned epoch = 0;
+    unsigned epoch = 0, nsync = 0;
     unsigned* bar = d.counters + kCntBarrier;
     const int tok = *d.token, pos = *d.pos;
     if (tok < 0 || tok >= m.vocab || pos < 0 || pos >= m.ctx) {
@@ -476,6 +661,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     uint32_t K4[4];
     load_kv_regs(d.tables, K4);
     load_iq_tables(T, d.tables, true, true);
+    // attention in one phase when the whole history of a head fits in shared memory
+    const bool fused = pos + 1 <= fused_cap(L.sb - L.xb);
+    const FusedStage fz = fused_stage(smem + L.xb, L.sb - L.xb);
     int qb = 0;
     issue_qkv(d, layers[0], buf[qb], L.norm);
     cp_async_commit();
@@ -531,14 +719,22 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT)
                 d.qkv[item_id(r / kTileRows) * kTileRows + r % kTileRows] =
                     finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
-            grid_sync(bar, epoch, d);
+            if (fused) issue_attn_fused(d, w, layer, pos, fz);   // the activation region is free again
+            cp_async_commit();
+            grid_sync(bar, epoch, nsync, d);
         }
         // ---------------- attention (CTAs 0..Hq-1) ----------------
-        const AttnStage stg = attn_stage(d, pos, smem + L.xb, L.sb - L.xb);
-        attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, buf[qb], L.norm, epoch);
-        grid_sync(bar, epoch, d);
-        attn_context(d, layer, pos, attn, reinterpret_cast<float*>(smem + L.xs), stg, epoch);
-        grid_sync(bar, epoch, d);
+        if (fused) {
+            attn_fused(d, w, layer, pos, attn, fz, reinterpret_cast<float*>(smem + L.xs), buf[qb], L.norm, epoch);
+            skip_sync(epoch, d);
+            grid_sync(bar, epoch, nsync, d);
+        } else {
+            const AttnStage stg = attn_stage(d, pos, smem + L.xb, L.sb - L.xb);
+            attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, buf[qb], L.norm, epoch);
+            grid_sync(bar, epoch, nsync, d);
+            attn_context(d, layer, pos, attn, reinterpret_cast<float*>(smem + L.xs), stg, epoch);
+            grid_sync(bar, epoch, nsync, d);
+        }
         // ---------------- O projection (weights in buf[1-qb]) ----------------
         {
             copy_to_smem(d.ctxv, xs, Q);
@@ -559,7 +755,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 d.attn_out[row] = o;
                 d.x[row] = d.x[row] + o;
             }
-            grid_sync(bar, epoch, d);
+            grid_sync(bar, epoch, nsync, d);
         }
         // ---------------- router (weights in buf[qb]) ----------------
         {
@@ -591,7 +787,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 acc = block_sum_d(acc, scratch);
                 if (threadIdx.x == 0) d.router_logits[item_id(k)] = acc;
             }
-            grid_sync(bar, epoch, d);
+            grid_sync(bar, epoch, nsync, d);
         }
         // ---------------- top-8 + gate/up (weights in buf[1-qb]) ----------------
         {
@@ -619,7 +815,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const double gd = (double)gv;
                 d.hbuf[(it / tpe) * I + (it % tpe) * kTileRows + rr] = (float)(gd / (1.0 + exp(-gd)) * (double)uv);
             }
-            grid_sync(bar, epoch, d);
+            grid_sync(bar, epoch, nsync, d);
         }
         // ---------------- down (weights in buf[qb]) ----------------
         {
@@ -648,7 +844,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 d.moe_out[row] = moe;
                 d.x[row] = d.x[row] + moe;
             }
-            grid_sync(bar, epoch, d);
+            grid_sync(bar, epoch, nsync, d);
         }
         qb = 1 - qb;
     }
@@ -699,7 +895,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             d.best_val[blockIdx.x] = bv;
             d.best_idx[blockIdx.x] = bi;
         }
-        grid_sync(bar, epoch, d);
+        grid_sync(bar, epoch, nsync, d);
         if (blockIdx.x == 0 && threadIdx.x == 0) {
             double v = d.best_val[0];
             int i = d.best_idx[0];
