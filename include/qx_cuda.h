@@ -60,10 +60,10 @@ typedef struct qx_cuda_options {
     uint32_t ctx_tokens;       /* persistent INT8 KV capacity, 1..65536 (reference caps at 4096) */
     uint32_t flags;            /* QX_CUDA_* */
     uint32_t ep_rank;          /* expert-parallel rank (0 when ep_world <= 1) */
-    uint32_t ep_world;         /* expert-parallel world size; 0 or 1 = single GPU */
+    uint32_t ep_world;         /* expert-parallel world size, 1..8; 0 or 1 = single GPU */
     uint32_t reserved;
     void *stream;              /* cudaStream_t to run on; NULL = engine-owned stream */
-    void *nccl_comm;           /* ncclComm_t spanning ep_world ranks (ep_world > 1) */
+    void *nccl_comm;           /* reserved (must be NULL): ranks exchange through mapped peer memory */
 } qx_cuda_options;
 
 /* Counters for the reference's `cuda_profile` block (src/qx_format.c:6683). */
@@ -201,6 +201,42 @@ int qx_cuda_time_kernels(qx_cuda_engine *engine, uint32_t token, uint32_t positi
  * A profiling aid (it allocates a buffer); not part of the reference API. */
 int qx_cuda_phase_trace(qx_cuda_engine *engine, uint32_t token, uint32_t position, uint64_t *stamps_ns,
                         uint32_t max_stamps, uint32_t *count, char *err, uint64_t err_len);
+
+/* ---- expert parallelism (one process per GPU, ranks on one node) ---------
+ *
+ * The reference decodes on one CPU thread; this is the B200 engine's own
+ * partitioning of qx_apply_real_moe_layer (src/qx_format.c:5198-5310) and of
+ * the head (:3554-3738) over ep_world GPUs, created with options.ep_world > 1
+ * and options.ep_rank.  Every rank holds the whole model and runs attention
+ * and the router itself (identical results on every rank); rank r computes
+ * the top-8 slots whose expert lies in its share (qx_cuda_ep_partition) and
+ * stores their weighted outputs into every rank's exchange buffer over NVLink
+ * (plain peer stores + release flags, no collective library on the data
+ * path); every rank then adds the 8 slots in rank order, exactly as one GPU
+ * does.  The head is split by vocabulary rows; ranks exchange (max logit,
+ * index) and take the lowest index among equal maxima.  Tokens, experts and
+ * the final residual equal the single-GPU engine's; decode_step's logits hold
+ * only this rank's vocabulary rows.
+ *
+ * Set-up: every rank calls qx_cuda_ep_handle, the caller gathers the handles
+ * of all ranks in rank order (any host transport), and every rank calls
+ * qx_cuda_ep_connect once.  Until then decode calls fail.  All ranks must run
+ * the same decode calls in the same order (their steps wait on each other, with
+ * a bounded wait that fails the step with "device grid barrier timed out"). */
+
+/* The split (host-only, no device needed): rank `rank` of `world` computes
+ * experts [out[0], out[1]) and head rows [out[2], out[3]) (vocab a multiple of
+ * 32).  Returns 0 on invalid arguments. */
+int qx_cuda_ep_partition(uint32_t experts, uint32_t vocab, uint32_t world, uint32_t rank, uint32_t out[4]);
+
+/* Write this rank's exchange-buffer handle (a cudaIpcMemHandle_t, 64 bytes)
+ * into handle[handle_size] (handle_size >= 64). */
+int qx_cuda_ep_handle(qx_cuda_engine *engine, void *handle, uint64_t handle_size, char *err, uint64_t err_len);
+
+/* Map the peers: handles holds `world` handles of handle_size bytes each,
+ * in rank order (this rank's own entry is ignored). */
+int qx_cuda_ep_connect(qx_cuda_engine *engine, const void *handles, uint64_t handle_size, uint32_t world,
+                       char *err, uint64_t err_len);
 
 /* The engine's CUDA stream (cudaStream_t) for callers that time with events. */
 void *qx_cuda_stream(const qx_cuda_engine *engine);

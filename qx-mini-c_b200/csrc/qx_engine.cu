@@ -56,6 +56,11 @@ struct qx_cuda_engine {
     LayerW* layers_dev = nullptr;   // device copy of the layer table (persistent step kernel)
     int mega_grid = 0;               // 0 = per-stage kernels
     int* d_topi = nullptr;
+    // expert parallelism
+    uint8_t* ep_xchg = nullptr;      // this rank's exchange buffer (its own allocation, exported by IPC)
+    uint8_t** ep_peers_dev = nullptr;
+    std::vector<void*> ep_opened;    // peer buffers mapped by qx_cuda_ep_connect
+    bool ep_connected = false;
     float* d_topv = nullptr;
     float* d_norm = nullptr;
     qx_cuda_profile prof{};
@@ -155,6 +160,9 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->weights) cudaFree(E->weights);
     if (E->work) cudaFree(E->work);
     if (E->layers_dev) cudaFree(E->layers_dev);
+    for (void* p : E->ep_opened) cudaIpcCloseMemHandle(p);
+    if (E->ep_xchg) cudaFree(E->ep_xchg);
+    if (E->ep_peers_dev) cudaFree(E->ep_peers_dev);
     if (E->h_io) cudaFreeHost(E->h_io);
     if (E->own_stream && E->stream) cudaStreamDestroy(E->stream);
     cudaSetDevice(prev);
@@ -169,7 +177,11 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     o.device = -1;
     o.ctx_tokens = 4096;
     if (opt) o = *opt;
-    if (o.ep_world > 1) { set_err(err, n, "expert-parallel engines are created with qx_cuda_engine_create_ep"); return 0; }
+    if (o.nccl_comm) { set_err(err, n, "nccl_comm is reserved and must be NULL"); return 0; }
+    if (o.ep_world > (uint32_t)qx::kEpMaxRanks || (o.ep_world > 1 && o.ep_rank >= o.ep_world)) {
+        set_err(err, n, "invalid expert-parallel rank or world size");
+        return 0;
+    }
     Dims dm{};
     dm.layers = (int)model->layers; dm.hidden = (int)model->hidden; dm.q_heads = (int)model->q_heads;
     dm.kv_heads = (int)model->kv_heads; dm.head_dim = (int)model->head_dim; dm.vocab = (int)model->vocab;
@@ -313,6 +325,7 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     add((void**)&d.pos, 4);
     add((void**)&d.tokens_out, C * 4);
     add((void**)&d.err, 4);
+    add((void**)&d.ep_seq, 4);
     add((void**)&E->d_topi, 32 * 4);
     add((void**)&E->d_topv, 32 * 4);
     add((void**)&E->d_norm, H * 4);
@@ -358,6 +371,31 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         if (ce != cudaSuccess) return fail(ce, "layer table");
     } else {
         E->mega_grid = 0;
+    }
+    d.ep_world = o.ep_world > 1 ? (int)o.ep_world : 1;
+    d.ep_rank = o.ep_world > 1 ? (int)o.ep_rank : 0;
+    {
+        uint32_t r[4];
+        qx_cuda_ep_partition((uint32_t)dm.experts, (uint32_t)dm.vocab, (uint32_t)d.ep_world, (uint32_t)d.ep_rank, r);
+        d.ep_e0 = (int)r[0];
+        d.ep_e1 = (int)r[1];
+        d.ep_hg0 = (int)(r[2] / 32);
+        d.ep_hg1 = (int)(r[3] / 32);
+    }
+    if (d.ep_world > 1) {
+        // the exchange lives in its own allocation so that peers can map it (CUDA IPC)
+        if (!E->mega_grid || dm.hidden > 8 * dm.moe_inter) {
+            set_err(err, n, "expert parallelism needs the persistent step kernel for this geometry");
+            qx_cuda_engine_destroy(E);
+            return 0;
+        }
+        ce = cudaMalloc((void**)&E->ep_xchg, qx::ep_xchg_bytes(dm.hidden));
+        if (ce == cudaSuccess) ce = cudaMemset(E->ep_xchg, 0, qx::ep_xchg_bytes(dm.hidden));
+        if (ce == cudaSuccess) ce = cudaMalloc((void**)&E->ep_peers_dev, qx::kEpMaxRanks * sizeof(uint8_t*));
+        if (ce == cudaSuccess) ce = cudaMemset(E->ep_peers_dev, 0, qx::kEpMaxRanks * sizeof(uint8_t*));
+        if (ce != cudaSuccess) return fail(ce, "expert-parallel exchange buffer");
+        d.ep_local = E->ep_xchg;
+        d.ep_peers = E->ep_peers_dev;
     }
     build_ops(E);
 
@@ -443,6 +481,15 @@ bool finish(qx_cuda_engine* E, char* err, uint64_t n) {
     return true;
 }
 
+// An expert-parallel engine runs decode steps only once every peer is mapped.
+bool ep_ready(const qx_cuda_engine* E, char* err, uint64_t n) {
+    if (E->dev.ep_world > 1 && !E->ep_connected) {
+        set_err(err, n, "expert-parallel engine is not connected to its peers");
+        return false;
+    }
+    return true;
+}
+
 bool set_scalars(qx_cuda_engine* E, uint32_t token, uint32_t pos, char* err, uint64_t n) {
     E->h_io[0] = (int)token;
     E->h_io[1] = (int)pos;
@@ -484,7 +531,7 @@ QX_API int qx_cuda_decode_step(qx_cuda_engine* E, uint32_t token, uint32_t posit
     if (token >= (uint32_t)E->dm.vocab) { set_err(err, n, "prompt token out of range"); return 0; }
     if (position >= (uint32_t)E->dm.ctx) { set_err(err, n, "steps exceed ctx"); return 0; }
     DeviceGuard g(E->device);
-    if (!set_scalars(E, token, position, err, n) || !run_step(E, err, n)) return 0;
+    if (!ep_ready(E, err, n) || !set_scalars(E, token, position, err, n) || !run_step(E, err, n)) return 0;
     if (!d2h(E, E->h_io + 2, E->dev.token, 4, err, n)) return 0;
     const size_t L = E->dm.layers;
     if (!d2h(E, logits, E->dev.logits, (size_t)E->dm.vocab * 4, err, n) ||
@@ -502,7 +549,7 @@ QX_API int qx_cuda_generate(qx_cuda_engine* E, uint32_t token, uint32_t position
     if (token >= (uint32_t)E->dm.vocab) { set_err(err, n, "prompt token out of range"); return 0; }
     if ((uint64_t)position + steps > (uint64_t)E->dm.ctx) { set_err(err, n, "steps exceed ctx"); return 0; }
     DeviceGuard g(E->device);
-    if (!set_scalars(E, token, position, err, n)) return 0;
+    if (!ep_ready(E, err, n) || !set_scalars(E, token, position, err, n)) return 0;
     for (uint32_t s = 0; s < steps; ++s)
         if (!run_step(E, err, n)) return 0;
     if (!d2h(E, tokens_out, E->dev.tokens_out + position, (size_t)steps * 4, err, n)) return 0;
@@ -622,7 +669,7 @@ QX_API int qx_cuda_time_kernels(qx_cuda_engine* E, uint32_t token, uint32_t posi
                                 uint32_t* kernel_count, char* err, uint64_t n) {
     if (!E || !steps || (uint64_t)position + steps > (uint64_t)E->dm.ctx) { set_err(err, n, "invalid argument"); return 0; }
     DeviceGuard g(E->device);
-    if (!set_scalars(E, token, position, err, n)) return 0;
+    if (!ep_ready(E, err, n) || !set_scalars(E, token, position, err, n)) return 0;
     const size_t nops = E->ops.size();
     std::vector<cudaEvent_t> ev(nops * steps + 1);
     for (auto& e : ev) cudaEventCreate(&e);
@@ -677,7 +724,7 @@ QX_API int qx_cuda_phase_trace(qx_cuda_engine* E, uint32_t token, uint32_t posit
     unsigned long long* tr = nullptr;
     if (!cuda_ok(cudaMalloc((void**)&tr, (size_t)total * 8), "cudaMalloc(trace)", err, n)) return 0;
     cudaMemsetAsync(tr, 0, (size_t)total * 8, E->stream);
-    bool ok = set_scalars(E, token, position, err, n);
+    bool ok = ep_ready(E, err, n) && set_scalars(E, token, position, err, n);
     if (ok) {
         Dev d = E->dev;
         d.trace = tr;
@@ -688,4 +735,53 @@ QX_API int qx_cuda_phase_trace(qx_cuda_engine* E, uint32_t token, uint32_t posit
     cudaFree(tr);
     if (ok) *count = c;
     return ok ? 1 : 0;
+}
+
+// ---- expert parallelism: the split and the mapping of the peers' buffers ----
+
+QX_API int qx_cuda_ep_partition(uint32_t experts, uint32_t vocab, uint32_t world, uint32_t rank, uint32_t out[4]) {
+    if (!out || world < 1 || rank >= world || vocab % 32) return 0;
+    const uint32_t groups = vocab / 32;                      // head rows go in groups of 32 (two 16-row tiles)
+    out[0] = (uint32_t)((uint64_t)rank * experts / world);
+    out[1] = (uint32_t)((uint64_t)(rank + 1) * experts / world);
+    out[2] = (uint32_t)((uint64_t)rank * groups / world) * 32u;
+    out[3] = (uint32_t)((uint64_t)(rank + 1) * groups / world) * 32u;
+    return 1;
+}
+
+QX_API int qx_cuda_ep_handle(qx_cuda_engine* E, void* handle, uint64_t handle_size, char* err, uint64_t n) {
+    if (!E || !handle || handle_size < sizeof(cudaIpcMemHandle_t)) { set_err(err, n, "invalid argument"); return 0; }
+    if (E->dev.ep_world <= 1) { set_err(err, n, "engine is not expert-parallel"); return 0; }
+    DeviceGuard g(E->device);
+    cudaIpcMemHandle_t h;
+    if (!cuda_ok(cudaIpcGetMemHandle(&h, E->ep_xchg), "cudaIpcGetMemHandle", err, n)) return 0;
+    memset(handle, 0, (size_t)handle_size);
+    memcpy(handle, &h, sizeof(h));
+    return 1;
+}
+
+QX_API int qx_cuda_ep_connect(qx_cuda_engine* E, const void* handles, uint64_t handle_size, uint32_t world, char* err,
+                              uint64_t n) {
+    if (!E || !handles || handle_size < sizeof(cudaIpcMemHandle_t)) { set_err(err, n, "invalid argument"); return 0; }
+    if (E->dev.ep_world <= 1 || (int)world != E->dev.ep_world) {
+        set_err(err, n, "peer count does not match the engine's expert-parallel world size");
+        return 0;
+    }
+    if (E->ep_connected) { set_err(err, n, "expert-parallel engine is already connected"); return 0; }
+    DeviceGuard g(E->device);
+    uint8_t* ptrs[qx::kEpMaxRanks] = {};
+    for (uint32_t p = 0; p < world; ++p) {
+        if ((int)p == E->dev.ep_rank) { ptrs[p] = E->ep_xchg; continue; }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)p * handle_size, sizeof(h));
+        void* mapped = nullptr;
+        if (!cuda_ok(cudaIpcOpenMemHandle(&mapped, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle", err, n))
+            return 0;
+        E->ep_opened.push_back(mapped);
+        ptrs[p] = static_cast<uint8_t*>(mapped);
+    }
+    if (!cuda_ok(cudaMemcpy(E->ep_peers_dev, ptrs, sizeof(ptrs), cudaMemcpyHostToDevice), "peer table", err, n))
+        return 0;
+    E->ep_connected = true;
+    return 1;
 }

@@ -64,6 +64,26 @@ struct Dev {
     int* err;                    // error bits
     int head_grid;               // CTAs of the head kernel (partials length)
     unsigned long long* trace;   // optional: global-timer stamp per grid barrier (CTA 0)
+    // expert parallelism (ep_world > 1; persistent step kernel only)
+    int ep_rank, ep_world;
+    uint8_t* ep_local;           // this rank's exchange buffer (peers store into it)
+    uint8_t* const* ep_peers;    // [ep_world] every rank's exchange buffer as mapped on this device
+    unsigned* ep_seq;            // decode steps run so far (the same count on every rank)
+    int ep_e0, ep_e1;            // experts this rank computes: [ep_e0, ep_e1)
+    int ep_hg0, ep_hg1;          // head row groups (32 rows each) this rank scans
+};
+
+// Exchange buffer of one rank: MoE terms [2 layer parities][8 top-8 slots][H]
+// floats written by the rank that owns each slot, then per-source flags and
+// the head's per-rank (max logit, index).
+constexpr int kEpMaxRanks = 8;
+__host__ __device__ inline size_t ep_terms_bytes(int hidden) { return (size_t)2 * 8 * hidden * 4; }
+__host__ __device__ inline size_t ep_xchg_bytes(int hidden) { return ep_terms_bytes(hidden) + 4096; }
+struct EpTail {                  // at offset ep_terms_bytes(H)
+    unsigned layer_flag[kEpMaxRanks];
+    unsigned head_flag[kEpMaxRanks];
+    double best_val[kEpMaxRanks];
+    int best_idx[kEpMaxRanks];
 };
 
 enum CounterSlot { kCntRouter = 8, kCntHead = 9, kCntBarrier = 10, kCntTotal = 16 };

@@ -161,26 +161,80 @@ __device__ void issue_router(const Dev& d, const LayerW& w, uint8_t* buf, uint32
         stage_copy(buf + (size_t)k * rowb, reinterpret_cast<const uint8_t*>(w.router) + (size_t)item_id(k) * rowb, rowb);
 }
 
-__device__ void issue_gateup(const Dev& d, const LayerW& w, const int* sel, uint8_t* buf) {
+// own[0..n_own): the top-8 slots (rank order) whose expert this GPU computes
+// (all 8 on one GPU).
+__device__ void issue_gateup(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf) {
     const int H = d.dm.hidden, I = d.dm.moe_inter;
     const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
-    const int tpe = I / kTileRows, mine = my_items(8 * tpe);
+    const int tpe = I / kTileRows, mine = my_items(n_own * tpe);
     for (int k = 0; k < mine; ++k) {
-        const int it = item_id(k), e = it / tpe, i0 = (it % tpe) * kTileRows;
+        const int it = item_id(k), e = own[it / tpe], i0 = (it % tpe) * kTileRows;
         const size_t off = (size_t)sel[e] * ((size_t)I * rb) + (size_t)i0 * rb;
         stage_copy(buf + (size_t)(2 * k) * tb, w.gate + off, tb);
         stage_copy(buf + (size_t)(2 * k + 1) * tb, w.up + off, tb);
     }
 }
 
-__device__ void issue_down(const Dev& d, const LayerW& w, const int* sel, uint8_t* buf) {
+__device__ void issue_down(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf) {
     const int H = d.dm.hidden, I = d.dm.moe_inter;
     const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
     const size_t slice = (size_t)H * rb;
     const int mine = my_items(H / kTileRows);
     for (int k = 0; k < mine; ++k)
-        for (int e = 0; e < 8; ++e)
-            stage_copy(buf + (size_t)(8 * k + e) * tb, w.down + (size_t)sel[e] * slice + (size_t)item_id(k) * tb, tb);
+        for (int j = 0; j < n_own; ++j)
+            stage_copy(buf + (size_t)(n_own * k + j) * tb, w.down + (size_t)sel[own[j]] * slice + (size_t)item_id(k) * tb,
+                       tb);
+}
+
+// ---- expert-parallel exchange ------------------------------------------------
+__device__ __forceinline__ float* ep_terms(uint8_t* base, int parity, int slot, int H) {
+    return reinterpret_cast<float*>(base) + ((size_t)parity * 8 + slot) * H;
+}
+__device__ __forceinline__ EpTail* ep_tail(uint8_t* base, int H) {
+    return reinterpret_cast<EpTail*>(base + ep_terms_bytes(H));
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread waits until flags[p] >= want for every rank p (wrap-safe), with
+// the grid barrier's bounds: on timeout it sets kErrTimeout and returns.
+__device__ void ep_wait_flags(const unsigned* flags, int world, unsigned want, int* err) {
+    const unsigned long long t0 = global_ns();
+    for (int p = 0; p < world; ++p)
+        for (long long it = 0; (int)(ld_acquire_sys(flags + p) - want) < 0; ++it)
+            if ((it & 63) == 63) {
+                if (*reinterpret_cast<volatile int*>(err) & kErrTimeout) return;
+                if (global_ns() - t0 > kBarrierTimeoutNs || it > kSpinLimit) {
+                    atomicOr(err, kErrTimeout);
+                    return;
+                }
+            }
+}
+
+// x + the MoE output of the previous layer (all 8 slots, rank order, float),
+// into xs[0..H): the single-GPU down phase's `moe` and residual add.
+__device__ void ep_combine(const Dev& d, int prev_layer, float* xs) {
+    const int H = d.dm.hidden;
+    for (int i = threadIdx.x; i < H; i += kMT) {
+        float moe = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) moe += __ldcg(ep_terms(d.ep_local, prev_layer & 1, k, H) + i);   // peer-written: skip L1
+        xs[i] = d.x[i] + moe;
+    }
+    __syncthreads();
+}
+
+// CTA-wide: wait for every rank's MoE terms of `prev_layer`.
+__device__ void ep_wait_layer(const Dev& d, unsigned seqb, int prev_layer) {
+    if (threadIdx.x == 0)
+        ep_wait_flags(ep_tail(d.ep_local, d.dm.hidden)->layer_flag, d.ep_world, seqb + prev_layer + 1, d.err);
+    __syncthreads();
 }
 
 constexpr int kHeadGroupTiles = 2;
@@ -639,6 +693,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     __shared__ double probs[kMT];
     __shared__ double wsel[8];
     __shared__ int sel[8];
+    __shared__ int own[8];
+    __shared__ int n_own_s;
     __shared__ AttnSmem attn;
     __shared__ double hbv[kMW];
     __shared__ int hbi[kMW];
@@ -658,6 +714,12 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         return;   // uniform across the grid: no barrier is entered
     }
     if (d.trace && blockIdx.x == 0 && threadIdx.x == 0) d.trace[0] = global_ns();
+    // expert parallelism: this rank's experts [e0, e1) and head groups [hg0, hg1)
+    // (qx_cuda_ep_partition); flags of this step are seqb + layer + 1 (MoE
+    // terms) and seqb + 63 (head)
+    const bool ep = d.ep_world > 1;
+    const unsigned seqb = ep ? *d.ep_seq * 64u : 0u;
+    const int e0 = d.ep_e0, e1 = d.ep_e1, hg0 = d.ep_hg0, hg1 = d.ep_hg1;
     uint32_t K4[4];
     load_kv_regs(d.tables, K4);
     load_iq_tables(T, d.tables, true, true);
@@ -693,8 +755,14 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         // ---------------- QKV (weights in buf[qb]) ----------------
         {
             cp_async_wait<0>();                  // this phase's tiles and norm vector
-            if (layer > 0) copy_to_smem(d.x, xs, H);
-            else __syncthreads();
+            if (layer > 0 && ep) {
+                ep_wait_layer(d, seqb, layer - 1);
+                ep_combine(d, layer - 1, xs);
+            } else if (layer > 0) {
+                copy_to_smem(d.x, xs, H);
+            } else {
+                __syncthreads();
+            }
             // attention RMSNorm of xs in place
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
             double ss = 0.0;
@@ -753,7 +821,14 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
                 const float o = finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
                 d.attn_out[row] = o;
-                d.x[row] = d.x[row] + o;
+                float xr = d.x[row];
+                if (ep && layer > 0) {           // the previous layer's MoE add, as ep_combine does it
+                    float moe = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) moe += __ldcg(ep_terms(d.ep_local, (layer - 1) & 1, k, H) + row);
+                    xr = xr + moe;
+                }
+                d.x[row] = xr + o;
             }
             grid_sync(bar, epoch, nsync, d);
         }
@@ -792,10 +867,18 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         // ---------------- top-8 + gate/up (weights in buf[1-qb]) ----------------
         {
             top8(d, layer, sel, wsel, probs, scratch);
+            if (threadIdx.x == 0) {
+                int n = 0;
+                for (int k = 0; k < 8; ++k)
+                    if (sel[k] >= e0 && sel[k] < e1) own[n++] = k;
+                n_own_s = n;
+            }
+            __syncthreads();
+            const int n_own = n_own_s;
             mark(d, epoch, 0);
-            issue_gateup(d, w, sel, buf[1 - qb]);
+            issue_gateup(d, w, sel, own, n_own, buf[1 - qb]);
             cp_async_commit();
-            issue_down(d, w, sel, buf[qb]);
+            issue_down(d, w, sel, own, n_own, buf[qb]);
             cp_async_commit();
             build_xq(xs, H, xb, sb);            // xs still holds the FFN-normed input
             __syncthreads();
@@ -804,7 +887,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             __syncthreads();
             mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
-            const int mine = my_items(8 * (I / kTileRows)), nblk = H / 256;
+            const int mine = my_items(n_own * (I / kTileRows)), nblk = H / 256;
             run_tasks<QXH_IQ2_XS_F>(buf[1 - qb], tb, rb, 2 * mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
             mark(d, epoch, 3);
             const int tpe = I / kTileRows;
@@ -819,11 +902,12 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         }
         // ---------------- down (weights in buf[qb]) ----------------
         {
-            copy_to_smem(d.hbuf, xs, 8 * I);
+            const int n_own = n_own_s;
+            copy_to_smem(d.hbuf, xs, n_own * I);
             mark(d, epoch, 0);
-            build_xq(xs, 8 * I, xb, sb);     // expert e's groups start at e * I / 16 (I % 256 == 0)
+            build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
             if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm);
-            else if ((int)blockIdx.x < m.vocab / (kTileRows * kHeadGroupTiles)) issue_head_group(d, blockIdx.x, buf[1 - qb]);
+            else if ((int)blockIdx.x < hg1 - hg0) issue_head_group(d, hg0 + blockIdx.x, buf[1 - qb]);
             cp_async_commit();
             __syncthreads();
             mark(d, epoch, 1);
@@ -832,25 +916,52 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = I / 256;
-            run_tasks<QXH_IQ3_XXS_F>(buf[qb], tb, rb, 8 * mine, nblk,
-                                     [&](int i) { return XQ{xb + (i % 8) * xq_words(I), sb + (i % 8) * (I / 256)}; },
+            run_tasks<QXH_IQ3_XXS_F>(buf[qb], tb, rb, n_own * mine, nblk,
+                                     [&](int i) {
+                                         return XQ{xb + (i % n_own) * xq_words(I), sb + (i % n_own) * (I / 256)};
+                                     },
                                      K4, T, part);
             mark(d, epoch, 3);
-            for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
-                const int k = r / kTileRows, rr = r % kTileRows, row = item_id(k) * kTileRows + rr;
-                float moe = 0.0f;
-                for (int e = 0; e < 8; ++e)
-                    moe += (float)(wsel[e] * (double)finite_or_zero_d(tile_row(part, 8 * k + e, nblk, rr)));
-                d.moe_out[row] = moe;
-                d.x[row] = d.x[row] + moe;
+            if (!ep) {
+                for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
+                    const int k = r / kTileRows, rr = r % kTileRows, row = item_id(k) * kTileRows + rr;
+                    float moe = 0.0f;
+                    for (int j = 0; j < n_own; ++j)
+                        moe += (float)(wsel[own[j]] * (double)finite_or_zero_d(tile_row(part, n_own * k + j, nblk, rr)));
+                    d.moe_out[row] = moe;
+                    d.x[row] = d.x[row] + moe;
+                }
+            } else {
+                // this rank's slots, weighted, into every rank's exchange buffer
+                for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
+                    const int k = r / kTileRows, rr = r % kTileRows, row = item_id(k) * kTileRows + rr;
+                    for (int j = 0; j < n_own; ++j) {
+                        const float term =
+                            (float)(wsel[own[j]] * (double)finite_or_zero_d(tile_row(part, n_own * k + j, nblk, rr)));
+                        for (int p = 0; p < d.ep_world; ++p) ep_terms(d.ep_peers[p], layer & 1, own[j], H)[row] = term;
+                    }
+                }
+                __threadfence_system();
             }
             grid_sync(bar, epoch, nsync, d);
+            if (ep && blockIdx.x == 0 && threadIdx.x == 0) {   // every CTA's stores are ordered before the barrier
+                __threadfence_system();
+                for (int p = 0; p < d.ep_world; ++p)
+                    st_release_sys(&ep_tail(d.ep_peers[p], H)->layer_flag[d.ep_rank], seqb + layer + 1);
+            }
         }
         qb = 1 - qb;
     }
     // ---------------- head (2-stage ring over buf[qb], buf[1-qb]) ----------------
     {
-        copy_to_smem(d.x, xs, H);
+        if (ep) {
+            ep_wait_layer(d, seqb, m.layers - 1);
+            ep_combine(d, m.layers - 1, xs);
+            if (blockIdx.x == 0)                // the final residual; d.x is still being read
+                for (int i = threadIdx.x; i < H; i += kMT) d.hbuf[i] = xs[i];
+        } else {
+            copy_to_smem(d.x, xs, H);
+        }
         double ss = 0.0;
         for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
         ss = block_sum_d(ss, scratch);
@@ -859,21 +970,21 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         __syncthreads();
         build_xq(xs, H, xb, sb);
         __syncthreads();
-        const int ngroups = m.vocab / (kTileRows * kHeadGroupTiles), mine = my_items(ngroups), nblk = H / 256;
+        const int mine = my_items(hg1 - hg0), nblk = H / 256;
         const uint32_t rb = (uint32_t)nblk * 210u, tb = (uint32_t)kTileRows * rb;
         double bv = -1.0e300;
         int bi = 0x7fffffff;
         bool bad = false;
         for (int k = 0; k < mine; ++k) {
             uint8_t* cur = buf[(qb + k) & 1];
-            if (k + 1 < mine) issue_head_group(d, item_id(k + 1), buf[(qb + k + 1) & 1]);
+            if (k + 1 < mine) issue_head_group(d, hg0 + item_id(k + 1), buf[(qb + k + 1) & 1]);
             cp_async_commit();
             cp_async_wait<1>();
             __syncthreads();
             run_tasks<QXH_Q6_K_F>(cur, tb, rb, kHeadGroupTiles, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
             if (threadIdx.x < kHeadGroupTiles * kTileRows) {
                 const int i = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows;
-                const int row = item_id(k) * kHeadGroupTiles * kTileRows + i * kTileRows + r;
+                const int row = (hg0 + item_id(k)) * kHeadGroupTiles * kTileRows + i * kTileRows + r;
                 const double v = tile_row(part, i, nblk, r);
                 if (!isfinite(v)) bad = true;
                 d.logits[row] = (float)v;
@@ -896,6 +1007,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             d.best_idx[blockIdx.x] = bi;
         }
         grid_sync(bar, epoch, nsync, d);
+        if (ep && blockIdx.x == 0)
+            for (int i = threadIdx.x; i < H; i += kMT) d.x[i] = d.hbuf[i];
         if (blockIdx.x == 0 && threadIdx.x == 0) {
             double v = d.best_val[0];
             int i = d.best_idx[0];
@@ -903,6 +1016,26 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const double cv = d.best_val[c];
                 const int ci = d.best_idx[c];
                 if (cv > v || (cv == v && ci < i)) { v = cv; i = ci; }
+            }
+            if (ep) {                             // every rank's shard maximum, lowest index on ties
+                for (int p = 0; p < d.ep_world; ++p) {
+                    EpTail* t = ep_tail(d.ep_peers[p], H);
+                    t->best_val[d.ep_rank] = v;
+                    t->best_idx[d.ep_rank] = i;
+                }
+                __threadfence_system();
+                for (int p = 0; p < d.ep_world; ++p)
+                    st_release_sys(&ep_tail(d.ep_peers[p], H)->head_flag[d.ep_rank], seqb + 63u);
+                EpTail* mine_t = ep_tail(d.ep_local, H);
+                ep_wait_flags(mine_t->head_flag, d.ep_world, seqb + 63u, d.err);
+                v = __ldcg(&mine_t->best_val[0]);
+                i = __ldcg(&mine_t->best_idx[0]);
+                for (int p = 1; p < d.ep_world; ++p) {
+                    const double cv = __ldcg(&mine_t->best_val[p]);
+                    const int ci = __ldcg(&mine_t->best_idx[p]);
+                    if (cv > v || (cv == v && ci < i)) { v = cv; i = ci; }
+                }
+                *d.ep_seq = seqb / 64u + 1u;
             }
             d.tokens_out[pos] = i;
             *d.token = i;

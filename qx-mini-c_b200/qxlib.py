@@ -117,6 +117,7 @@ ENGINE_SYMBOLS = [
     "qx_cuda_engine_destroy", "qx_cuda_reset", "qx_cuda_decode_step", "qx_cuda_generate", "qx_cuda_final_head",
     "qx_cuda_moe_layer", "qx_cuda_attention_layer", "qx_cuda_embed", "qx_cuda_kv_write", "qx_cuda_kv_read",
     "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_phase_trace", "qx_cuda_stream",
+    "qx_cuda_ep_handle", "qx_cuda_ep_connect", "qx_cuda_ep_partition",
 ]
 
 VERIFY_CHECKSUMS = 0x1
@@ -146,6 +147,9 @@ def cuda():
             "qx_cuda_profile_get": [P, C.POINTER(CudaProfile)],
             "qx_cuda_time_kernels": [P, U32, U32, U32, C.c_char_p, U64, P, P, U32, P, E, U64],
             "qx_cuda_phase_trace": [P, U32, U32, P, U32, P, E, U64],
+            "qx_cuda_ep_handle": [P, P, U64, E, U64],
+            "qx_cuda_ep_connect": [P, P, U64, U32, E, U64],
+            "qx_cuda_ep_partition": [U32, U32, U32, U32, P],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)
@@ -163,16 +167,36 @@ def _p(a):
     return None if a is None else a.ctypes.data
 
 
+def ep_partition(experts, vocab, world, rank):
+    """(expert_begin, expert_end, head_row_begin, head_row_end) of `rank`
+    (qx_cuda_ep_partition; host-only, no GPU needed)."""
+    out = np.zeros(4, np.uint32)
+    if not cuda().qx_cuda_ep_partition(experts, vocab, world, rank, out.ctypes.data):
+        raise ValueError("invalid expert-parallel partition arguments")
+    return tuple(int(v) for v in out)
+
+
+def connect_ep(engine, all_gather):
+    """Map every rank's exchange buffer into `engine`.  all_gather(obj) must
+    return the list of every rank's obj in rank order (e.g. a wrapper of
+    torch.distributed.all_gather_object)."""
+    handles = all_gather(engine.ep_handle())
+    engine.ep_connect(handles)
+    return handles
+
+
 class Engine:
     """Thin owner of a qx_cuda_engine*; every method is one C-ABI call."""
 
-    def __init__(self, image=None, path=None, ctx=4096, device=-1, flags=0, stream=None):
+    def __init__(self, image=None, path=None, ctx=4096, device=-1, flags=0, stream=None, ep_rank=0, ep_world=1):
         lib = cuda()
         opt = CudaOptions()
         opt.device = device
         opt.ctx_tokens = ctx
         opt.flags = flags
         opt.stream = stream
+        opt.ep_rank = ep_rank
+        opt.ep_world = ep_world
         h = C.c_void_p()
         err = err_buf()
         if path is not None:
@@ -189,6 +213,20 @@ class Engine:
         self.layers, self.hidden, self.q_heads, self.kv_heads, self.head_dim = (int(m[2]), int(m[3]), int(m[5]),
                                                                                   int(m[6]), int(m[7]))
         self.vocab, self.experts, self.moe_intermediate = int(m[8]), int(m[10]), int(m[12])
+
+    EP_HANDLE_BYTES = 64
+
+    def ep_handle(self):
+        """This rank's exchange-buffer handle (bytes) for qx_cuda_ep_connect."""
+        buf = C.create_string_buffer(self.EP_HANDLE_BYTES)
+        self._call("qx_cuda_ep_handle", buf, self.EP_HANDLE_BYTES)
+        return buf.raw
+
+    def ep_connect(self, handles):
+        """Map every rank's exchange buffer; handles: list of bytes in rank order."""
+        blob = b"".join(h.ljust(self.EP_HANDLE_BYTES, b"\0")[:self.EP_HANDLE_BYTES] for h in handles)
+        buf = C.create_string_buffer(blob, len(blob))
+        self._call("qx_cuda_ep_connect", buf, self.EP_HANDLE_BYTES, len(handles))
 
     def close(self):
         if getattr(self, "h", None):
