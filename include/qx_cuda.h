@@ -177,6 +177,24 @@ int qx_cuda_kv_write(qx_cuda_engine *engine, uint32_t layer, uint32_t first, uin
 int qx_cuda_kv_read(qx_cuda_engine *engine, uint32_t layer, uint32_t first, uint32_t count, int8_t *k, int8_t *v,
                     float *k_scales, float *v_scales, char *err, uint64_t err_len);
 
+/* ---- KV snapshots (QXKVSNP1) -------------------------------------------
+ *
+ * The reference's accumulated-KV snapshot (--kv-snapshot-out / --kv-snapshot-in,
+ * qx_write_accumulated_kv_snapshot / qx_read_accumulated_kv_snapshot,
+ * src/qx_format.c:5860-5969): version 2, INT8 format, the K row, V row and two
+ * scales of positions 0..positions-1 of every layer, SHA-256 trailer.  The
+ * bytes are the reference's, so the CPU path and this engine can continue
+ * from each other's KV; ctx_tokens and seed must match on both sides (they are
+ * part of the header).  Import checks the header, every scale and the digest
+ * with the reference's messages ("accumulated KV snapshot header mismatch",
+ * "accumulated KV snapshot payload mismatch") and leaves the device KV as it
+ * was on failure; on success it replaces the whole cache (positions beyond
+ * the snapshot read as zero) and returns the positions and next token. */
+int qx_cuda_kv_export(qx_cuda_engine *engine, const char *path, uint32_t positions, uint32_t next_token,
+                      uint32_t seed, char *err, uint64_t err_len);
+int qx_cuda_kv_import(qx_cuda_engine *engine, const char *path, uint32_t seed, uint32_t *positions,
+                      uint32_t *next_token, char *err, uint64_t err_len);
+
 /* ---- introspection ----------------------------------------------------- */
 
 int qx_cuda_profile_get(const qx_cuda_engine *engine, qx_cuda_profile *out);

@@ -290,3 +290,19 @@ QXREF_API const void *qxref_table(uint32_t which) {
 QXREF_API uint32_t qxref_sizeof(uint32_t which) {
     return which == 0 ? (uint32_t)sizeof(qx_header) : which == 1 ? (uint32_t)sizeof(qx_tensor_dir_entry) : 0u;
 }
+
+/* The reference's accumulated-KV snapshot writer and reader (INT8 format). */
+QXREF_API int qxref_kv_snapshot_write(const char *path, uint32_t layers, uint32_t positions, uint32_t ctx,
+                                      uint32_t kv_heads, uint32_t head_dim, uint32_t next_token, uint32_t seed,
+                                      const unsigned char *k, const unsigned char *v, const float *ks, const float *vs,
+                                      char *err, uint64_t err_len) {
+    return qx_write_accumulated_kv_snapshot(path, layers, positions, ctx, kv_heads, head_dim, "int8",
+                                            (uint64_t)kv_heads * head_dim, next_token, seed, k, v, ks, vs, err, err_len);
+}
+
+QXREF_API int qxref_kv_snapshot_read(const char *path, uint32_t layers, uint32_t ctx, uint32_t kv_heads,
+                                     uint32_t head_dim, uint32_t seed, unsigned char *k, unsigned char *v, float *ks,
+                                     float *vs, uint32_t *positions, uint32_t *next_token, char *err, uint64_t err_len) {
+    return qx_read_accumulated_kv_snapshot(path, layers, ctx, kv_heads, head_dim, "int8", (uint64_t)kv_heads * head_dim,
+                                           seed, k, v, ks, vs, positions, next_token, err, err_len);
+}

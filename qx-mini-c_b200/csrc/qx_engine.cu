@@ -785,3 +785,50 @@ QX_API int qx_cuda_ep_connect(qx_cuda_engine* E, const void* handles, uint64_t h
     E->ep_connected = true;
     return 1;
 }
+
+// ---- QXKVSNP1 snapshot of the persistent INT8 KV ----------------------------
+
+QX_API int qx_cuda_kv_export(qx_cuda_engine* E, const char* path, uint32_t positions, uint32_t next_token,
+                             uint32_t seed, char* err, uint64_t n) {
+    if (!E || !path || positions == 0 || positions > (uint32_t)E->dm.ctx) {
+        set_err(err, n, "invalid accumulated KV snapshot output");
+        return 0;
+    }
+    DeviceGuard g(E->device);
+    const size_t L = E->dm.layers, C = E->dm.ctx, KV = E->dm.kv_dim();
+    std::vector<int8_t> k(L * C * KV), v(L * C * KV);
+    std::vector<float> ks(L * C), vs(L * C);
+    cudaError_t ce = cudaStreamSynchronize(E->stream);
+    if (ce == cudaSuccess) ce = cudaMemcpy(k.data(), E->dev.kcache, k.size(), cudaMemcpyDeviceToHost);
+    if (ce == cudaSuccess) ce = cudaMemcpy(v.data(), E->dev.vcache, v.size(), cudaMemcpyDeviceToHost);
+    if (ce == cudaSuccess) ce = cudaMemcpy(ks.data(), E->dev.kscale, ks.size() * 4, cudaMemcpyDeviceToHost);
+    if (ce == cudaSuccess) ce = cudaMemcpy(vs.data(), E->dev.vscale, vs.size() * 4, cudaMemcpyDeviceToHost);
+    if (!cuda_ok(ce, "KV snapshot d2h", err, n)) return 0;
+    E->prof.device_to_host_bytes += 2 * (k.size() + ks.size() * 4);
+    return qxh_kv_snapshot_write(path, (uint32_t)L, positions, (uint32_t)C, (uint32_t)E->dm.kv_heads,
+                                 (uint32_t)E->dm.head_dim, next_token, seed, k.data(), v.data(), ks.data(), vs.data(),
+                                 err, n);
+}
+
+QX_API int qx_cuda_kv_import(qx_cuda_engine* E, const char* path, uint32_t seed, uint32_t* positions,
+                             uint32_t* next_token, char* err, uint64_t n) {
+    if (!E || !path || !positions || !next_token) { set_err(err, n, "invalid argument"); return 0; }
+    DeviceGuard g(E->device);
+    const size_t L = E->dm.layers, C = E->dm.ctx, KV = E->dm.kv_dim();
+    std::vector<int8_t> k(L * C * KV, 0), v(L * C * KV, 0);
+    std::vector<float> ks(L * C, 0.f), vs(L * C, 0.f);
+    uint32_t pos = 0, nt = 0;
+    if (!qxh_kv_snapshot_read(path, (uint32_t)L, (uint32_t)C, (uint32_t)E->dm.kv_heads, (uint32_t)E->dm.head_dim, seed,
+                              k.data(), v.data(), ks.data(), vs.data(), &pos, &nt, err, n))
+        return 0;                         // the device KV is untouched on failure
+    cudaError_t ce = cudaStreamSynchronize(E->stream);
+    if (ce == cudaSuccess) ce = cudaMemcpy(E->dev.kcache, k.data(), k.size(), cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(E->dev.vcache, v.data(), v.size(), cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(E->dev.kscale, ks.data(), ks.size() * 4, cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(E->dev.vscale, vs.data(), vs.size() * 4, cudaMemcpyHostToDevice);
+    if (!cuda_ok(ce, "KV snapshot h2d", err, n)) return 0;
+    E->prof.host_to_device_bytes += 2 * (k.size() + ks.size() * 4);
+    *positions = pos;
+    *next_token = nt;
+    return 1;
+}

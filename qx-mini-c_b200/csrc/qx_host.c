@@ -619,3 +619,178 @@ int qxh_synth_build(const qxh_synth_config *c, void *image_v, uint64_t size, cha
     if (!ok) { qxh_set_err(err, err_len, "thread start failed"); return 0; }
     return 1;
 }
+
+/* ---- SHA-256 (FIPS 180-4) ------------------------------------------------ */
+
+static const uint32_t qxh_sha_k[64] = {
+    0x428a2f98u, 0x71374491u, 0xb5c0fbcfu, 0xe9b5dba5u, 0x3956c25bu, 0x59f111f1u, 0x923f82a4u, 0xab1c5ed5u,
+    0xd807aa98u, 0x12835b01u, 0x243185beu, 0x550c7dc3u, 0x72be5d74u, 0x80deb1feu, 0x9bdc06a7u, 0xc19bf174u,
+    0xe49b69c1u, 0xefbe4786u, 0x0fc19dc6u, 0x240ca1ccu, 0x2de92c6fu, 0x4a7484aau, 0x5cb0a9dcu, 0x76f988dau,
+    0x983e5152u, 0xa831c66du, 0xb00327c8u, 0xbf597fc7u, 0xc6e00bf3u, 0xd5a79147u, 0x06ca6351u, 0x14292967u,
+    0x27b70a85u, 0x2e1b2138u, 0x4d2c6dfcu, 0x53380d13u, 0x650a7354u, 0x766a0abbu, 0x81c2c92eu, 0x92722c85u,
+    0xa2bfe8a1u, 0xa81a664bu, 0xc24b8b70u, 0xc76c51a3u, 0xd192e819u, 0xd6990624u, 0xf40e3585u, 0x106aa070u,
+    0x19a4c116u, 0x1e376c08u, 0x2748774cu, 0x34b0bcb5u, 0x391c0cb3u, 0x4ed8aa4au, 0x5b9cca4fu, 0x682e6ff3u,
+    0x748f82eeu, 0x78a5636fu, 0x84c87814u, 0x8cc70208u, 0x90befffau, 0xa4506cebu, 0xbef9a3f7u, 0xc67178f2u};
+
+#define QXH_ROR(x, n) (((x) >> (n)) | ((x) << (32 - (n))))
+
+static void qxh_sha256_block(qxh_sha256 *s, const unsigned char *p) {
+    uint32_t w[64];
+    for (int i = 0; i < 16; ++i)
+        w[i] = ((uint32_t)p[4 * i] << 24) | ((uint32_t)p[4 * i + 1] << 16) | ((uint32_t)p[4 * i + 2] << 8) | p[4 * i + 3];
+    for (int i = 16; i < 64; ++i) {
+        const uint32_t a = w[i - 15], b = w[i - 2];
+        w[i] = w[i - 16] + (QXH_ROR(a, 7) ^ QXH_ROR(a, 18) ^ (a >> 3)) + w[i - 7] + (QXH_ROR(b, 17) ^ QXH_ROR(b, 19) ^ (b >> 10));
+    }
+    uint32_t v[8];
+    memcpy(v, s->h, sizeof v);
+    for (int i = 0; i < 64; ++i) {
+        const uint32_t e = v[4], a = v[0];
+        const uint32_t t1 = v[7] + (QXH_ROR(e, 6) ^ QXH_ROR(e, 11) ^ QXH_ROR(e, 25)) + ((e & v[5]) ^ (~e & v[6])) +
+                            qxh_sha_k[i] + w[i];
+        const uint32_t t2 = (QXH_ROR(a, 2) ^ QXH_ROR(a, 13) ^ QXH_ROR(a, 22)) + ((a & v[1]) ^ (a & v[2]) ^ (v[1] & v[2]));
+        memmove(v + 1, v, 7 * sizeof(uint32_t));
+        v[4] += t1;
+        v[0] = t1 + t2;
+    }
+    for (int i = 0; i < 8; ++i) s->h[i] += v[i];
+}
+
+void qxh_sha256_init(qxh_sha256 *s) {
+    static const uint32_t h0[8] = {0x6a09e667u, 0xbb67ae85u, 0x3c6ef372u, 0xa54ff53au,
+                                   0x510e527fu, 0x9b05688cu, 0x1f83d9abu, 0x5be0cd19u};
+    memcpy(s->h, h0, sizeof h0);
+    s->bytes = 0;
+    s->fill = 0;
+}
+
+void qxh_sha256_update(qxh_sha256 *s, const void *data, uint64_t len) {
+    const unsigned char *p = (const unsigned char *)data;
+    s->bytes += len;
+    while (len) {
+        uint32_t take = 64u - s->fill;
+        if (take > len) take = (uint32_t)len;
+        memcpy(s->buf + s->fill, p, take);
+        s->fill += take;
+        p += take;
+        len -= take;
+        if (s->fill == 64u) {
+            qxh_sha256_block(s, s->buf);
+            s->fill = 0;
+        }
+    }
+}
+
+void qxh_sha256_final(qxh_sha256 *s, unsigned char out[32]) {
+    const uint64_t bits = s->bytes * 8u;
+    const unsigned char one = 0x80u, zero = 0u;
+    qxh_sha256_update(s, &one, 1);
+    while (s->fill != 56u) qxh_sha256_update(s, &zero, 1);
+    unsigned char len[8];
+    for (int i = 0; i < 8; ++i) len[i] = (unsigned char)(bits >> (56 - 8 * i));
+    qxh_sha256_update(s, len, 8);
+    for (int i = 0; i < 8; ++i) {
+        out[4 * i] = (unsigned char)(s->h[i] >> 24);
+        out[4 * i + 1] = (unsigned char)(s->h[i] >> 16);
+        out[4 * i + 2] = (unsigned char)(s->h[i] >> 8);
+        out[4 * i + 3] = (unsigned char)s->h[i];
+    }
+}
+
+/* ---- QXKVSNP1 accumulated-KV snapshot (INT8 KV) ---------------------------- */
+
+static void qxh_le32(unsigned char *p, uint32_t v) {
+    p[0] = (unsigned char)v; p[1] = (unsigned char)(v >> 8); p[2] = (unsigned char)(v >> 16); p[3] = (unsigned char)(v >> 24);
+}
+static uint32_t qxh_rd32(const unsigned char *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+int qxh_kv_snapshot_write(const char *path, uint32_t layers, uint32_t positions, uint32_t ctx, uint32_t kv_heads,
+                          uint32_t head_dim, uint32_t next_token, uint32_t seed, const int8_t *k, const int8_t *v,
+                          const float *kscale, const float *vscale, char *err, uint64_t err_len) {
+    const uint64_t row = (uint64_t)kv_heads * head_dim;
+    if (!path || !*path || !k || !v || !kscale || !vscale || positions == 0u || positions > ctx || row > UINT32_MAX) {
+        qxh_set_err(err, err_len, "invalid accumulated KV snapshot output");
+        return 0;
+    }
+    FILE *fp = fopen(path, "wb");
+    if (!fp) { qxh_set_err(err, err_len, "cannot open accumulated KV snapshot output"); return 0; }
+    unsigned char hdr[48] = {0};
+    memcpy(hdr, "QXKVSNP1", 8);
+    const uint32_t fields[10] = {2u, layers, positions, ctx, kv_heads, head_dim, 1u /* int8 */, (uint32_t)row,
+                                 next_token, seed};
+    for (int i = 0; i < 10; ++i) qxh_le32(hdr + 8 + 4 * i, fields[i]);
+    qxh_sha256 h;
+    qxh_sha256_init(&h);
+    qxh_sha256_update(&h, hdr, sizeof hdr);
+    int ok = fwrite(hdr, 1, sizeof hdr, fp) == sizeof hdr;
+    for (uint32_t l = 0; l < layers && ok; ++l)
+        for (uint32_t p = 0; p < positions && ok; ++p) {
+            const uint64_t slot = (uint64_t)l * ctx + p;
+            unsigned char sc[8];
+            uint32_t bits;
+            memcpy(&bits, &kscale[slot], 4); qxh_le32(sc, bits);
+            memcpy(&bits, &vscale[slot], 4); qxh_le32(sc + 4, bits);
+            qxh_sha256_update(&h, k + slot * row, row);
+            qxh_sha256_update(&h, v + slot * row, row);
+            qxh_sha256_update(&h, sc, 8);
+            ok = fwrite(k + slot * row, 1, (size_t)row, fp) == row && fwrite(v + slot * row, 1, (size_t)row, fp) == row &&
+                 fwrite(sc, 1, 8, fp) == 8;
+        }
+    unsigned char digest[32];
+    qxh_sha256_final(&h, digest);
+    if (ok) ok = fwrite(digest, 1, 32, fp) == 32;
+    if (fclose(fp) != 0) ok = 0;
+    if (!ok) qxh_set_err(err, err_len, "cannot write complete accumulated KV snapshot");
+    return ok;
+}
+
+int qxh_kv_snapshot_read(const char *path, uint32_t layers, uint32_t ctx, uint32_t kv_heads, uint32_t head_dim,
+                         uint32_t seed, int8_t *k, int8_t *v, float *kscale, float *vscale, uint32_t *positions_out,
+                         uint32_t *next_token_out, char *err, uint64_t err_len) {
+    const uint64_t row = (uint64_t)kv_heads * head_dim;
+    FILE *fp = path ? fopen(path, "rb") : NULL;
+    if (!fp) { qxh_set_err(err, err_len, "cannot open accumulated KV snapshot input"); return 0; }
+    unsigned char hdr[48];
+    int ok = fread(hdr, 1, sizeof hdr, fp) == sizeof hdr;
+    const uint32_t positions = ok ? qxh_rd32(hdr + 16) : 0u;
+    if (!ok || memcmp(hdr, "QXKVSNP1", 8) != 0 || qxh_rd32(hdr + 8) != 2u || qxh_rd32(hdr + 12) != layers ||
+        positions == 0u || positions > ctx || qxh_rd32(hdr + 20) != ctx || qxh_rd32(hdr + 24) != kv_heads ||
+        qxh_rd32(hdr + 28) != head_dim || qxh_rd32(hdr + 32) != 1u || qxh_rd32(hdr + 36) != row ||
+        qxh_rd32(hdr + 44) != seed) {
+        fclose(fp);
+        qxh_set_err(err, err_len, "accumulated KV snapshot header mismatch");
+        return 0;
+    }
+    qxh_sha256 h;
+    qxh_sha256_init(&h);
+    qxh_sha256_update(&h, hdr, sizeof hdr);
+    for (uint32_t l = 0; l < layers && ok; ++l)
+        for (uint32_t p = 0; p < positions && ok; ++p) {
+            const uint64_t slot = (uint64_t)l * ctx + p;
+            unsigned char sc[8];
+            ok = fread(k + slot * row, 1, (size_t)row, fp) == row && fread(v + slot * row, 1, (size_t)row, fp) == row &&
+                 fread(sc, 1, 8, fp) == 8;
+            if (!ok) break;
+            qxh_sha256_update(&h, k + slot * row, row);
+            qxh_sha256_update(&h, v + slot * row, row);
+            qxh_sha256_update(&h, sc, 8);
+            uint32_t kb = qxh_rd32(sc), vb = qxh_rd32(sc + 4);
+            memcpy(&kscale[slot], &kb, 4);
+            memcpy(&vscale[slot], &vb, 4);
+            if (!isfinite(kscale[slot]) || !isfinite(vscale[slot])) ok = 0;
+        }
+    unsigned char want[32], got[32];
+    if (ok) ok = fread(want, 1, 32, fp) == 32;
+    if (ok) {
+        qxh_sha256_final(&h, got);
+        ok = memcmp(want, got, 32) == 0;
+    }
+    if (ok && fgetc(fp) != EOF) ok = 0;
+    if (fclose(fp) != 0) ok = 0;
+    if (!ok) { qxh_set_err(err, err_len, "accumulated KV snapshot payload mismatch"); return 0; }
+    *positions_out = positions;
+    *next_token_out = qxh_rd32(hdr + 40);
+    return 1;
+}

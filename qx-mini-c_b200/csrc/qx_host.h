@@ -103,6 +103,30 @@ int qxh_synth_build(const qxh_synth_config *cfg, void *image, uint64_t size, cha
 /* Deterministic N(0,1) vector for test inputs (seeded, host only). */
 void qxh_normal_vector(uint64_t seed, float *out, uint64_t n);
 
+/* SHA-256 (FIPS 180-4), for the KV snapshot trailer. */
+typedef struct qxh_sha256 {
+    uint32_t h[8];
+    uint64_t bytes;
+    unsigned char buf[64];
+    uint32_t fill;
+} qxh_sha256;
+void qxh_sha256_init(qxh_sha256 *s);
+void qxh_sha256_update(qxh_sha256 *s, const void *data, uint64_t len);
+void qxh_sha256_final(qxh_sha256 *s, unsigned char out[32]);
+
+/* QXKVSNP1 version-2 accumulated-KV snapshot with INT8 KV, the reference's
+ * file format and checks (src/qx_format.c:5860-5969): 48-byte header
+ * ("QXKVSNP1", version, layers, positions, ctx, kv_heads, head_dim, format 1,
+ * bytes per K or V row, next token, seed), then per layer and position the K
+ * row, the V row and the two F32 scales, then the SHA-256 of everything
+ * before.  Buffers are [layers][ctx][kv_heads*head_dim] and [layers][ctx]. */
+int qxh_kv_snapshot_write(const char *path, uint32_t layers, uint32_t positions, uint32_t ctx, uint32_t kv_heads,
+                          uint32_t head_dim, uint32_t next_token, uint32_t seed, const int8_t *k, const int8_t *v,
+                          const float *kscale, const float *vscale, char *err, uint64_t err_len);
+int qxh_kv_snapshot_read(const char *path, uint32_t layers, uint32_t ctx, uint32_t kv_heads, uint32_t head_dim,
+                         uint32_t seed, int8_t *k, int8_t *v, float *kscale, float *vscale, uint32_t *positions_out,
+                         uint32_t *next_token_out, char *err, uint64_t err_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,6 +65,14 @@ def host():
         lib.qxh_f32_to_fp16.argtypes = [C.c_float]
         lib.qxh_f32_to_fp16.restype = C.c_uint16
         lib.qxh_tables.restype = C.c_void_p
+        lib.qxh_sha256_init.argtypes = [C.c_void_p]
+        lib.qxh_sha256_update.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64]
+        lib.qxh_sha256_final.argtypes = [C.c_void_p, C.c_void_p]
+        VP, U32 = C.c_void_p, C.c_uint32
+        lib.qxh_kv_snapshot_write.argtypes = [C.c_char_p, U32, U32, U32, U32, U32, U32, U32, VP, VP, VP, VP,
+                                              C.c_char_p, C.c_uint64]
+        lib.qxh_kv_snapshot_read.argtypes = [C.c_char_p, U32, U32, U32, U32, U32, VP, VP, VP, VP, VP, VP,
+                                             C.c_char_p, C.c_uint64]
         _host = lib
     return _host
 
@@ -117,7 +125,7 @@ ENGINE_SYMBOLS = [
     "qx_cuda_engine_destroy", "qx_cuda_reset", "qx_cuda_decode_step", "qx_cuda_generate", "qx_cuda_final_head",
     "qx_cuda_moe_layer", "qx_cuda_attention_layer", "qx_cuda_embed", "qx_cuda_kv_write", "qx_cuda_kv_read",
     "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_phase_trace", "qx_cuda_stream",
-    "qx_cuda_ep_handle", "qx_cuda_ep_connect", "qx_cuda_ep_partition",
+    "qx_cuda_ep_handle", "qx_cuda_ep_connect", "qx_cuda_ep_partition", "qx_cuda_kv_export", "qx_cuda_kv_import",
 ]
 
 VERIFY_CHECKSUMS = 0x1
@@ -150,6 +158,8 @@ def cuda():
             "qx_cuda_ep_handle": [P, P, U64, E, U64],
             "qx_cuda_ep_connect": [P, P, U64, U32, E, U64],
             "qx_cuda_ep_partition": [U32, U32, U32, U32, P],
+            "qx_cuda_kv_export": [P, C.c_char_p, U32, U32, U32, E, U64],
+            "qx_cuda_kv_import": [P, C.c_char_p, U32, P, P, E, U64],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)
@@ -165,6 +175,42 @@ def cuda():
 
 def _p(a):
     return None if a is None else a.ctypes.data
+
+
+def sha256(data):
+    """SHA-256 digest (bytes) by the host library's implementation."""
+    state = C.create_string_buffer(128)
+    buf = bytes(data)
+    out = C.create_string_buffer(32)
+    host().qxh_sha256_init(state)
+    host().qxh_sha256_update(state, buf, len(buf))
+    host().qxh_sha256_final(state, out)
+    return out.raw
+
+
+def kv_snapshot_write(path, k, v, ks, vs, positions, next_token, seed, kv_heads, head_dim):
+    """Host writer of a QXKVSNP1 file from arrays k, v [layers][ctx][kv_heads*head_dim]
+    (int8) and ks, vs [layers][ctx] (float32)."""
+    layers, ctx = ks.shape
+    err = err_buf()
+    ok = host().qxh_kv_snapshot_write(str(path).encode(), layers, positions, ctx, kv_heads, head_dim, next_token, seed,
+                                      _p(k), _p(v), _p(ks), _p(vs), err, len(err))
+    check(ok, err, "qxh_kv_snapshot_write")
+
+
+def kv_snapshot_read(path, layers, ctx, kv_heads, head_dim, seed):
+    """Host reader; returns (k, v, ks, vs, positions, next_token)."""
+    kvv = kv_heads * head_dim
+    k = np.zeros((layers, ctx, kvv), np.int8)
+    v = np.zeros((layers, ctx, kvv), np.int8)
+    ks = np.zeros((layers, ctx), np.float32)
+    vs = np.zeros((layers, ctx), np.float32)
+    pos, nt = np.zeros(1, np.uint32), np.zeros(1, np.uint32)
+    err = err_buf()
+    ok = host().qxh_kv_snapshot_read(str(path).encode(), layers, ctx, kv_heads, head_dim, seed, _p(k), _p(v), _p(ks),
+                                     _p(vs), _p(pos), _p(nt), err, len(err))
+    check(ok, err, "qxh_kv_snapshot_read")
+    return k, v, ks, vs, int(pos[0]), int(nt[0])
 
 
 def ep_partition(experts, vocab, world, rank):
@@ -215,6 +261,15 @@ class Engine:
         self.vocab, self.experts, self.moe_intermediate = int(m[8]), int(m[10]), int(m[12])
 
     EP_HANDLE_BYTES = 64
+
+    def kv_export(self, path, positions, next_token, seed):
+        self._call("qx_cuda_kv_export", str(path).encode(), positions, next_token, seed)
+
+    def kv_import(self, path, seed):
+        """Returns (positions, next_token)."""
+        pos, nt = np.zeros(1, np.uint32), np.zeros(1, np.uint32)
+        self._call("qx_cuda_kv_import", str(path).encode(), seed, _p(pos), _p(nt))
+        return int(pos[0]), int(nt[0])
 
     def ep_handle(self):
         """This rank's exchange-buffer handle (bytes) for qx_cuda_ep_connect."""
