@@ -84,3 +84,45 @@ def test_two_gpu_expert_parallel_matches_one_gpu(kind, tmp_path):
         np.testing.assert_array_equal(ep["gen"], single["gen"], err_msg="tokens, rank %d" % r)
         np.testing.assert_array_equal(ep["experts"], single["experts"], err_msg="experts, rank %d" % r)
         np.testing.assert_array_equal(ep["resid"], single["resid"], err_msg="final residual, rank %d" % r)
+
+
+def _stall_main(rank, world, port, out_dir):
+    """Rank 1 connects but never decodes: rank 0's step must end with the
+    bounded-wait error instead of hanging, and its context must stay usable."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        img = model_image("mini")
+        eng = qxlib.Engine(img, ctx=64, device=rank, ep_rank=rank, ep_world=world)
+
+        def gather(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+
+        qxlib.connect_ep(eng, gather)
+        msg = ""
+        if rank == 0:
+            try:
+                eng.decode_step(W.START_TOKEN, 0)
+            except RuntimeError as e:
+                msg = str(e)
+            # the device still works for a single-GPU engine afterwards
+            single = qxlib.Engine(img, ctx=64, device=0)
+            ok = single.decode_step(W.START_TOKEN, 0)["token"] >= 0
+            single.close()
+            with open(os.path.join(out_dir, "stall.txt"), "w") as f:
+                f.write("%s\n%d\n" % (msg, int(ok)))
+        dist.barrier()                     # rank 1 leaves only after rank 0 is done
+        eng.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_a_rank_that_never_steps_fails_the_peer_step_with_a_bounded_wait(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("expert parallelism needs two GPUs")
+    mp.spawn(_stall_main, args=(2, free_port(), str(tmp_path)), nprocs=2, join=True)
+    msg, ok = (tmp_path / "stall.txt").read_text().splitlines()
+    assert "device grid barrier timed out" in msg
+    assert ok == "1"
