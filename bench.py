@@ -220,6 +220,63 @@ def ncu_traffic(kernel, algorithmic_bytes):
     return None
 
 
+def run_stage(args):
+    """Configs 1-3: time one stage entry point (qx_cuda_final_head /
+    qx_cuda_moe_layer / qx_cuda_attention_layer) on the device with CUDA events
+    on the engine stream; each call streams that stage's weights from HBM
+    (config 3: attention history of 4095 positions pre-filled)."""
+    import torch
+    torch.cuda.set_device(0)
+    cfg = W.model_config(full=True)
+    img = qxlib.build_image(cfg)
+    H, I = cfg.hidden, cfg.moe_intermediate
+    Q, KV = cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    eng = qxlib.Engine(img, ctx=4096, device=0)
+    stream = torch.cuda.ExternalStream(eng.stream())
+    rng = np.random.default_rng(3)
+    if args.workload == "head":
+        x = W.head_input(H)
+        call = lambda: eng.final_head(x, 1)
+        nbytes = cfg.vocab * (H // 256) * 210 + 2 * H * 4
+        what = "config1: Q6_K head 151936x2048 + final RMSNorm + argmax"
+    elif args.workload == "moe":
+        x = W.moe_input(H)
+        call = lambda: eng.moe_layer(W.MOE_LAYER, x)
+        nbytes = cfg.experts * H * 4 + 8 * (2 * I * (H // 256) * 74 + H * (I // 256) * 98) + H * 4
+        what = "config2: one MoE layer (F32 router, top-8, IQ2_XS gate/up + SwiGLU, IQ3_XXS down)"
+    else:
+        P = 4095
+        k = rng.integers(-127, 128, (P, KV), dtype=np.int8)
+        v = rng.integers(-127, 128, (P, KV), dtype=np.int8)
+        sc = (rng.random(P, dtype=np.float32) * 0.02 + 0.01).astype(np.float32)
+        eng.kv_write(W.ATTN_LAYER, 0, k, v, sc, sc)
+        x = W.attn_input(H)
+        call = lambda: eng.attention_layer(W.ATTN_LAYER, P, x)
+        nbytes = (Q + 2 * KV) * (H // 256) * 136 + H * (Q // 256) * 136 + (P + 1) * (2 * KV + 8)
+        what = "config3: attention layer at ctx 4096 (IQ4_XS QKV/O, INT8 KV history)"
+    for _ in range(max(3, args.warmup)):
+        call()
+    torch.cuda.synchronize()
+    # one event pair per call (the calls return to the host in between), median
+    times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1000.0)
+    us = float(np.median(times))
+    peak, peak_kind = peaks()
+    gbs = nbytes / us / 1e3
+    print(json.dumps({"workload": args.workload, "config": what, "us_per_call": us, "algorithmic_bytes": nbytes,
+                      "GB/s": gbs, "frac_of_measured_hbm": gbs / peak, "peak_source": peak_kind,
+                      "note": "device time of the whole entry point (kernels + 8 KB input/output copies)",
+                      "steps": args.steps}))
+    eng.close()
+    return 0
+
+
 def ep_saved_bytes(cfg, world):
     """Weight bytes per token one GPU does NOT read under expert parallelism:
     on average (1 - 1/world) of the 8 selected experts' gate/up/down slices and
@@ -242,10 +299,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling case only: the same model with fewer layers (default: all 48)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "head", "moe", "attention"],
+                    help="decode = config 4 (the bench line); head/moe/attention = configs 1-3 through the "
+                         "stage entry points, one JSON line each with the stage's HBM bandwidth")
     args = ap.parse_args()
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
+    if args.workload != "decode":
+        return run_stage(args)
 
     import torch
     import torch.distributed as dist

@@ -72,6 +72,13 @@ void set_err(char* err, uint64_t n, const std::string& m) {
     if (err && n) snprintf(err, (size_t)n, "%s", m.c_str());
 }
 
+// Kernels one per-stage decode step launches (attention may be two kernels).
+size_t stage_launches(const qx_cuda_engine* E) {
+    size_t k = 0;
+    for (const Op& op : E->ops) k += op.kind == kAttn ? (size_t)qx::attn_launches(E->dm) : 1u;
+    return k;
+}
+
 bool cuda_ok(cudaError_t e, const char* what, char* err, uint64_t n) {
     if (e == cudaSuccess) return true;
     set_err(err, n, std::string(what) + ": " + cudaGetErrorString(e));
@@ -116,7 +123,7 @@ bool run_step(qx_cuda_engine* E, char* err, uint64_t n) {
         for (const Op& op : E->ops) run_op(E, op);
         if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return false;
     }
-    E->prof.kernel_launches += E->mega_grid ? 1 : E->ops.size();
+    E->prof.kernel_launches += E->mega_grid ? 1 : stage_launches(E);
     E->prof.decode_steps++;
     return true;
 }
@@ -607,7 +614,7 @@ QX_API int qx_cuda_attention_layer(qx_cuda_engine* E, uint32_t layer, uint32_t p
     qx::launch_qkv(E->dev, w, E->stream);
     qx::launch_attn(E->dev, w, (int)layer, E->stream);
     qx::launch_oproj(E->dev, w, E->stream);
-    E->prof.kernel_launches += 3;
+    E->prof.kernel_launches += 2 + qx::attn_launches(E->dm);
     if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
     if (!d2h(E, residual, E->dev.x, (size_t)E->dm.hidden * 4, err, n) ||
         !d2h(E, attn_out, E->dev.attn_out, (size_t)E->dm.hidden * 4, err, n) ||
@@ -709,7 +716,7 @@ QX_API int qx_cuda_time_kernels(qx_cuda_engine* E, uint32_t token, uint32_t posi
     }
     if (kernel_count) *kernel_count = c;
     if (names && names_len) snprintf(names, (size_t)names_len, "%s", joined.c_str());
-    E->prof.kernel_launches += nops * steps;
+    E->prof.kernel_launches += (E->mega_grid ? nops : stage_launches(E)) * steps;
     return 1;
 }
 

@@ -573,6 +573,7 @@ cudaError_t configure_kernels() {
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)a.sharedSizeBytes);
     };
+    if (e == cudaSuccess) e = attn2_configure();
     set((const void*)k_qkv);
     set((const void*)k_oproj);
     set((const void*)k_router);
@@ -608,8 +609,19 @@ void launch_qkv(const Dev& d, const LayerW& w, cudaStream_t st) {
     k_qkv<<<(nt + kQkvTiles - 1) / kQkvTiles, kThreads, smem_qkv(d.dm), st>>>(d, w);
 }
 
+// The two-phase all-SM attention when it fits (attn2_supported), else one CTA
+// per query head (any context length).
+int attn_launches(const Dims& m) { return attn2_supported(m) ? 2 : 1; }
+
 void launch_attn(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
-    k_attn<<<d.dm.q_heads, 128, 0, st>>>(d, w, layer);
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    if (attn2_supported(d.dm)) launch_attn2(d, w, layer, sms, st);
+    else k_attn<<<d.dm.q_heads, 128, 0, st>>>(d, w, layer);
 }
 
 void launch_oproj(const Dev& d, const LayerW& w, cudaStream_t st) {

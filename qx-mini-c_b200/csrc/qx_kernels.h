@@ -109,6 +109,11 @@ bool geometry_supported(const Dims& m);
 cudaError_t configure_kernels();
 // Persistent one-launch decode step (qx_mega.cu).
 int mega_setup(int device, const Dims& m, int* grid_out);
+// Stand-alone two-phase attention (the one-launch kernel's attention code, qx_mega.cu).
+bool attn2_supported(const Dims& m);
+int attn_launches(const Dims& m);             // kernels launch_attn starts (1 or 2)
+cudaError_t attn2_configure();
+void launch_attn2(const Dev& d, const LayerW& w, int layer, int sms, cudaStream_t st);
 cudaError_t launch_decode_step(const Dev& d, const LayerW* layers_dev, int grid, cudaStream_t st);
 
 }  // namespace qx

@@ -325,6 +325,40 @@ __device__ void issue_attn_context(const Dev& d, int layer, int pos, const AttnS
     (void)pos;
 }
 
+// Context of 32 dims over positions 0..T-1: acc_d = sum_t (float)(w_t * v_t,d)
+// in float, t in order (src/qx_format.c:5152-5172).  The products of a
+// 64-position chunk are computed by warps 1.. into one half of `prod` while
+// warp 0 (lane = dim) adds the previous chunk from the other half.
+// vv(t, dd) returns the dequantized V value; prod: 2 * 64 * 32 floats.
+constexpr int kCtxChunk = 64;
+template <class VV>
+__device__ float context_chain(int T, const double* w_s, float* prod, VV vv) {
+    const int SW = 32, i = threadIdx.x, nch = (T + kCtxChunk - 1) / kCtxChunk;
+    auto products = [&](int c) {
+        float* dst = prod + (c & 1) * kCtxChunk * SW;
+        const int t0 = c * kCtxChunk, n = min(kCtxChunk, T - t0);
+        for (int idx = i - 32; idx < n * SW; idx += kMT - 32) {
+            const int t = t0 + idx / SW;
+            dst[idx] = (float)(w_s[t] * (double)vv(t, idx % SW));
+        }
+    };
+    float acc = 0.0f;
+    if (i >= 32) products(0);
+    __syncthreads();
+    for (int c = 0; c < nch; ++c) {
+        if (i < 32) {
+            const float* src = prod + (c & 1) * kCtxChunk * SW;
+            const int n = min(kCtxChunk, T - c * kCtxChunk);
+#pragma unroll 8
+            for (int tt = 0; tt < n; ++tt) acc += src[tt * SW + i];
+        } else if (c + 1 < nch) {
+            products(c + 1);
+        }
+        __syncthreads();
+    }
+    return acc;
+}
+
 // Scores.  The CTAs form kv_heads groups of G/kv_heads; group g serves the
 // query heads of KV head g, CTA r of the group positions r, r + cpg, ...;
 // thread i scores query head i % group at one of those positions.  Every CTA
@@ -354,7 +388,7 @@ __device__ void attn_scores(const Dev& d, const LayerW& w, int layer, int pos, A
     // they do not queue ahead of those loads
     issue_attn_scores(d, w, layer, pos, st);
     cp_async_commit();
-    issue_router(d, w, router_buf, norm);
+    if (router_buf) issue_router(d, w, router_buf, norm);   // none in the stand-alone kernel
     cp_async_commit();
     if (!active) return;
     cp_async_wait<1>();
@@ -457,22 +491,10 @@ __device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, floa
         const int8_t* vb = d.vcache + (size_t)layer * ctx * KV + g * D + sl * SW;
         const float* vs = d.vscale + (size_t)layer * ctx;
         const int vcap = staged ? st.vcap : 0;
-        float acc = 0.0f;
-        for (int t0 = 0; t0 < T; t0 += kVChunk) {
-            const int n = min(kVChunk, T - t0);
-            __syncthreads();
-            for (int idx = i; idx < n * SW; idx += kMT) {
-                const int t = t0 + idx / SW, dd = idx % SW;
-                const float vv = t < vcap ? (float)st.vrows[t * SW + dd] * st.vscl[t]
-                                          : (float)vb[(size_t)t * KV + dd] * vs[t];
-                prod[idx] = (float)(w_s[t] * (double)vv);
-            }
-            __syncthreads();
-            if (i < SW) {
-#pragma unroll 8
-                for (int tt = 0; tt < n; ++tt) acc += prod[tt * SW + i];
-            }
-        }
+        __syncthreads();
+        const float acc = context_chain(T, w_s, prod, [&](int t, int dd) {
+            return t < vcap ? (float)st.vrows[t * SW + dd] * st.vscl[t] : (float)vb[(size_t)t * KV + dd] * vs[t];
+        });
         if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
         mark(d, epoch, 1);
         __syncthreads();
@@ -620,21 +642,10 @@ __device__ void attn_fused(const Dev& d, const LayerW& w, int layer, int pos, At
     if (!isfinite(den) || den <= 0.0) den = 1.0;
     for (int t = i; t < T; t += kMT) f.w_s[t] = f.w_s[t] / den;
     mark(d, epoch, 2);
-    float acc = 0.0f;
-    for (int t0 = 0; t0 < T; t0 += kVChunk) {
-        const int n = min(kVChunk, T - t0);
-        __syncthreads();
-        for (int idx = i; idx < n * SW; idx += kMT) {
-            const int t = t0 + idx / SW, dd = idx % SW;
-            const float vv = t == pos ? (float)S.v8[g * D + sl * SW + dd] * vsc : (float)f.vrows[t * SW + dd] * f.vscl[t];
-            prod[idx] = (float)(f.w_s[t] * (double)vv);
-        }
-        __syncthreads();
-        if (i < SW) {
-#pragma unroll 8
-            for (int tt = 0; tt < n; ++tt) acc += prod[tt * SW + i];
-        }
-    }
+    __syncthreads();
+    const float acc = context_chain(T, f.w_s, prod, [&](int t, int dd) {
+        return t == pos ? (float)S.v8[g * D + sl * SW + dd] * vsc : (float)f.vrows[t * SW + dd] * f.vscl[t];
+    });
     if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
     __syncthreads();
 }
@@ -1044,6 +1055,34 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     }
 }
 
+// ---- the same two-phase attention as stand-alone kernels (per-stage path) ----
+// Used by the stage entry point and the per-stage decode path, so both share
+// the one-launch kernel's attention arithmetic.  Shared memory: the staging
+// region (kAttnStageBytes) followed by the query / product scratch.
+constexpr uint32_t kAttnStageBytes = 200 * 1024;   // ctx 4096: 32 KB of weights + 36 B per staged position
+constexpr uint32_t kAttnScratchBytes = kVChunk * 132 > 16 * kQdStride * 8 ? kVChunk * 132 : 16 * kQdStride * 8;
+
+__global__ void __launch_bounds__(kMT, 1) k_attn_scores(Dev d, LayerW w, int layer) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ AttnSmem attn;
+    const int pos = *d.pos;
+    if (pos < 0 || pos >= d.dm.ctx) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(d.err, kErrPosition);
+        return;
+    }
+    const AttnStage stg = attn_stage(d, pos, smem, kAttnStageBytes);
+    attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + kAttnStageBytes), stg, nullptr, 0, 0);
+}
+
+__global__ void __launch_bounds__(kMT, 1) k_attn_context(Dev d, int layer) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ AttnSmem attn;
+    const int pos = *d.pos;
+    if (pos < 0 || pos >= d.dm.ctx) return;
+    const AttnStage stg = attn_stage(d, pos, smem, kAttnStageBytes);
+    attn_context(d, layer, pos, attn, reinterpret_cast<float*>(smem + kAttnStageBytes), stg, 0);
+}
+
 namespace {
 MegaLayout g_layout;
 uint32_t a16u(size_t v) { return (uint32_t)((v + 15) / 16 * 16); }
@@ -1124,6 +1163,31 @@ cudaError_t launch_decode_step(const Dev& d, const LayerW* layers_dev, int grid,
     const LayerW* lw = layers_dev;
     void* args[] = {&dd, &lw, &L};
     return cudaLaunchCooperativeKernel((const void*)k_decode_step, dim3(grid), dim3(kMT), args, L.total, st);
+}
+
+}  // namespace qx
+
+namespace qx {
+
+// The stand-alone two-phase attention fits when the softmax weights of the
+// whole context fit the staging region and the query heads fit the scratch.
+bool attn2_supported(const Dims& m) {
+    const int group = m.q_heads / m.kv_heads;
+    return (size_t)m.ctx * 8 + 2048 <= kAttnStageBytes && kMT % group == 0 && group * 128 <= 8 * kMT &&
+           (size_t)group * kQdStride * 8 <= kAttnScratchBytes;
+}
+
+cudaError_t attn2_configure() {
+    const int bytes = (int)(kAttnStageBytes + kAttnScratchBytes);
+    cudaError_t e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_context, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    return e;
+}
+
+void launch_attn2(const Dev& d, const LayerW& w, int layer, int sms, cudaStream_t st) {
+    const size_t bytes = kAttnStageBytes + kAttnScratchBytes;
+    k_attn_scores<<<sms, kMT, bytes, st>>>(d, w, layer);
+    k_attn_context<<<std::min(sms, d.dm.q_heads * kCtxSlices), kMT, bytes, st>>>(d, layer);
 }
 
 }  // namespace qx
