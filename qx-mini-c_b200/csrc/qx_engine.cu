@@ -56,6 +56,13 @@ struct qx_cuda_engine {
     LayerW* layers_dev = nullptr;   // device copy of the layer table (persistent step kernel)
     int mega_grid = 0;               // 0 = per-stage kernels
     int* d_topi = nullptr;
+    double* d_logits_d = nullptr;    // final_head: double logits for the top-N
+    double* d_cand_v = nullptr;      // top-N candidates per part
+    int* d_cand_i = nullptr;
+    uint8_t* h_stage = nullptr;      // pinned bounce buffer for large device-to-host copies
+    size_t h_stage_bytes = 0, h_stage_used = 0;
+    struct Pending { void* dst; size_t off, bytes; };
+    std::vector<Pending> pending;    // bounce-buffer copies to finish after the stream syncs
     // expert parallelism
     uint8_t* ep_xchg = nullptr;      // this rank's exchange buffer (its own allocation, exported by IPC)
     uint8_t** ep_peers_dev = nullptr;
@@ -171,6 +178,7 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->ep_xchg) cudaFree(E->ep_xchg);
     if (E->ep_peers_dev) cudaFree(E->ep_peers_dev);
     if (E->h_io) cudaFreeHost(E->h_io);
+    if (E->h_stage) cudaFreeHost(E->h_stage);
     if (E->own_stream && E->stream) cudaStreamDestroy(E->stream);
     cudaSetDevice(prev);
     delete E;
@@ -333,6 +341,9 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     add((void**)&d.tokens_out, C * 4);
     add((void**)&d.err, 4);
     add((void**)&d.ep_seq, 4);
+    add((void**)&E->d_logits_d, (size_t)dm.vocab * 8);
+    add((void**)&E->d_cand_v, (size_t)qx::kTopnParts * 32 * 8);
+    add((void**)&E->d_cand_i, (size_t)qx::kTopnParts * 32 * 4);
     add((void**)&E->d_topi, 32 * 4);
     add((void**)&E->d_topv, 32 * 4);
     add((void**)&E->d_norm, H * 4);
@@ -370,6 +381,10 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
     if (ce != cudaSuccess) return fail(ce, "upload tables");
     ce = cudaHostAlloc((void**)&E->h_io, 64, cudaHostAllocDefault);
+    if (ce == cudaSuccess) {
+        E->h_stage_bytes = (size_t)dm.vocab * 4 + (size_t)64 * 1024;   // logits + the small outputs of one call
+        ce = cudaHostAlloc((void**)&E->h_stage, E->h_stage_bytes, cudaHostAllocDefault);
+    }
     if (ce != cudaSuccess) return fail(ce, "cudaHostAlloc");
     if (!(o.flags & QX_CUDA_PER_STAGE) && qx::mega_setup(dev, dm, &E->mega_grid)) {
         ce = cudaMalloc((void**)&E->layers_dev, E->layers.size() * sizeof(LayerW));
@@ -478,6 +493,11 @@ bool finish(qx_cuda_engine* E, char* err, uint64_t n) {
     E->prof.device_to_host_bytes += 4;
     if (ce == cudaSuccess) ce = cudaMemsetAsync(E->dev.err, 0, 4, E->stream);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
+    const bool copied = ce == cudaSuccess;
+    for (const auto& p : E->pending)
+        if (copied) memcpy(p.dst, E->h_stage + p.off, p.bytes);
+    E->pending.clear();
+    E->h_stage_used = 0;
     if (!cuda_ok(ce, "device execution", err, n)) return false;
     const int bits = E->h_io[3];
     if (bits & qx::kErrToken) { set_err(err, n, "token id out of range"); return false; }
@@ -506,10 +526,29 @@ bool set_scalars(qx_cuda_engine* E, uint32_t token, uint32_t pos, char* err, uin
     return cuda_ok(ce, "cudaMemcpyAsync(scalars)", err, n);
 }
 
+// Device-to-host copy of a call's output; large ones go through the pinned
+// bounce buffer (a pageable destination is copied at pageable speed) and land
+// in `dst` when finish() has synchronised.
 bool d2h(qx_cuda_engine* E, void* dst, const void* src, size_t bytes, char* err, uint64_t n) {
     if (!dst) return true;
     E->prof.device_to_host_bytes += bytes;
-    return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, E->stream), "cudaMemcpyAsync(d2h)", err, n);
+    const size_t off = (E->h_stage_used + 255) / 256 * 256;
+    if (bytes >= 16384 && E->h_stage && off + bytes <= E->h_stage_bytes) {
+        if (!cuda_ok(cudaMemcpyAsync(E->h_stage + off, src, bytes, cudaMemcpyDeviceToHost, E->stream),
+                     "cudaMemcpyAsync(d2h)", err, n)) {
+            E->pending.clear();               // the call fails: none of its outputs is delivered
+            E->h_stage_used = 0;
+            return false;
+        }
+        E->h_stage_used = off + bytes;
+        E->pending.push_back({dst, off, bytes});
+        return true;
+    }
+    if (cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, E->stream), "cudaMemcpyAsync(d2h)", err, n))
+        return true;
+    E->pending.clear();
+    E->h_stage_used = 0;
+    return false;
 }
 
 bool h2d(qx_cuda_engine* E, void* dst, const void* src, size_t bytes, char* err, uint64_t n) {
@@ -571,10 +610,16 @@ QX_API int qx_cuda_final_head(qx_cuda_engine* E, const float* residual, float* n
     if (!h2d(E, E->dev.x, residual, (size_t)E->dm.hidden * 4, err, n)) return 0;
     E->h_io[1] = 0;
     if (!cuda_ok(cudaMemcpyAsync(E->dev.pos, E->h_io + 1, 4, cudaMemcpyHostToDevice, E->stream), "h2d", err, n)) return 0;
-    qx::launch_head(E->dev, E->stream);
+    if (top_n && E->dm.vocab > qx::kTopnParts * 2048) { set_err(err, n, "vocabulary too large for the top-N"); return 0; }
+    Dev dh = E->dev;
+    dh.logits_d = top_n ? E->d_logits_d : nullptr;
+    qx::launch_head(dh, E->stream);
     E->prof.kernel_launches++;
     if (normalized) { qx::launch_final_norm(E->dev, E->d_norm, E->stream); E->prof.kernel_launches++; }
-    if (top_n) { qx::launch_topn(E->dev, (int)top_n, E->d_topi, E->d_topv, E->stream); E->prof.kernel_launches++; }
+    if (top_n) {
+        qx::launch_topn(dh, (int)top_n, E->d_cand_v, E->d_cand_i, E->d_topi, E->d_topv, E->stream);
+        E->prof.kernel_launches += 2;
+    }
     if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
     if (!d2h(E, normalized, E->d_norm, (size_t)E->dm.hidden * 4, err, n) ||
         !d2h(E, logits, E->dev.logits, (size_t)E->dm.vocab * 4, err, n) ||

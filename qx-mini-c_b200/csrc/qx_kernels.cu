@@ -466,6 +466,7 @@ __global__ void __launch_bounds__(kThreads) k_head(Dev d) {
             const double v = sum_parts(part, tl, parts, r);
             if (!isfinite(v)) bad = true;
             d.logits[row] = (float)v;
+            if (d.logits_d) d.logits_d[row] = v;
             if (v > bv || (v == bv && row < bi)) { bv = v; bi = row; }
         }
     }
@@ -509,37 +510,74 @@ __global__ void __launch_bounds__(256) k_final_norm(Dev d, float* out) {
     for (int i = threadIdx.x; i < d.dm.hidden; i += blockDim.x) out[i] = xs[i];
 }
 
-// Top-N of the logits buffer by repeated argmax (ties to the lower index),
-// the order qx_compute_real_final_head keeps (:3715-3731).
-__global__ void __launch_bounds__(1024) k_topn(Dev d, int top_n, int* out_idx, float* out_val) {
-    __shared__ float wv[32];
-    __shared__ int wi[32];
-    __shared__ int chosen[32];
-    const int V = d.dm.vocab, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int k = 0; k < top_n; ++k) {
-        float bv = -FLT_MAX;
+// Top-N of the head's double logits in the order qx_compute_real_final_head
+// keeps its list (:3715-3731): descending logit, the lower token first among
+// equal logits.  Stage 1: each of kTopnParts CTAs takes a contiguous slice and
+// picks its own top-N by N rounds of a block argmax; stage 2: one CTA picks
+// the top-N of those candidates the same way.
+__device__ void block_argmax(double v, int i, double* sv, int* si, double& bv, int& bi) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int o = 16; o; o >>= 1) {
+        const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+    }
+    __syncthreads();
+    if (lane == 0) { sv[warp] = v; si[warp] = i; }
+    __syncthreads();
+    bv = sv[0];
+    bi = si[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+        if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+}
+
+// Each thread holds up to 8 candidates (values, indices); picks N in order.
+template <int PER>
+__device__ void select_top(const double* vals, const int* idxs, int count, int top_n, double* out_v, int* out_i) {
+    __shared__ double sv[32];
+    __shared__ int si[32];
+    double v[PER];
+    int ix[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int j = threadIdx.x + k * (int)blockDim.x;
+        v[k] = j < count ? vals[j] : -1.0e300;
+        ix[k] = j < count ? (idxs ? idxs[j] : j) : 0x7fffffff;
+    }
+    for (int r = 0; r < top_n; ++r) {
+        double bv = -1.0e300;
         int bi = 0x7fffffff;
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            bool taken = false;
-            for (int j = 0; j < k; ++j) taken |= chosen[j] == i;
-            const float v = d.logits[i];
-            if (!taken && (v > bv || (v == bv && i < bi))) { bv = v; bi = i; }
-        }
-        for (int o = 16; o; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (lane == 0) { wv[warp] = bv; wi[warp] = bi; }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            for (int i = 1; i < (int)(blockDim.x >> 5); ++i)
-                if (wv[i] > bv || (wv[i] == bv && wi[i] < bi)) { bv = wv[i]; bi = wi[i]; }
-            chosen[k] = bi;
-            out_idx[k] = bi;
-            out_val[k] = bv;
-        }
-        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+            if (v[k] > bv || (v[k] == bv && ix[k] < bi)) { bv = v[k]; bi = ix[k]; }
+        double gv;
+        int gi;
+        block_argmax(bv, bi, sv, si, gv, gi);
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+            if (ix[k] == gi) { v[k] = -1.0e300; ix[k] = 0x7fffffff; }   // indices are unique
+        if (threadIdx.x == 0) { out_v[r] = gv; out_i[r] = gi; }
+    }
+}
+
+__global__ void __launch_bounds__(256) k_topn_part(Dev d, int top_n, double* cand_v, int* cand_i) {
+    const int V = d.dm.vocab, b = blockIdx.x;
+    const int r0 = (int)((long long)b * V / gridDim.x), r1 = (int)((long long)(b + 1) * V / gridDim.x);
+    __shared__ int ids[2048];
+    for (int j = threadIdx.x; j < r1 - r0 && j < 2048; j += blockDim.x) ids[j] = r0 + j;
+    __syncthreads();
+    select_top<8>(d.logits_d + r0, ids, r1 - r0, top_n, cand_v + (size_t)b * top_n, cand_i + (size_t)b * top_n);
+}
+
+__global__ void __launch_bounds__(1024) k_topn_merge(int parts, int top_n, const double* cand_v, const int* cand_i,
+                                                     int* out_idx, float* out_val) {
+    __shared__ double rv[32];
+    __shared__ int ri[32];
+    select_top<5>(cand_v, cand_i, parts * top_n, top_n, rv, ri);   // parts * top_n candidates, compact
+    __syncthreads();
+    if (threadIdx.x < top_n) {
+        out_idx[threadIdx.x] = ri[threadIdx.x];
+        out_val[threadIdx.x] = (float)rv[threadIdx.x];
     }
 }
 
@@ -647,8 +685,9 @@ void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st) {
     k_final_norm<<<1, 256, (size_t)d.dm.hidden * 4, st>>>(d, normalized);
 }
 
-void launch_topn(const Dev& d, int top_n, int* out_idx, float* out_val, cudaStream_t st) {
-    k_topn<<<1, 1024, 0, st>>>(d, top_n, out_idx, out_val);
+void launch_topn(const Dev& d, int top_n, double* cand_v, int* cand_i, int* out_idx, float* out_val, cudaStream_t st) {
+    k_topn_part<<<kTopnParts, 256, 0, st>>>(d, top_n, cand_v, cand_i);
+    k_topn_merge<<<1, 1024, 0, st>>>(kTopnParts, top_n, cand_v, cand_i, out_idx, out_val);
 }
 
 }  // namespace qx

@@ -55,6 +55,7 @@ struct Dev {
     double* selw_d;              // [8] weights of the current layer (double)
     float* hbuf;                 // SwiGLU outputs [8][I]
     float* logits;               // [V]
+    double* logits_d;            // optional [V]: the head's double logits (top-N of the stage entry point)
     double* best_val;            // per-CTA argmax partials (double logits, as the reference compares)
     int* best_idx;
     unsigned* counters;          // ticket counters for last-CTA reductions
@@ -98,7 +99,9 @@ void launch_router(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
 void launch_gateup(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
 void launch_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
 void launch_head(const Dev& d, cudaStream_t st);
-void launch_topn(const Dev& d, int top_n, int* out_idx, float* out_val, cudaStream_t st);
+// Top-N (N <= 32) of the double logits: per-CTA candidates, then one merge.
+constexpr int kTopnParts = 148;
+void launch_topn(const Dev& d, int top_n, double* cand_v, int* cand_i, int* out_idx, float* out_val, cudaStream_t st);
 void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st);
 int head_grid_size(int device, const Dims& m);
 size_t attn_scores_bytes(const Dims& m);
