@@ -20,6 +20,8 @@ struct Tables {
     float iq3xxs[256][4];    // IQ3_XXS lattice magnitudes as floats
     uint8_t ksigns[128];     // 7 stored sign bits + even-parity 8th bit
     float kvalues[16];       // IQ4_NL codebook
+    uint32_t iq2s[1024][2];  // IQ2_S lattice: 8 magnitude bytes per entry (value order)
+    uint32_t iq3s[512];      // IQ3_S lattice: 4 magnitude bytes per entry
 };
 
 // binary16 -> binary32 with the reference's Inf/NaN rule (exp==31 -> +-65504),

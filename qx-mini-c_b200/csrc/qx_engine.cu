@@ -10,6 +10,7 @@
 #include <map>
 #include <string>
 #include <unordered_map>
+#include <initializer_list>
 #include <vector>
 
 #include "qx_cuda.h"
@@ -82,7 +83,9 @@ void set_err(char* err, uint64_t n, const std::string& m) {
 // Kernels one per-stage decode step launches (attention may be two kernels).
 size_t stage_launches(const qx_cuda_engine* E) {
     size_t k = 0;
-    for (const Op& op : E->ops) k += op.kind == kAttn ? (size_t)qx::attn_launches(E->dm) : 1u;
+    for (const Op& op : E->ops)
+        k += op.kind == kAttn ? (size_t)qx::attn_launches(E->dm)
+             : op.kind == kQkv ? (size_t)qx::qkv_launches(E->layers[op.layer]) : 1u;
     return k;
 }
 
@@ -140,14 +143,23 @@ struct Tensor {
     size_t offset;               // in the weight arena
 };
 
+// `types`: the accepted ggml types (the first is the benchmark mix's).
 bool check_tensor(const std::unordered_map<std::string, const qx_cuda_tensor*>& by, const std::string& name,
-                  uint32_t type, uint32_t rank, uint64_t d0, uint64_t d1, uint64_t d2, char* err, uint64_t n) {
+                  std::initializer_list<uint32_t> types, uint32_t rank, uint64_t d0, uint64_t d1, uint64_t d2,
+                  char* err, uint64_t n) {
     auto it = by.find(name);
     if (it == by.end()) { set_err(err, n, "tensor not found: " + name); return false; }
     const qx_cuda_tensor* t = it->second;
-    if (t->ggml_type != type) {
+    const uint32_t type = t->ggml_type;
+    bool accepted = false;
+    std::string list;
+    for (uint32_t a : types) {
+        accepted |= a == type;
+        list += (list.empty() ? "" : "/") + std::to_string(a);
+    }
+    if (!accepted) {
         set_err(err, n, "unsupported ggml type " + std::to_string(t->ggml_type) + " for " + name +
-                            " (engine path expects " + std::to_string(type) + ")");
+                            " (engine path expects " + list + ")");
         return false;
     }
     if (t->rank != rank || t->dims[0] != d0 || (rank > 1 && t->dims[1] != d1) || (rank > 2 && t->dims[2] != d2)) {
@@ -214,23 +226,31 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         if (tensors[i].name) by[tensors[i].name] = &tensors[i];
     const uint64_t H = dm.hidden, Q = dm.q_dim(), KV = dm.kv_dim(), Ee = dm.experts, I = dm.moe_inter;
     std::vector<std::string> names;
-    auto need = [&](const std::string& nm, uint32_t type, uint32_t rank, uint64_t d0, uint64_t d1, uint64_t d2) {
+    auto need = [&](const std::string& nm, std::initializer_list<uint32_t> types, uint32_t rank, uint64_t d0,
+                    uint64_t d1, uint64_t d2) {
         names.push_back(nm);
-        return check_tensor(by, nm, type, rank, d0, d1, d2, err, n);
+        return check_tensor(by, nm, types, rank, d0, d1, d2, err, n);
     };
-    bool ok = need("token_embd.weight", QXH_Q4_K, 2, H, dm.vocab, 0) &&
-              need("output_norm.weight", QXH_F32, 1, H, 0, 0) && need("output.weight", QXH_Q6_K, 2, H, dm.vocab, 0);
+    const std::initializer_list<uint32_t> kAttnT = {QXH_IQ4_XS, QXH_Q5_K, QXH_Q6_K};
+    const std::initializer_list<uint32_t> kGateT = {QXH_IQ2_XS, QXH_IQ2_S};
+    const std::initializer_list<uint32_t> kDownT = {QXH_IQ3_XXS, QXH_IQ3_S, QXH_IQ4_XS};
+    bool ok = need("token_embd.weight", {QXH_Q4_K}, 2, H, dm.vocab, 0) &&
+              need("output_norm.weight", {QXH_F32}, 1, H, 0, 0) && need("output.weight", {QXH_Q6_K}, 2, H, dm.vocab, 0);
     for (int l = 0; ok && l < dm.layers; ++l) {
         std::string p = "blk." + std::to_string(l) + ".";
-        ok = need(p + "attn_norm.weight", QXH_F32, 1, H, 0, 0) && need(p + "attn_q.weight", QXH_IQ4_XS, 2, H, Q, 0) &&
-             need(p + "attn_k.weight", QXH_IQ4_XS, 2, H, KV, 0) && need(p + "attn_v.weight", QXH_IQ4_XS, 2, H, KV, 0) &&
-             need(p + "attn_output.weight", QXH_IQ4_XS, 2, Q, H, 0) &&
-             need(p + "attn_q_norm.weight", QXH_F32, 1, dm.head_dim, 0, 0) &&
-             need(p + "attn_k_norm.weight", QXH_F32, 1, dm.head_dim, 0, 0) &&
-             need(p + "ffn_norm.weight", QXH_F32, 1, H, 0, 0) && need(p + "ffn_gate_inp.weight", QXH_F32, 2, H, Ee, 0) &&
-             need(p + "ffn_gate_exps.weight", QXH_IQ2_XS, 3, H, I, Ee) &&
-             need(p + "ffn_up_exps.weight", QXH_IQ2_XS, 3, H, I, Ee) &&
-             need(p + "ffn_down_exps.weight", QXH_IQ3_XXS, 3, I, H, Ee);
+        ok = need(p + "attn_norm.weight", {QXH_F32}, 1, H, 0, 0) && need(p + "attn_q.weight", kAttnT, 2, H, Q, 0) &&
+             need(p + "attn_k.weight", kAttnT, 2, H, KV, 0) && need(p + "attn_v.weight", kAttnT, 2, H, KV, 0) &&
+             need(p + "attn_output.weight", kAttnT, 2, Q, H, 0) &&
+             need(p + "attn_q_norm.weight", {QXH_F32}, 1, dm.head_dim, 0, 0) &&
+             need(p + "attn_k_norm.weight", {QXH_F32}, 1, dm.head_dim, 0, 0) &&
+             need(p + "ffn_norm.weight", {QXH_F32}, 1, H, 0, 0) &&
+             need(p + "ffn_gate_inp.weight", {QXH_F32}, 2, H, Ee, 0) &&
+             need(p + "ffn_gate_exps.weight", kGateT, 3, H, I, Ee) && need(p + "ffn_up_exps.weight", kGateT, 3, H, I, Ee) &&
+             need(p + "ffn_down_exps.weight", kDownT, 3, I, H, Ee);
+        if (ok && by[p + "ffn_gate_exps.weight"]->ggml_type != by[p + "ffn_up_exps.weight"]->ggml_type) {
+            set_err(err, n, "gate and up experts must share one type: " + p);
+            ok = false;
+        }
     }
     if (!ok) return 0;
     if (o.flags & QX_CUDA_VERIFY_CHECKSUMS) {
@@ -294,6 +314,13 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         lw.gate = W(p + "ffn_gate_exps.weight");
         lw.up = W(p + "ffn_up_exps.weight");
         lw.down = W(p + "ffn_down_exps.weight");
+        lw.tq = (int)by[p + "attn_q.weight"]->ggml_type;
+        lw.tk = (int)by[p + "attn_k.weight"]->ggml_type;
+        lw.tv = (int)by[p + "attn_v.weight"]->ggml_type;
+        lw.to = (int)by[p + "attn_output.weight"]->ggml_type;
+        lw.tgate = (int)by[p + "ffn_gate_exps.weight"]->ggml_type;
+        lw.tup = (int)by[p + "ffn_up_exps.weight"]->ggml_type;
+        lw.tdown = (int)by[p + "ffn_down_exps.weight"]->ggml_type;
         E->layers.push_back(lw);
     }
 
@@ -365,6 +392,8 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     for (int i = 0; i < 512; ++i) for (int j = 0; j < 8; ++j) ht.iq2xs[i][j] = (float)T->iq2xs[i][j];
     for (int i = 0; i < 256; ++i) for (int j = 0; j < 4; ++j) ht.iq3xxs[i][j] = (float)T->iq3xxs[i][j];
     memcpy(ht.ksigns, T->ksigns, 128);
+    for (int i = 0; i < 1024; ++i) memcpy(ht.iq2s[i], T->iq2s[i], 8);
+    for (int i = 0; i < 512; ++i) memcpy(&ht.iq3s[i], T->iq3s[i], 4);
     static const int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
     for (int i = 0; i < 16; ++i) ht.kvalues[i] = (float)kv[i];
     std::vector<double> rope(C * (D / 2) * 2);
@@ -386,7 +415,9 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         ce = cudaHostAlloc((void**)&E->h_stage, E->h_stage_bytes, cudaHostAllocDefault);
     }
     if (ce != cudaSuccess) return fail(ce, "cudaHostAlloc");
-    if (!(o.flags & QX_CUDA_PER_STAGE) && qx::mega_setup(dev, dm, &E->mega_grid)) {
+    // the one-launch kernel covers the benchmark mix; any other mix runs per stage
+    if (!(o.flags & QX_CUDA_PER_STAGE) && qx::benchmark_mix(E->layers.data(), dm.layers) &&
+        qx::mega_setup(dev, dm, &E->mega_grid)) {
         ce = cudaMalloc((void**)&E->layers_dev, E->layers.size() * sizeof(LayerW));
         if (ce == cudaSuccess)
             ce = cudaMemcpy(E->layers_dev, E->layers.data(), E->layers.size() * sizeof(LayerW), cudaMemcpyHostToDevice);
@@ -659,7 +690,7 @@ QX_API int qx_cuda_attention_layer(qx_cuda_engine* E, uint32_t layer, uint32_t p
     qx::launch_qkv(E->dev, w, E->stream);
     qx::launch_attn(E->dev, w, (int)layer, E->stream);
     qx::launch_oproj(E->dev, w, E->stream);
-    E->prof.kernel_launches += 2 + qx::attn_launches(E->dm);
+    E->prof.kernel_launches += 1 + qx::qkv_launches(w) + qx::attn_launches(E->dm);
     if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
     if (!d2h(E, residual, E->dev.x, (size_t)E->dm.hidden * 4, err, n) ||
         !d2h(E, attn_out, E->dev.attn_out, (size_t)E->dm.hidden * 4, err, n) ||

@@ -358,6 +358,8 @@ static double grid_msq(uint32_t type) {
     double s = 0.0;
     if (type == QXH_IQ2_XS) { for (int i = 0; i < 512; ++i) for (int j = 0; j < 8; ++j) s += T->iq2xs[i][j] * (double)T->iq2xs[i][j]; return s / 4096.0; }
     if (type == QXH_IQ3_XXS) { for (int i = 0; i < 256; ++i) for (int j = 0; j < 4; ++j) s += T->iq3xxs[i][j] * (double)T->iq3xxs[i][j]; return s / 1024.0; }
+    if (type == QXH_IQ2_S) { for (int i = 0; i < 1024; ++i) for (int j = 0; j < 8; ++j) s += T->iq2s[i][j] * (double)T->iq2s[i][j]; return s / 8192.0; }
+    if (type == QXH_IQ3_S) { for (int i = 0; i < 512; ++i) for (int j = 0; j < 4; ++j) s += T->iq3s[i][j] * (double)T->iq3s[i][j]; return s / 2048.0; }
     return 1.0;
 }
 
@@ -367,6 +369,9 @@ static double unit_gain_scale(uint32_t type, uint64_t fan_in) {
         case QXH_IQ4_XS: per = 341.5 * 4548.0; break;                   /* (ls-32)^2 * kvalues^2 */
         case QXH_IQ2_XS: per = (85.25 / 16.0) * grid_msq(type); break;  /* ((0.5+s)/4)^2 * g^2 */
         case QXH_IQ3_XXS: per = (85.25 / 4.0) * grid_msq(type); break;  /* ((0.5+s)/2)^2 * g^2 */
+        case QXH_IQ2_S: per = (85.25 / 16.0) * grid_msq(type); break;   /* ((0.5+s)/4)^2 * g^2 */
+        case QXH_IQ3_S: per = 341.0 * grid_msq(type); break;             /* (1+2s)^2 * g^2 */
+        case QXH_Q5_K: per = 1312.5 * 325.5; break;                      /* sc^2 * q^2 */
         case QXH_Q6_K: per = 1365.0 * 341.5; break;
         case QXH_Q4_K: per = 1312.5 * 77.5; break;
         default: break;
@@ -390,6 +395,7 @@ static int add_tensor(synth_plan *p, uint32_t cap, const char *name, uint32_t ty
     t->blocks = type == QXH_F32 ? (elems + 255u) / 256u : elems / bv;
     if (kind == K_QUANT) t->dscale = unit_gain_scale(type, d0);
     if (type == QXH_Q4_K) t->dmin_scale = 4.0 * t->dscale;
+    if (type == QXH_Q5_K) t->dmin_scale = 15.5 * t->dscale;   /* E[sc*q] = 15.5 E[m]: zero-mean weights */
     return 1;
 }
 
@@ -474,9 +480,10 @@ static void gen_block(const synth_tensor *t, uint64_t seed, uint32_t tindex, uin
             put16(dst + 208, half_abs_normal(&r, t->dscale));
             break;
         case QXH_Q4_K:         /* d, dmin, scales[12], qs[128] */
+        case QXH_Q5_K:         /* d, dmin, scales[12], qh[32], qs[128] */
             put16(dst, half_abs_normal(&r, t->dscale));
             put16(dst + 2, half_abs_normal(&r, t->dmin_scale));
-            fill_bytes(&r, dst + 4, 140);
+            fill_bytes(&r, dst + 4, t->block_bytes - 4u);
             break;
         default:               /* IQ2_XS/IQ3_XXS/IQ4_XS/...: d @0 then uniform payload */
             put16(dst, half_abs_normal(&r, t->dscale));

@@ -286,6 +286,109 @@ __device__ __forceinline__ void dot_iq3_xxs_mma(const uint8_t* r0, const uint8_t
     }
 }
 
+// IQ2_S (82-byte blocks: d, qs[32] low index bytes, signs[32], qh[8], scales[8];
+// src/qx_format.c:1961-1984): w = d/8 * (1+2s) * g * sign, g from the
+// 1024-entry lattice, index = qs[e] | (2 bits of qh).  Same lane mapping as
+// IQ2_XS: m16n8k16 per 16-value group, lane t takes half (t&1) of entry
+// 2gq + (t>>1).  grid: the lattice in global memory (read through L1).
+__device__ __forceinline__ void dot_iq2_s_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,
+                                              const uint32_t (*grid)[2], int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3, half = t & 1, sub = t >> 1;
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + b * 82;
+        const uint8_t* p1 = r1 + b * 82;
+        acc.zero_block();
+#pragma unroll 4
+        for (int gq = 0; gq < 16; ++gq) {
+            const int e = 2 * gq + sub, ib = e >> 2, l = e & 3;
+            const uint32_t i0 = p0[2 + e] | (((uint32_t)p0[66 + ib] << (8 - 2 * l)) & 0x300u);
+            const uint32_t i1 = p1[2 + e] | (((uint32_t)p1[66 + ib] << (8 - 2 * l)) & 0x300u);
+            const uint32_t a0 = signed_bytes(__ldg(&grid[i0][half]), (uint32_t)p0[34 + e] >> (4 * half));
+            const uint32_t a1 = signed_bytes(__ldg(&grid[i1][half]), (uint32_t)p1[34 + e] >> (4 * half));
+            const int sc0 = 1 + 2 * ((p0[74 + (gq >> 1)] >> (4 * (gq & 1))) & 15);
+            const int sc1 = 1 + 2 * ((p1[74 + (gq >> 1)] >> (4 * (gq & 1))) & 15);
+            int D[4];
+            mma_k16(D, a0, a1, x.b[(b * 16 + gq) * kXG + lane]);
+            acc.add(D, sc0, sc1);
+        }
+        const double sc = pow2d(-x.s[b] - 3);
+        acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
+    }
+}
+
+// IQ3_S (110-byte blocks: d, qs[64], qh[8], signs[32], scales[4];
+// src/qx_format.c:1987-2030): w = d * (1+2s) * g * sign, g from the 512-entry
+// lattice; in 32-value group ib the 4-value quad q has index qs[8ib+q] | bit q
+// of qh[ib] << 8 and sign nibble q&1 of signs[4ib + q/2]; s is nibble ib&1 of
+// scales[ib/2].  m16n8k32 per group, lane t: quads t and 4+t.
+__device__ __forceinline__ void dot_iq3_s_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,
+                                              const uint32_t* grid, int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3;
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + b * 110;
+        const uint8_t* p1 = r1 + b * 110;
+        acc.zero_block();
+#pragma unroll 2
+        for (int ib = 0; ib < 8; ++ib) {
+            uint32_t a[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {                 // a0: row 0 quad t, a1: row 1 quad t, a2/a3: quad 4+t
+                const uint8_t* p = (k & 1) ? p1 : p0;
+                const int q = (k >> 1) * 4 + t;
+                const uint32_t idx = p[2 + 8 * ib + q] | ((((uint32_t)p[66 + ib] >> q) & 1u) << 8);
+                a[k] = signed_bytes(__ldg(&grid[idx]), (uint32_t)p[74 + 4 * ib + (q >> 1)] >> (4 * (q & 1)));
+            }
+            const int s0 = 1 + 2 * ((p0[106 + (ib >> 1)] >> (4 * (ib & 1))) & 15);
+            const int s1 = 1 + 2 * ((p1[106 + (ib >> 1)] >> (4 * (ib & 1))) & 15);
+            const int G = b * 16 + 2 * ib;
+            int D[4];
+            mma_k32(D, a[0], a[1], a[2], a[3], x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
+            acc.add(D, s0, s1);
+        }
+        const double sc = pow2d(-x.s[b]);
+        acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
+    }
+}
+
+// Q5_K (176-byte blocks: d, dmin, scales[12], qh[32], qs[128];
+// src/qx_format.c:2112-2145): w = d*sc*q - dmin*m is affine, and the
+// subtraction rounds, so w is not an exact integer multiple: each weight is
+// decoded to the reference's float with the same operations (no contraction)
+// and multiplied into a double accumulator (the product is exact, the FMA
+// rounds like the reference's add).  One warp per row; lane l takes values
+// 64j+l and 64j+32+l of every block.  Returns the warp's double sum.
+__device__ __forceinline__ void q5k_scale_min(int j, const uint8_t* q, uint32_t& sc, uint32_t& m) {
+    if (j < 4) { sc = q[j] & 63u; m = q[j + 4] & 63u; }
+    else { sc = (q[j + 4] & 15u) | ((q[j - 4] >> 6) << 4); m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4); }
+}
+
+__device__ inline double dot_q5_k_row(const uint8_t* row, int nblk, const float* xs, int lane) {
+    double acc = 0.0;
+    for (int b = 0; b < nblk; ++b) {
+        const uint8_t* blk = row + (size_t)b * 176;
+        const float d = h2f(ld16(blk)), dmin = h2f(ld16(blk + 2));
+        const uint8_t qh = blk[16 + lane];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint8_t qv = blk[48 + 32 * j + lane];
+            uint32_t sc, m;
+            q5k_scale_min(2 * j, blk + 4, sc, m);
+            const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+            q5k_scale_min(2 * j + 1, blk + 4, sc, m);
+            const float d2 = __fmul_rn(d, (float)sc), m2 = __fmul_rn(dmin, (float)m);
+            const int qa = (qv & 15) | (((qh >> (2 * j)) & 1) << 4), qb = (qv >> 4) | (((qh >> (2 * j + 1)) & 1) << 4);
+            const float wa = __fsub_rn(__fmul_rn(d1, (float)qa), m1), wb = __fsub_rn(__fmul_rn(d2, (float)qb), m2);
+            const int ia = b * 256 + 64 * j + lane;
+            acc = fma((double)wa, (double)xs[ia], acc);
+            acc = fma((double)wb, (double)xs[ia + 32], acc);
+        }
+    }
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    return acc;
+}
+
 // Q6_K: m16n8k16 per 16-value scale group.  Values of a 128-value half:
 // pos = 32*s + l (section s, l in 0..31); lane t takes l = 16*lh + 4t .. +3.
 __device__ __forceinline__ uint32_t q6_word(uint32_t ql, uint32_t qh, int s) {

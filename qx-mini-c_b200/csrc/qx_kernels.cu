@@ -49,6 +49,12 @@ __global__ void __launch_bounds__(256) k_embed(Dev d) {
 // (qx_projection_matvec_fill_mode, src/qx_format.c:4207-4297; :6283-6290).
 // 2 tiles per CTA, 4 block-parts per tile.
 // ---------------------------------------------------------------------------
+// Bytes of one 256-value block of a ggml type on the decode path.
+constexpr uint32_t block_bytes(int fmt) {
+    return fmt == 17 ? 74u : fmt == 22 ? 82u : fmt == 18 ? 98u : fmt == 21 ? 110u : fmt == 23 ? 136u : fmt == 14 ? 210u
+                                                                                                           : 176u;
+}
+
 constexpr int kQkvTiles = 2;
 
 __global__ void __launch_bounds__(kThreads) k_qkv(Dev d, LayerW w) {
@@ -228,6 +234,90 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dev d, LayerW w) {
 }
 
 // ---------------------------------------------------------------------------
+// Projections of other quant types (per-stage path for mixes other than the
+// benchmark one).  k_proj: IQ4_XS (23) or Q6_K (14) rows of W [rows][K], two
+// 16-row tiles per CTA, exact integer tensor-core dots; input `in` is RMS-
+// normed with norm_w when given; residual != 0: the O projection epilogue
+// (attn_out = o, x += o), else out[row] = o.  k_proj_q5k: Q5_K rows, one warp
+// per row, weights decoded to the reference's floats, double FMA.
+// ---------------------------------------------------------------------------
+template <int FMT>
+__global__ void __launch_bounds__(kThreads) k_proj(Dev d, const float* in, const float* norm_w, const uint8_t* W,
+                                                   int rows, int K, float* out, int residual) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ double scratch[kWarps];
+    const int nblk = K / 256;
+    const uint32_t rb = (uint32_t)nblk * block_bytes(FMT), tb = (uint32_t)kTileRows * rb;
+    Carve cv(smem);
+    uint8_t* tiles = cv.take<uint8_t>(2 * tb);
+    float* xs = cv.take<float>(K);
+    uint32_t* xb = cv.take<uint32_t>(xq_words(K));
+    int* sb = cv.take<int>(K / 256);
+    double* part = cv.take<double>(kWarps * kTileRows);
+    const int ntiles = rows / kTileRows;
+    for (int k = 0; k < 2; ++k) {
+        const int t = blockIdx.x * 2 + k;
+        if (t < ntiles) stage_copy(tiles + k * tb, W + (size_t)t * tb, tb);
+    }
+    cp_async_commit();
+    uint32_t K4[4];
+    if (FMT == 23) load_kv_regs(d.tables, K4);
+    if (norm_w) rmsnorm_to_smem(in, norm_w, xs, K, scratch);
+    else copy_to_smem(in, xs, K);
+    build_xq(xs, K, xb, sb);
+    cp_async_wait<0>();
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+    const int parts = kWarps / 2, tile = warp / parts, p = warp % parts, t = blockIdx.x * 2 + tile;
+    if (t < ntiles) {
+        const uint8_t* base = tiles + tile * tb;
+        Acc acc{};
+        if (FMT == 23)
+            dot_iq4_xs_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, K4,
+                           lane, acc);
+        else
+            dot_q6_k_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, lane,
+                         acc);
+        store_tile_rows(part, warp, acc);
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 * kTileRows) {
+        const int tl = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows, tt = blockIdx.x * 2 + tl;
+        if (tt < ntiles) {
+            const int row = tt * kTileRows + r;
+            const float o = finite_or_zero_d(sum_parts(part, tl, parts, r));
+            if (residual) {
+                d.attn_out[row] = o;
+                d.x[row] = d.x[row] + o;
+            } else {
+                out[row] = o;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) k_proj_q5k(Dev d, const float* in, const float* norm_w, const uint8_t* W,
+                                                       int rows, int K, float* out, int residual) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ double scratch[kWarps];
+    float* xs = reinterpret_cast<float*>(smem);
+    if (norm_w) rmsnorm_to_smem(in, norm_w, xs, K, scratch);
+    else copy_to_smem(in, xs, K);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = blockIdx.x * kWarps + warp;
+    if (row >= rows) return;
+    const double v = dot_q5_k_row(W + (size_t)row * (K / 256) * 176, K / 256, xs, lane);
+    if (lane == 0) {
+        const float o = finite_or_zero_d(v);
+        if (residual) {
+            d.attn_out[row] = o;
+            d.x[row] = d.x[row] + o;
+        } else {
+            out[row] = o;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Router: FFN RMSNorm + F32 router matvec in double, softmax, top-8 by
 // repeated strict-> argmax (lowest index on ties), renormalisation
 // (qx_apply_real_moe_layer, src/qx_format.c:5250-5285).
@@ -325,11 +415,12 @@ __global__ void __launch_bounds__(kThreads) k_router(Dev d, LayerW w, int layer)
 // CTA = (expert rank, 16-row tile): tile 0 = gate rows, tile 1 = up rows;
 // 4 block-parts each.
 // ---------------------------------------------------------------------------
+template <int FMT>   // IQ2_XS (17) or IQ2_S (22)
 __global__ void __launch_bounds__(kThreads) k_gateup(Dev d, LayerW w, int layer) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int H = d.dm.hidden, I = d.dm.moe_inter;
     const int nblk = H / 256;
-    const uint32_t rb = (uint32_t)nblk * 74u, tb = (uint32_t)kTileRows * rb;
+    const uint32_t rb = (uint32_t)nblk * block_bytes(FMT), tb = (uint32_t)kTileRows * rb;
     Carve cv(smem);
     uint8_t* tiles = cv.take<uint8_t>(2 * tb);
     IqTab* T = cv.take<IqTab>(1);
@@ -343,7 +434,7 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dev d, LayerW w, int layer)
     stage_copy(tiles, w.gate + off, tb);
     stage_copy(tiles + tb, w.up + off, tb);
     cp_async_commit();
-    load_iq_tables(T, d.tables, true, false);
+    if (FMT == 17) load_iq_tables(T, d.tables, true, false);
     copy_to_smem(d.xn, xs, H);
     build_xq(xs, H, xb, sb);
     cp_async_wait<0>();
@@ -352,8 +443,12 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dev d, LayerW w, int layer)
     const int parts = kWarps / 2, tile = warp / parts, p = warp % parts;
     const uint8_t* base = tiles + tile * tb;
     Acc acc{};
-    dot_iq2_xs_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, *T, lane,
-                   acc);
+    if (FMT == 17)
+        dot_iq2_xs_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, *T,
+                       lane, acc);
+    else
+        dot_iq2_s_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb},
+                      d.tables->iq2s, lane, acc);
     store_tile_rows(part, warp, acc);
     __syncthreads();
     if (threadIdx.x < kTileRows) {
@@ -369,11 +464,12 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dev d, LayerW w, int layer)
 // and the residual add fused (:5298-5309).  CTA = rows [16c, 16c+16) of all 8
 // experts; warp k computes expert k on its own input h[k].
 // ---------------------------------------------------------------------------
+template <int FMT>   // IQ3_XXS (18), IQ3_S (21) or IQ4_XS (23)
 __global__ void __launch_bounds__(kThreads) k_down(Dev d, LayerW w, int layer) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int H = d.dm.hidden, I = d.dm.moe_inter;
     const int nblk = I / 256;
-    const uint32_t rb = (uint32_t)nblk * 98u, tb = (uint32_t)kTileRows * rb;
+    const uint32_t rb = (uint32_t)nblk * block_bytes(FMT), tb = (uint32_t)kTileRows * rb;
     Carve cv(smem);
     uint8_t* tiles = cv.take<uint8_t>(8 * tb);
     IqTab* T = cv.take<IqTab>(1);
@@ -385,7 +481,9 @@ __global__ void __launch_bounds__(kThreads) k_down(Dev d, LayerW w, int layer) {
     for (int k = 0; k < 8; ++k)
         stage_copy(tiles + k * tb, w.down + (size_t)d.sel[layer * 8 + k] * slice + (size_t)blockIdx.x * tb, tb);
     cp_async_commit();
-    load_iq_tables(T, d.tables, false, true);
+    uint32_t K4[4];
+    if (FMT == 18) load_iq_tables(T, d.tables, false, true);
+    if (FMT == 23) load_kv_regs(d.tables, K4);
     copy_to_smem(d.hbuf, hs, 8 * I);
     build_xq(hs, 8 * I, xb, sb);   // expert k's groups start at k * I / 16 (I % 256 == 0)
     cp_async_wait<0>();
@@ -393,8 +491,10 @@ __global__ void __launch_bounds__(kThreads) k_down(Dev d, LayerW w, int layer) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
     const uint8_t* base = tiles + warp * tb;
     Acc acc{};
-    dot_iq3_xxs_mma(base + g * rb, base + (g + 8) * rb, 0, nblk,
-                    XQ{xb + warp * xq_words(I), sb + warp * (I / 256)}, *T, lane, acc);
+    const XQ xw{xb + warp * xq_words(I), sb + warp * (I / 256)};
+    if (FMT == 18) dot_iq3_xxs_mma(base + g * rb, base + (g + 8) * rb, 0, nblk, xw, *T, lane, acc);
+    if (FMT == 21) dot_iq3_s_mma(base + g * rb, base + (g + 8) * rb, 0, nblk, xw, d.tables->iq3s, lane, acc);
+    if (FMT == 23) dot_iq4_xs_mma(base + g * rb, base + (g + 8) * rb, 0, nblk, xw, K4, lane, acc);
     store_tile_rows(part, warp, acc);
     __syncthreads();
     if (threadIdx.x < kTileRows) {
@@ -591,9 +691,12 @@ size_t part_bytes() { return a16((size_t)kWarps * kTileRows * 8); }
 size_t smem_qkv(const Dims& m) { return 16 + a16((size_t)kQkvTiles * kTileRows * (m.hidden / 256) * 136) + xq_bytes(m.hidden) + part_bytes(); }
 size_t smem_oproj(const Dims& m) { return 16 + a16((size_t)kTileRows * (m.q_dim() / 256) * 136) + xq_bytes(m.q_dim()) + part_bytes(); }
 size_t smem_router(const Dims& m) { return (size_t)m.hidden * 4; }
-size_t smem_gateup(const Dims& m) { return 16 + a16(2 * (size_t)kTileRows * (m.hidden / 256) * 74) + a16(sizeof(IqTab)) + xq_bytes(m.hidden) + part_bytes(); }
-size_t smem_down(const Dims& m) {
-    return 16 + a16(8 * (size_t)kTileRows * (m.moe_inter / 256) * 98) + a16(sizeof(IqTab)) + a16((size_t)8 * m.moe_inter * 4) +
+size_t smem_gateup(const Dims& m, uint32_t bb = 74) {
+    return 16 + a16(2 * (size_t)kTileRows * (m.hidden / 256) * bb) + a16(sizeof(IqTab)) + xq_bytes(m.hidden) + part_bytes();
+}
+size_t smem_proj(int K, uint32_t bb) { return 16 + a16(2 * (size_t)kTileRows * (K / 256) * bb) + xq_bytes(K) + part_bytes(); }
+size_t smem_down(const Dims& m, uint32_t bb = 136) {
+    return 16 + a16(8 * (size_t)kTileRows * (m.moe_inter / 256) * bb) + a16(sizeof(IqTab)) + a16((size_t)8 * m.moe_inter * 4) +
            a16(xq_words(8 * m.moe_inter) * 4) + a16((size_t)8 * m.moe_inter / 256 * 4) + part_bytes();
 }
 size_t smem_head(const Dims& m) {
@@ -615,8 +718,14 @@ cudaError_t configure_kernels() {
     set((const void*)k_qkv);
     set((const void*)k_oproj);
     set((const void*)k_router);
-    set((const void*)k_gateup);
-    set((const void*)k_down);
+    set((const void*)k_gateup<17>);
+    set((const void*)k_gateup<22>);
+    set((const void*)k_down<18>);
+    set((const void*)k_down<21>);
+    set((const void*)k_down<23>);
+    set((const void*)k_proj<23>);
+    set((const void*)k_proj<14>);
+    set((const void*)k_proj_q5k);
     set((const void*)k_head);
     set((const void*)k_final_norm);
     return e;
@@ -642,7 +751,34 @@ bool geometry_supported(const Dims& m) {
 
 void launch_embed(const Dev& d, cudaStream_t st) { k_embed<<<1, 256, 0, st>>>(d); }
 
+bool benchmark_mix(const LayerW* layers, int n) {
+    for (int l = 0; l < n; ++l) {
+        const LayerW& w = layers[l];
+        if (w.tq != 23 || w.tk != 23 || w.tv != 23 || w.to != 23 || w.tgate != 17 || w.tup != 17 || w.tdown != 18)
+            return false;
+    }
+    return true;
+}
+
+// One projection of any accepted attention type (rows of W, K inputs).
+static void launch_proj(const Dev& d, int type, const float* in, const float* norm_w, const uint8_t* W, int rows, int K,
+                        float* out, int residual, cudaStream_t st) {
+    const int grid2 = (rows / kTileRows + 1) / 2;
+    if (type == 23) k_proj<23><<<grid2, kThreads, smem_proj(K, 136), st>>>(d, in, norm_w, W, rows, K, out, residual);
+    else if (type == 14) k_proj<14><<<grid2, kThreads, smem_proj(K, 210), st>>>(d, in, norm_w, W, rows, K, out, residual);
+    else k_proj_q5k<<<(rows + kWarps - 1) / kWarps, kThreads, (size_t)K * 4, st>>>(d, in, norm_w, W, rows, K, out, residual);
+}
+
+int qkv_launches(const LayerW& w) { return w.tq == 23 && w.tk == 23 && w.tv == 23 ? 1 : 3; }
+
 void launch_qkv(const Dev& d, const LayerW& w, cudaStream_t st) {
+    if (qkv_launches(w) == 3) {                 // another mix: one launch per tensor
+        const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
+        launch_proj(d, w.tq, d.x, w.attn_norm, w.wq, Q, H, d.qkv, 0, st);
+        launch_proj(d, w.tk, d.x, w.attn_norm, w.wk, KV, H, d.qkv + Q, 0, st);
+        launch_proj(d, w.tv, d.x, w.attn_norm, w.wv, KV, H, d.qkv + Q + KV, 0, st);
+        return;
+    }
     const int nt = (d.dm.q_dim() + 2 * d.dm.kv_dim()) / kTileRows;
     k_qkv<<<(nt + kQkvTiles - 1) / kQkvTiles, kThreads, smem_qkv(d.dm), st>>>(d, w);
 }
@@ -663,6 +799,10 @@ void launch_attn(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
 }
 
 void launch_oproj(const Dev& d, const LayerW& w, cudaStream_t st) {
+    if (w.to != 23) {
+        launch_proj(d, w.to, d.ctxv, nullptr, w.wo, d.dm.hidden, d.dm.q_dim(), nullptr, 1, st);
+        return;
+    }
     k_oproj<<<d.dm.hidden / kTileRows, kThreads, smem_oproj(d.dm), st>>>(d, w);
 }
 
@@ -672,11 +812,16 @@ void launch_router(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
 }
 
 void launch_gateup(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
-    k_gateup<<<8 * d.dm.moe_inter / kTileRows, kThreads, smem_gateup(d.dm), st>>>(d, w, layer);
+    const int grid = 8 * d.dm.moe_inter / kTileRows;
+    if (w.tgate == 22) k_gateup<22><<<grid, kThreads, smem_gateup(d.dm, 82), st>>>(d, w, layer);
+    else k_gateup<17><<<grid, kThreads, smem_gateup(d.dm, 74), st>>>(d, w, layer);
 }
 
 void launch_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
-    k_down<<<d.dm.hidden / kTileRows, kThreads, smem_down(d.dm), st>>>(d, w, layer);
+    const int grid = d.dm.hidden / kTileRows;
+    if (w.tdown == 21) k_down<21><<<grid, kThreads, smem_down(d.dm, 110), st>>>(d, w, layer);
+    else if (w.tdown == 23) k_down<23><<<grid, kThreads, smem_down(d.dm, 136), st>>>(d, w, layer);
+    else k_down<18><<<grid, kThreads, smem_down(d.dm, 98), st>>>(d, w, layer);
 }
 
 void launch_head(const Dev& d, cudaStream_t st) { k_head<<<d.head_grid, kThreads, smem_head(d.dm), st>>>(d); }

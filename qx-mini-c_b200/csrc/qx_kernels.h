@@ -22,7 +22,15 @@ struct LayerW {                  // device pointers into the weight arena (nativ
     const uint8_t* gate;         // IQ2_XS [E][I rows][H]
     const uint8_t* up;           // IQ2_XS [E][I rows][H]
     const uint8_t* down;         // IQ3_XXS [E][H rows][I]
+    // ggml types of the quantized tensors: the benchmark mix is IQ4_XS (23)
+    // attention, IQ2_XS (17) gate/up, IQ3_XXS (18) down; the per-stage kernels
+    // also take Q5_K (13) / Q6_K (14) attention, IQ2_S (22) gate/up and
+    // IQ3_S (21) / IQ4_XS (23) down
+    int tq, tk, tv, to, tgate, tup, tdown;
 };
+
+// True when every layer uses the benchmark mix (the one-launch kernel's types).
+bool benchmark_mix(const LayerW* layers, int n);
 
 struct Dims {
     int layers, hidden, q_heads, kv_heads, head_dim, vocab, experts, moe_inter, ctx;
@@ -115,6 +123,7 @@ int mega_setup(int device, const Dims& m, int* grid_out);
 // Stand-alone two-phase attention (the one-launch kernel's attention code, qx_mega.cu).
 bool attn2_supported(const Dims& m);
 int attn_launches(const Dims& m);             // kernels launch_attn starts (1 or 2)
+int qkv_launches(const LayerW& w);            // kernels launch_qkv starts (1, or 3 for other mixes)
 cudaError_t attn2_configure();
 void launch_attn2(const Dev& d, const LayerW& w, int layer, int sms, cudaStream_t st);
 cudaError_t launch_decode_step(const Dev& d, const LayerW* layers_dev, int grid, cudaStream_t st);
