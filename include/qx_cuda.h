@@ -54,6 +54,11 @@ typedef struct qx_cuda_model {
 #define QX_CUDA_VERIFY_CHECKSUMS 0x1u   /* verify FNV checksums of every tensor once, at create */
 #define QX_CUDA_NO_GRAPH         0x2u   /* launch kernels one by one instead of replaying a CUDA graph */
 #define QX_CUDA_PER_STAGE        0x4u   /* decode with one kernel per stage instead of the one-launch step kernel */
+/* The reference's --activation q8_k_compat (src/qx_format.c:3869-4205):
+ * activations of the attention projections, experts and head quantized to
+ * Q8_K, exact int32 block sums, float epilogues in the reference's order.
+ * Runs on the per-stage kernels; not with expert parallelism. */
+#define QX_CUDA_Q8K_COMPAT       0x8u
 
 typedef struct qx_cuda_options {
     int32_t device;            /* CUDA ordinal; -1 = current device */

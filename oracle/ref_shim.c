@@ -17,6 +17,11 @@
 
 #define QXREF_API __attribute__((visibility("default")))
 
+/* Activation format of every projection / expert / head call below:
+ * "f32" (default) or "q8_k_compat" (src/qx_format.c:3869-4205). */
+static const char *g_activation = "f32";
+QXREF_API void qxref_set_activation(int q8_k_compat) { g_activation = q8_k_compat ? "q8_k_compat" : "f32"; }
+
 typedef struct qxref_model {
     qx_file file;
     int in_memory;
@@ -99,7 +104,7 @@ QXREF_API int qxref_final_head(qxref_model *m, const float *residual, float *nor
                                uint32_t top_n, uint32_t *top_tokens, double *top_logits, char *err, uint64_t err_len) {
     qx_real_head_result result;
     uint32_t hidden = m->file.header.manifest.hidden;
-    if (!qx_compute_real_final_head(&m->file, residual, normalized, hidden, top_n, "f32", "baseline", "serial", 1u,
+    if (!qx_compute_real_final_head(&m->file, residual, normalized, hidden, top_n, g_activation, "baseline", "serial", 1u,
                                     "scalar", logits, m->file.header.manifest.vocab, &result, err, err_len)) return 0;
     for (uint32_t i = 0; i < result.top_n && top_tokens; ++i) {
         top_tokens[i] = result.top[i].token;
@@ -115,7 +120,7 @@ QXREF_API int qxref_moe_layer(qxref_model *m, uint32_t layer, const float *resid
     uint32_t g = 0, u = 0, d = 0;
     double l2 = 0.0;
     return qx_apply_real_moe_layer(&m->file, layer, residual_after_attention, m->file.header.manifest.hidden,
-                                   layer_output, moe_output, selected, weights, &g, &u, &d, "f32", NULL, &l2,
+                                   layer_output, moe_output, selected, weights, &g, &u, &d, g_activation, NULL, &l2,
                                    err, err_len);
 }
 
@@ -170,9 +175,9 @@ QXREF_API int qxref_attention_layer(qxref_model *m, uint32_t layer, uint32_t ste
     uint64_t vals = 0;
     if (ok) ok = qx_apply_f32_rmsnorm(file, an, residual, normed, hidden, NULL, err, err_len);
     if (ok) ok = qx_projection_matvec_fill_mode(file, kt, kbuf, kfloat, kv_values, hidden, normed, hidden, 0u, layer,
-                                                1u + step * 17u, "f32", &pw, &probe, &vals, err, err_len);
+                                                1u + step * 17u, g_activation, &pw, &probe, &vals, err, err_len);
     if (ok) ok = qx_projection_matvec_fill_mode(file, vt, vbuf, vfloat, kv_values, hidden, normed, hidden, 0u, layer,
-                                                (1u ^ 0x9e3779b9u) + step * 17u, "f32", &pw, &probe, &vals, err, err_len);
+                                                (1u ^ 0x9e3779b9u) + step * 17u, g_activation, &pw, &probe, &vals, err, err_len);
     if (ok) ok = qx_apply_f32_head_rmsnorm(file, kn, kfloat, kv_heads, head_dim, err, err_len);
     if (ok) {
         qx_apply_rope(kfloat, kv_heads, head_dim, step, 1000000.0);
@@ -195,7 +200,7 @@ QXREF_API int qxref_attention_layer(qxref_model *m, uint32_t layer, uint32_t ste
         ok = qx_rope_gqa_attention_partial(file, layer, step, ctx, kv_values, (const unsigned char *)kcache,
                                            (const unsigned char *)vcache, kv_values, 1u, kscales, vscales, normed,
                                            hidden, q_heads, kv_heads, head_dim, 0u, 1u, out_vec, ctx_capture,
-                                           q_heads * head_dim, &s, &smin, &smax, &qrun, &qv, &qn, &on, "f32", &pw,
+                                           q_heads * head_dim, &s, &smin, &smax, &qrun, &qv, &qn, &on, g_activation, &pw,
                                            NULL, err, err_len);
     }
     if (ok) {

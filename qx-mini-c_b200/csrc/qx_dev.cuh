@@ -12,7 +12,12 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kTileRows = 16;          // rows per staged tile (16*row_bytes is 16-byte aligned for every format)
 
 // Error bits written to Dev::err (read by the host after each call).
-enum : int { kErrToken = 1, kErrPosition = 2, kErrNonFinite = 4, kErrRouter = 8, kErrTimeout = 16 };
+enum : int {
+    kErrToken = 1, kErrPosition = 2, kErrNonFinite = 4, kErrRouter = 8, kErrTimeout = 16,
+    kErrQ8Input = 32,     // q8_k_compat: non-finite activation
+    kErrQ8Expert = 64,    // q8_k_compat: non-finite expert output
+    kErrQ8Head = 128      // q8_k_compat: non-finite logit
+};
 
 // Lattice / codebook tables, built on the host (qx_host.c) and uploaded once.
 struct Tables {

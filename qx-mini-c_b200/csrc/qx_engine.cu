@@ -85,7 +85,7 @@ size_t stage_launches(const qx_cuda_engine* E) {
     size_t k = 0;
     for (const Op& op : E->ops)
         k += op.kind == kAttn ? (size_t)qx::attn_launches(E->dm)
-             : op.kind == kQkv ? (size_t)qx::qkv_launches(E->layers[op.layer]) : 1u;
+             : op.kind == kQkv ? (size_t)qx::qkv_launches(E->dev, E->layers[op.layer]) : 1u;
     return k;
 }
 
@@ -416,7 +416,13 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     }
     if (ce != cudaSuccess) return fail(ce, "cudaHostAlloc");
     // the one-launch kernel covers the benchmark mix; any other mix runs per stage
-    if (!(o.flags & QX_CUDA_PER_STAGE) && qx::benchmark_mix(E->layers.data(), dm.layers) &&
+    d.q8 = (o.flags & QX_CUDA_Q8K_COMPAT) ? 1 : 0;
+    if (d.q8 && o.ep_world > 1) {
+        set_err(err, n, "q8_k_compat runs on the per-stage path, without expert parallelism");
+        qx_cuda_engine_destroy(E);
+        return 0;
+    }
+    if (!(o.flags & QX_CUDA_PER_STAGE) && !d.q8 && qx::benchmark_mix(E->layers.data(), dm.layers) &&
         qx::mega_setup(dev, dm, &E->mega_grid)) {
         ce = cudaMalloc((void**)&E->layers_dev, E->layers.size() * sizeof(LayerW));
         if (ce == cudaSuccess)
@@ -536,6 +542,9 @@ bool finish(qx_cuda_engine* E, char* err, uint64_t n) {
     if (bits & qx::kErrNonFinite) { set_err(err, n, "non-finite final logit"); return false; }
     if (bits & qx::kErrRouter) { set_err(err, n, "invalid selected router weights"); return false; }
     if (bits & qx::kErrTimeout) { set_err(err, n, "device grid barrier timed out"); return false; }
+    if (bits & qx::kErrQ8Input) { set_err(err, n, "Q8_K activation contains NaN or Inf"); return false; }
+    if (bits & qx::kErrQ8Expert) { set_err(err, n, "non-finite packed expert Q8_K output"); return false; }
+    if (bits & qx::kErrQ8Head) { set_err(err, n, "non-finite final Q6_K Q8_K logit"); return false; }
     return true;
 }
 
@@ -690,7 +699,7 @@ QX_API int qx_cuda_attention_layer(qx_cuda_engine* E, uint32_t layer, uint32_t p
     qx::launch_qkv(E->dev, w, E->stream);
     qx::launch_attn(E->dev, w, (int)layer, E->stream);
     qx::launch_oproj(E->dev, w, E->stream);
-    E->prof.kernel_launches += 1 + qx::qkv_launches(w) + qx::attn_launches(E->dm);
+    E->prof.kernel_launches += 1 + qx::qkv_launches(E->dev, w) + qx::attn_launches(E->dm);
     if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
     if (!d2h(E, residual, E->dev.x, (size_t)E->dm.hidden * 4, err, n) ||
         !d2h(E, attn_out, E->dev.attn_out, (size_t)E->dm.hidden * 4, err, n) ||

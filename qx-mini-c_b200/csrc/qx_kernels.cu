@@ -715,6 +715,7 @@ cudaError_t configure_kernels() {
             e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)a.sharedSizeBytes);
     };
     if (e == cudaSuccess) e = attn2_configure();
+    if (e == cudaSuccess) e = q8_configure();
     set((const void*)k_qkv);
     set((const void*)k_oproj);
     set((const void*)k_router);
@@ -769,10 +770,17 @@ static void launch_proj(const Dev& d, int type, const float* in, const float* no
     else k_proj_q5k<<<(rows + kWarps - 1) / kWarps, kThreads, (size_t)K * 4, st>>>(d, in, norm_w, W, rows, K, out, residual);
 }
 
-int qkv_launches(const LayerW& w) { return w.tq == 23 && w.tk == 23 && w.tv == 23 ? 1 : 3; }
+int qkv_launches(const Dev& d, const LayerW& w) { return !d.q8 && w.tq == 23 && w.tk == 23 && w.tv == 23 ? 1 : 3; }
 
 void launch_qkv(const Dev& d, const LayerW& w, cudaStream_t st) {
-    if (qkv_launches(w) == 3) {                 // another mix: one launch per tensor
+    if (d.q8) {
+        const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
+        launch_q8_proj(d, w.tq, d.x, w.attn_norm, w.wq, Q, H, d.qkv, 0, st);
+        launch_q8_proj(d, w.tk, d.x, w.attn_norm, w.wk, KV, H, d.qkv + Q, 0, st);
+        launch_q8_proj(d, w.tv, d.x, w.attn_norm, w.wv, KV, H, d.qkv + Q + KV, 0, st);
+        return;
+    }
+    if (qkv_launches(d, w) == 3) {              // another mix: one launch per tensor
         const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
         launch_proj(d, w.tq, d.x, w.attn_norm, w.wq, Q, H, d.qkv, 0, st);
         launch_proj(d, w.tk, d.x, w.attn_norm, w.wk, KV, H, d.qkv + Q, 0, st);
@@ -799,6 +807,10 @@ void launch_attn(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
 }
 
 void launch_oproj(const Dev& d, const LayerW& w, cudaStream_t st) {
+    if (d.q8) {
+        launch_q8_proj(d, w.to, d.ctxv, nullptr, w.wo, d.dm.hidden, d.dm.q_dim(), nullptr, 1, st);
+        return;
+    }
     if (w.to != 23) {
         launch_proj(d, w.to, d.ctxv, nullptr, w.wo, d.dm.hidden, d.dm.q_dim(), nullptr, 1, st);
         return;
@@ -812,19 +824,24 @@ void launch_router(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
 }
 
 void launch_gateup(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
+    if (d.q8) { launch_q8_gateup(d, w, layer, st); return; }
     const int grid = 8 * d.dm.moe_inter / kTileRows;
     if (w.tgate == 22) k_gateup<22><<<grid, kThreads, smem_gateup(d.dm, 82), st>>>(d, w, layer);
     else k_gateup<17><<<grid, kThreads, smem_gateup(d.dm, 74), st>>>(d, w, layer);
 }
 
 void launch_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
+    if (d.q8) { launch_q8_down(d, w, layer, st); return; }
     const int grid = d.dm.hidden / kTileRows;
     if (w.tdown == 21) k_down<21><<<grid, kThreads, smem_down(d.dm, 110), st>>>(d, w, layer);
     else if (w.tdown == 23) k_down<23><<<grid, kThreads, smem_down(d.dm, 136), st>>>(d, w, layer);
     else k_down<18><<<grid, kThreads, smem_down(d.dm, 98), st>>>(d, w, layer);
 }
 
-void launch_head(const Dev& d, cudaStream_t st) { k_head<<<d.head_grid, kThreads, smem_head(d.dm), st>>>(d); }
+void launch_head(const Dev& d, cudaStream_t st) {
+    if (d.q8) launch_q8_head(d, st);
+    else k_head<<<d.head_grid, kThreads, smem_head(d.dm), st>>>(d);
+}
 
 void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st) {
     k_final_norm<<<1, 256, (size_t)d.dm.hidden * 4, st>>>(d, normalized);

@@ -64,6 +64,7 @@ struct Dev {
     float* hbuf;                 // SwiGLU outputs [8][I]
     float* logits;               // [V]
     double* logits_d;            // optional [V]: the head's double logits (top-N of the stage entry point)
+    int q8;                      // 1: q8_k_compat activations (per-stage kernels, qx_q8k.cu)
     double* best_val;            // per-CTA argmax partials (double logits, as the reference compares)
     int* best_idx;
     unsigned* counters;          // ticket counters for last-CTA reductions
@@ -123,7 +124,14 @@ int mega_setup(int device, const Dims& m, int* grid_out);
 // Stand-alone two-phase attention (the one-launch kernel's attention code, qx_mega.cu).
 bool attn2_supported(const Dims& m);
 int attn_launches(const Dims& m);             // kernels launch_attn starts (1 or 2)
-int qkv_launches(const LayerW& w);            // kernels launch_qkv starts (1, or 3 for other mixes)
+int qkv_launches(const Dev& d, const LayerW& w);   // kernels launch_qkv starts (1, or 3 for other mixes / q8)
+// q8_k_compat kernels (qx_q8k.cu)
+cudaError_t q8_configure();
+void launch_q8_proj(const Dev& d, int type, const float* in, const float* norm_w, const uint8_t* W, int rows, int K,
+                    float* out, int residual, cudaStream_t st);
+void launch_q8_gateup(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
+void launch_q8_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st);
+void launch_q8_head(const Dev& d, cudaStream_t st);
 cudaError_t attn2_configure();
 void launch_attn2(const Dev& d, const LayerW& w, int layer, int sms, cudaStream_t st);
 cudaError_t launch_decode_step(const Dev& d, const LayerW* layers_dev, int grid, cudaStream_t st);
