@@ -11,6 +11,9 @@
 #include <string>
 #include <unordered_map>
 #include <initializer_list>
+#include <thread>
+#include <atomic>
+#include <algorithm>
 #include <vector>
 
 #include "qx_cuda.h"
@@ -254,10 +257,28 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     }
     if (!ok) return 0;
     if (o.flags & QX_CUDA_VERIFY_CHECKSUMS) {
-        for (const auto& nm : names) {
-            const qx_cuda_tensor* t = by[nm];
-            if (qxh_fnv1a64(t->data, t->byte_size) != t->checksum) { set_err(err, n, "tensor checksum mismatch: " + nm); return 0; }
-        }
+        // FNV-1a is sequential within a tensor, independent across tensors:
+        // verify on every host core, largest tensors first; report the first
+        // mismatch in directory order
+        std::vector<const qx_cuda_tensor*> tp(names.size());   // resolved here: the workers only read
+        for (size_t i = 0; i < names.size(); ++i) tp[i] = by[names[i]];
+        std::vector<size_t> order(names.size());
+        for (size_t i = 0; i < order.size(); ++i) order[i] = i;
+        std::sort(order.begin(), order.end(), [&](size_t a, size_t b) { return tp[a]->byte_size > tp[b]->byte_size; });
+        std::vector<char> bad(names.size(), 0);
+        std::atomic<size_t> next{0};
+        const unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+        std::vector<std::thread> pool;
+        for (unsigned k = 0; k < nt; ++k)
+            pool.emplace_back([&]() {
+                for (size_t j; (j = next.fetch_add(1)) < order.size();) {
+                    const qx_cuda_tensor* t = tp[order[j]];
+                    bad[order[j]] = qxh_fnv1a64(t->data, t->byte_size) != t->checksum;
+                }
+            });
+        for (auto& th : pool) th.join();
+        for (size_t i = 0; i < names.size(); ++i)
+            if (bad[i]) { set_err(err, n, "tensor checksum mismatch: " + names[i]); return 0; }
     }
 
     auto* E = new qx_cuda_engine();
@@ -292,11 +313,43 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     E->weight_bytes = wb;
     ce = cudaMalloc(&E->weights, wb);
     if (ce != cudaSuccess) return fail(ce, "cudaMalloc(weights)");
-    for (const auto& nm : names) {
-        ce = cudaMemcpyAsync((uint8_t*)E->weights + off[nm], by[nm]->data, by[nm]->byte_size, cudaMemcpyHostToDevice,
-                             E->stream);
-        if (ce != cudaSuccess) return fail(ce, "cudaMemcpy(weights)");
-        E->prof.host_to_device_bytes += by[nm]->byte_size;
+    {
+        // two pinned staging buffers: the host copy of chunk i+1 (4 threads)
+        // overlaps the DMA of chunk i
+        const size_t kChunk = (size_t)64 << 20;
+        uint8_t* pin[2] = {nullptr, nullptr};
+        cudaEvent_t done[2] = {nullptr, nullptr};
+        ce = cudaHostAlloc((void**)&pin[0], 2 * kChunk, cudaHostAllocDefault);
+        if (ce == cudaSuccess) { pin[1] = pin[0] + kChunk; ce = cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming); }
+        if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming);
+        int slot = 0;
+        bool used[2] = {false, false};
+        for (size_t i = 0; ce == cudaSuccess && i < names.size(); ++i) {
+            const qx_cuda_tensor* t = by[names[i]];
+            for (size_t pos = 0; ce == cudaSuccess && pos < t->byte_size; pos += kChunk) {
+                const size_t len = std::min(kChunk, (size_t)t->byte_size - pos);
+                if (used[slot]) ce = cudaEventSynchronize(done[slot]);     // its previous DMA is finished
+                if (ce != cudaSuccess) break;
+                const uint8_t* src = static_cast<const uint8_t*>(t->data) + pos;
+                const size_t part = (len + 3) / 4;
+                std::thread cp[4];
+                for (int k = 0; k < 4; ++k) {
+                    const size_t a = std::min(len, k * part), b = std::min(len, (k + 1) * part);
+                    cp[k] = std::thread([=]() { if (b > a) memcpy(pin[slot] + a, src + a, b - a); });
+                }
+                for (auto& th : cp) th.join();
+                ce = cudaMemcpyAsync((uint8_t*)E->weights + off[names[i]] + pos, pin[slot], len, cudaMemcpyHostToDevice,
+                                     E->stream);
+                if (ce == cudaSuccess) ce = cudaEventRecord(done[slot], E->stream);
+                used[slot] = true;
+                slot ^= 1;
+            }
+            E->prof.host_to_device_bytes += t->byte_size;
+        }
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
+        for (auto ev : done) if (ev) cudaEventDestroy(ev);
+        if (pin[0]) cudaFreeHost(pin[0]);
+        if (ce != cudaSuccess) return fail(ce, "upload weights");
     }
     auto W = [&](const std::string& nm) { return (const uint8_t*)E->weights + off[nm]; };
     for (int l = 0; l < dm.layers; ++l) {
