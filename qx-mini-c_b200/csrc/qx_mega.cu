@@ -63,16 +63,23 @@ __device__ __forceinline__ void mark(const Dev& d, unsigned epoch, int k) {
 // kBarrierTimeoutNs (or kSpinLimit polls); then it sets kErrTimeout and
 // returns, and every later barrier returns at once when it sees that flag, so
 // a broken step ends quickly with an error the host reports.
-__device__ __forceinline__ void grid_sync(unsigned* bar, unsigned& epoch, unsigned& nsync, const Dev& d) {
-    int* err = d.err;
-    unsigned long long* trace = d.trace;
+__device__ __forceinline__ void grid_arrive(unsigned* bar, unsigned& epoch, unsigned& nsync, const Dev& d) {
     __syncthreads();
     epoch += 1;
     nsync += 1;
     if (threadIdx.x == 0) {
-        if (trace) trace[9 * trace_n(d) + (size_t)epoch * gridDim.x + blockIdx.x] = global_ns();
+        if (d.trace) d.trace[9 * trace_n(d) + (size_t)epoch * gridDim.x + blockIdx.x] = global_ns();
         // the CTA's writes are ordered before this release by the bar.sync above
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+    }
+}
+
+// Second half of a split barrier: between grid_arrive and grid_wait a CTA may
+// only do work that touches its own shared memory (or issues cp.async reads of
+// data that no CTA writes in the current phase).
+__device__ __forceinline__ void grid_wait(unsigned* bar, unsigned epoch, unsigned nsync, const Dev& d) {
+    int* err = d.err;
+    if (threadIdx.x == 0) {
         const unsigned target = nsync * gridDim.x;
         const unsigned long long t0 = global_ns();
         for (long long it = 0; ld_acquire(bar) < target; ++it) {
@@ -84,9 +91,14 @@ __device__ __forceinline__ void grid_sync(unsigned* bar, unsigned& epoch, unsign
                 }
             }
         }
-        if (trace && blockIdx.x == 0) trace[epoch] = global_ns();
+        if (d.trace && blockIdx.x == 0) d.trace[epoch] = global_ns();
     }
     __syncthreads();
+}
+
+__device__ __forceinline__ void grid_sync(unsigned* bar, unsigned& epoch, unsigned& nsync, const Dev& d) {
+    grid_arrive(bar, epoch, nsync, d);
+    grid_wait(bar, epoch, nsync, d);
 }
 
 // Advance the barrier numbering without synchronising (a phase that is
@@ -572,9 +584,9 @@ __device__ void issue_attn_fused(const Dev& d, const LayerW& w, int layer, int p
 }
 
 // The fused phase.  The staged group must be the second most recent
-// cp.async group once the router copies are issued here.
-__device__ void attn_fused(const Dev& d, const LayerW& w, int layer, int pos, AttnSmem& S, const FusedStage& f,
-                           float* prod, uint8_t* router_buf, uint32_t norm, unsigned epoch) {
+// cp.async group (the router rows follow it).
+__device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const FusedStage& f, float* prod,
+                           unsigned epoch) {
     const int D = 128, SW = D / kCtxSlices, KVH = d.dm.kv_heads, group = d.dm.q_heads / KVH;
     const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx, i = threadIdx.x;
     const int warp = i >> 5, lane = i & 31, item = blockIdx.x, T = pos + 1;
@@ -589,8 +601,6 @@ __device__ void attn_fused(const Dev& d, const LayerW& w, int layer, int pos, At
         if (i < D) qf[i] = d.qkv[h * D + i];
     }
     __syncthreads();
-    issue_router(d, w, router_buf, norm);
-    cp_async_commit();
     if (!active) return;
     cp_async_wait<1>();
     __syncthreads();
@@ -651,37 +661,100 @@ __device__ void attn_fused(const Dev& d, const LayerW& w, int layer, int pos, At
 }
 
 // Router softmax + top-8 over the logits in global memory (every CTA; the
-// result is identical everywhere).  sel/w in shared memory.  The reference
-// picks the 8 largest probabilities one at a time, ties to the lower expert
-// index (src/qx_format.c:5272-5285); the same list comes from ranking every
-// expert by (probability descending, index ascending) in parallel.
-__device__ void top8(const Dev& d, int layer, int* sel, double* wsel, double* probs, double* scratch) {
-    const int E = d.dm.experts, t = threadIdx.x;
-    const double lg = t < E ? d.router_logits[t] : -1.0e300;
-    const double m = block_max_d(lg, scratch);
-    const double ex = t < E ? exp(lg - m) : 0.0;
-    const double den = block_sum_d(ex, scratch);
-    const double p = t < E ? ex / den : -1.0;
-    // probabilities are >= 0, so their bit patterns order like the values:
-    // rank with integer compares (a NaN makes the weight sum NaN, which is
-    // reported as an error whatever the order)
-    long long* pb = reinterpret_cast<long long*>(probs);
-    const long long key = __double_as_longlong(p);
-    pb[t] = key;
-    __syncthreads();
-    if (t < E) {
-        int rank = 0;
-        for (int u = 0; u < E; ++u) {
-            const long long q = pb[u];
-            rank += (q > key) | ((q == key) & (u < t));
+// result is identical everywhere).  The reference picks the 8 largest
+// probabilities one at a time, ties to the lower expert index
+// (src/qx_format.c:5272-5285); the same list comes from ranking every expert
+// by (probability descending, index ascending).
+//
+// Warp 0 runs the softmax with shuffles only (each lane holds experts
+// lane + 32j); the operations are the same in every CTA, so the bits are too.  Probabilities are >= 0, so their bit patterns order like
+// the values and ranks come from integer compares.  The fast ranks count only
+// strictly larger keys; equal keys share a rank, which leaves one of the eight
+// slots empty or doubly filled, and then the exact (key, index) ranking runs.
+// A NaN makes the weight sum NaN, reported as an error in top8_weights.
+__device__ __forceinline__ int key_slot(int u) { return u + 2 * (u >> 5); }   // 32-key chunks on distinct banks
+
+__device__ void top8_select(const Dev& d, int* sel, double* wsel, long long* keys, int* cnt) {
+    const int E = d.dm.experts, t = threadIdx.x, lane = t & 31;
+    if (t < 32) {                                 // warp 0: softmax, lane holds experts lane + 32j
+        double lg[8], ex[8];
+        double m = -1.0e300;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane + 32 * j;
+            lg[j] = e < E ? __ldcg(d.router_logits + e) : -1.0e300;
+            m = fmax(m, lg[j]);
         }
-        if (rank < 8) {
-            sel[rank] = t;
-            wsel[rank] = p;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+        double den = 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            ex[j] = 0.0;
+            if (32 * j < E) {
+                const int e = lane + 32 * j;
+                ex[j] = e < E ? exp(lg[j] - m) : 0.0;
+                den += ex[j];
+            }
         }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane + 32 * j;
+            if (e < E) keys[key_slot(e)] = __double_as_longlong(ex[j] / den);
+        }
+        if (t == 0) cnt[0] = cnt[1] = 0;
     }
     __syncthreads();
-    if (t < 8) {                                  // same sum order on each of the 8 threads
+    // P adjacent threads per expert, each over a contiguous chunk of candidates
+    const int P = E <= kMT / 4 ? 4 : (E <= kMT / 2 ? 2 : 1);
+    const int e = t / P, q = t % P, chunk = (E + P - 1) / P;
+    const long long ke = e < E ? keys[key_slot(e)] : 0;
+    int rank = 0;
+    if (e < E) {
+        if (E == 128) {
+            const longlong2* kp = reinterpret_cast<const longlong2*>(keys + key_slot(32 * q));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const longlong2 v = kp[i];
+                rank += (v.x > ke) + (v.y > ke);
+            }
+        } else {
+            for (int u = q * chunk; u < min(E, (q + 1) * chunk); ++u) rank += keys[key_slot(u)] > ke;
+        }
+    }
+    if (P >= 2) rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+    if (P >= 4) rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+    if (e < E && q == 0 && rank < 8) {
+        sel[rank] = e;
+        wsel[rank] = __longlong_as_double(ke);
+        atomicAdd(cnt, 1);
+        atomicOr(cnt + 1, 1 << rank);
+    }
+    __syncthreads();
+    if (cnt[0] != 8 || cnt[1] != 0xff) {          // equal probabilities near the top: exact ranks
+        rank = 0;
+        if (e < E)
+            for (int u = q; u < E; u += P) {
+                const long long k2 = keys[key_slot(u)];
+                rank += (k2 > ke) | ((k2 == ke) & (u < e));
+            }
+        if (P >= 2) rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+        if (P >= 4) rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+        if (e < E && q == 0 && rank < 8) {
+            sel[rank] = e;
+            wsel[rank] = __longlong_as_double(ke);
+        }
+        __syncthreads();
+    }
+}
+
+// Normalise the 8 selected probabilities (rank-order sum, :5287); CTA 0
+// records the selection.  Readers of wsel sync before they read it.
+__device__ void top8_weights(const Dev& d, int layer, const int* sel, double* wsel) {
+    const int t = threadIdx.x;
+    if (t < 8) {
         double sum = 0.0;
         for (int k = 0; k < 8; ++k) sum += wsel[k];
         if (t == 0 && (!(sum > 0.0) || !isfinite(sum))) atomicOr(d.err, kErrRouter);
@@ -693,7 +766,6 @@ __device__ void top8(const Dev& d, int layer, int* sel, double* wsel, double* pr
             d.selw[layer * 8 + t] = (float)wk;
         }
     }
-    __syncthreads();
 }
 
 }  // namespace
@@ -701,7 +773,8 @@ __device__ void top8(const Dev& d, int layer, int* sel, double* wsel, double* pr
 __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __restrict__ layers, MegaLayout L) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ double scratch[kMW];
-    __shared__ double probs[kMT];
+    __shared__ __align__(16) double probs[kMT];
+    __shared__ int top_cnt[2];
     __shared__ double wsel[8];
     __shared__ int sel[8];
     __shared__ int own[8];
@@ -738,7 +811,13 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     const bool fused = pos + 1 <= fused_cap(L.sb - L.xb);
     const FusedStage fz = fused_stage(smem + L.xb, L.sb - L.xb);
     int qb = 0;
+    // cp.async groups: a buffer's next tiles are issued as soon as its last
+    // reader is done, mostly while the CTA waits at a grid barrier.  Order:
+    // QKV(l) at gate/up of l-1, O-proj(l) at down of l-1, attention staging and
+    // router(l) at QKV(l), gate/up(l) and down(l) after top-8.
     issue_qkv(d, layers[0], buf[qb], L.norm);
+    cp_async_commit();
+    issue_oproj(d, layers[0], buf[1 - qb]);
     cp_async_commit();
     // embedding (every CTA into its own xs; CTA 0 also writes the residual)
     {
@@ -765,7 +844,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         const LayerW& w = layers[layer];
         // ---------------- QKV (weights in buf[qb]) ----------------
         {
-            cp_async_wait<0>();                  // this phase's tiles and norm vector
+            cp_async_wait<1>();                  // this phase's tiles and norm vector (not O-proj's)
             if (layer > 0 && ep) {
                 ep_wait_layer(d, seqb, layer - 1);
                 ep_combine(d, layer - 1, xs);
@@ -784,13 +863,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             __syncthreads();
             mark(d, epoch, 0);
             build_xq(xs, H, xb, sb);
-            issue_oproj(d, w, buf[1 - qb]);
-            cp_async_commit();
             __syncthreads();
             mark(d, epoch, 1);
-            cp_async_wait<1>();
-            __syncthreads();
-            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(H / 256) * 136u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items((Q + 2 * KV) / kTileRows), nblk = H / 256;
             run_tasks<QXH_IQ4_XS_F>(buf[qb], tb, rb, mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
@@ -798,18 +872,21 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT)
                 d.qkv[item_id(r / kTileRows) * kTileRows + r % kTileRows] =
                     finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
+            grid_arrive(bar, epoch, nsync, d);
             if (fused) issue_attn_fused(d, w, layer, pos, fz);   // the activation region is free again
             cp_async_commit();
-            grid_sync(bar, epoch, nsync, d);
+            issue_router(d, w, buf[qb], L.norm);                  // the QKV tiles are consumed
+            cp_async_commit();
+            grid_wait(bar, epoch, nsync, d);
         }
         // ---------------- attention (CTAs 0..Hq-1) ----------------
         if (fused) {
-            attn_fused(d, w, layer, pos, attn, fz, reinterpret_cast<float*>(smem + L.xs), buf[qb], L.norm, epoch);
+            attn_fused(d, layer, pos, attn, fz, reinterpret_cast<float*>(smem + L.xs), epoch);
             skip_sync(epoch, d);
             grid_sync(bar, epoch, nsync, d);
         } else {
             const AttnStage stg = attn_stage(d, pos, smem + L.xb, L.sb - L.xb);
-            attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, buf[qb], L.norm, epoch);
+            attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, nullptr, 0, epoch);
             grid_sync(bar, epoch, nsync, d);
             attn_context(d, layer, pos, attn, reinterpret_cast<float*>(smem + L.xs), stg, epoch);
             grid_sync(bar, epoch, nsync, d);
@@ -873,16 +950,19 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 acc = block_sum_d(acc, scratch);
                 if (threadIdx.x == 0) d.router_logits[item_id(k)] = acc;
             }
-            grid_sync(bar, epoch, nsync, d);
+            grid_arrive(bar, epoch, nsync, d);
+            build_xq(xs, H, xb, sb);             // the FFN input for gate/up, while the grid gathers
+            grid_wait(bar, epoch, nsync, d);
         }
         // ---------------- top-8 + gate/up (weights in buf[1-qb]) ----------------
         {
-            top8(d, layer, sel, wsel, probs, scratch);
-            if (threadIdx.x == 0) {
-                int n = 0;
-                for (int k = 0; k < 8; ++k)
-                    if (sel[k] >= e0 && sel[k] < e1) own[n++] = k;
-                n_own_s = n;
+            top8_select(d, sel, wsel, reinterpret_cast<long long*>(probs), top_cnt);
+            if (threadIdx.x < 32) {              // the slots whose expert this rank owns, in rank order
+                const unsigned mine_mask =
+                    __ballot_sync(0xffffffffu, threadIdx.x < 8 && sel[threadIdx.x & 7] >= e0 && sel[threadIdx.x & 7] < e1);
+                if (threadIdx.x < 8 && ((mine_mask >> threadIdx.x) & 1u))
+                    own[__popc(mine_mask & ((1u << threadIdx.x) - 1u))] = threadIdx.x;
+                if (threadIdx.x == 0) n_own_s = __popc(mine_mask);
             }
             __syncthreads();
             const int n_own = n_own_s;
@@ -891,8 +971,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             cp_async_commit();
             issue_down(d, w, sel, own, n_own, buf[qb]);
             cp_async_commit();
-            build_xq(xs, H, xb, sb);            // xs still holds the FFN-normed input
-            __syncthreads();
+            top8_weights(d, layer, sel, wsel);  // read in the down phase, after several block syncs
             mark(d, epoch, 1);
             cp_async_wait<1>();
             __syncthreads();
@@ -909,7 +988,12 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const double gd = (double)gv;
                 d.hbuf[(it / tpe) * I + (it % tpe) * kTileRows + rr] = (float)(gd / (1.0 + exp(-gd)) * (double)uv);
             }
-            grid_sync(bar, epoch, nsync, d);
+            grid_arrive(bar, epoch, nsync, d);
+            // the gate/up buffer is free: next layer's QKV tiles (or the first head group)
+            if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm);
+            else if ((int)blockIdx.x < hg1 - hg0) issue_head_group(d, hg0 + blockIdx.x, buf[1 - qb]);
+            cp_async_commit();
+            grid_wait(bar, epoch, nsync, d);
         }
         // ---------------- down (weights in buf[qb]) ----------------
         {
@@ -917,9 +1001,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             copy_to_smem(d.hbuf, xs, n_own * I);
             mark(d, epoch, 0);
             build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
-            if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm);
-            else if ((int)blockIdx.x < hg1 - hg0) issue_head_group(d, hg0 + blockIdx.x, buf[1 - qb]);
-            cp_async_commit();
             __syncthreads();
             mark(d, epoch, 1);
             cp_async_wait<1>();
@@ -954,7 +1035,11 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 }
                 __threadfence_system();
             }
-            grid_sync(bar, epoch, nsync, d);
+            grid_arrive(bar, epoch, nsync, d);
+            // the down buffer is free: next layer's O-projection tiles
+            if (layer + 1 < m.layers) issue_oproj(d, layers[layer + 1], buf[qb]);
+            cp_async_commit();
+            grid_wait(bar, epoch, nsync, d);
             if (ep && blockIdx.x == 0 && threadIdx.x == 0) {   // every CTA's stores are ordered before the barrier
                 __threadfence_system();
                 for (int p = 0; p < d.ep_world; ++p)
