@@ -36,9 +36,20 @@ __device__ inline void rmsnorm_to_smem(const float* x, const float* w, float* xs
     __syncthreads();
 }
 
+// Global (L2) -> shared copy of n floats (n % 4 == 0, 16-byte aligned), all of
+// a thread's loads issued before its stores so the L2 round trips overlap.
 __device__ inline void copy_to_smem(const float* x, float* xs, int n) {
-    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
-        *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
+    constexpr int U = 2;
+    const int step = blockDim.x * 4;
+    for (int i0 = threadIdx.x * 4; i0 < n; i0 += U * step) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * step < n) v[u] = __ldcg(reinterpret_cast<const float4*>(x + i0 + u * step));
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * step < n) *reinterpret_cast<float4*>(xs + i0 + u * step) = v[u];
+    }
     __syncthreads();
 }
 
@@ -134,8 +145,8 @@ __device__ inline void head_norm_rope(float* v, const float* nw, const double* r
     if (i < 64) {
         const double c = rope[2 * i], s = rope[2 * i + 1];
         const float x0 = v[i], x1 = v[i + 64];
-        v[i] = (float)((double)x0 * c - (double)x1 * s);
-        v[i + 64] = (float)((double)x0 * s + (double)x1 * c);
+        v[i] = (float)__dsub_rn(__dmul_rn((double)x0, c), __dmul_rn((double)x1, s));   // no contraction
+        v[i + 64] = (float)__dadd_rn(__dmul_rn((double)x0, s), __dmul_rn((double)x1, c));
     }
     __syncthreads();
 }
@@ -171,10 +182,15 @@ __device__ __forceinline__ void warp_norm_rope(float* v, const float* nw, const 
         const int i = lane + 32 * k;
         const double c = rope[2 * i], s = rope[2 * i + 1];
         const float x0 = y[k], x1 = y[k + 2];
-        v[i] = (float)((double)x0 * c - (double)x1 * s);
-        v[i + 64] = (float)((double)x0 * s + (double)x1 * c);
+        v[i] = (float)__dsub_rn(__dmul_rn((double)x0, c), __dmul_rn((double)x1, s));   // no contraction
+        v[i + 64] = (float)__dadd_rn(__dmul_rn((double)x0, s), __dmul_rn((double)x1, c));
     }
 }
+
+// (float)k for an INT8 value, exactly, as one FP32 add instead of an integer
+// conversion: 1.5 * 2^23 + k has k in its last mantissa bits (ulp 1 there),
+// and subtracting 1.5 * 2^23 is exact (Sterbenz).  Valid for |k| < 2^22.
+__device__ __forceinline__ float i8_to_f32(int k) { return __fsub_rn(__int_as_float(0x4b400000 + k), 12582912.0f); }
 
 // Attention score of one cached INT8 key row (128 dims) against a query head
 // held as doubles: the dot product in dimension order in double, exactly as the
@@ -188,7 +204,7 @@ __device__ __forceinline__ double score_row(const double* qd, const int8_t* kp, 
         const int4 raw = *reinterpret_cast<const int4*>(kp + j);
         const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
 #pragma unroll
-        for (int u = 0; u < 16; ++u) s = fma(qd[j + u], (double)((float)kb[u] * ks), s);
+        for (int u = 0; u < 16; ++u) s = fma(qd[j + u], (double)(i8_to_f32(kb[u]) * ks), s);
     }
     s /= sqrt_d;
     return isfinite(s) ? s : 0.0;
@@ -203,7 +219,7 @@ __device__ __forceinline__ double score_row_sw(const double* qd, const int8_t* k
         const int4 raw = *reinterpret_cast<const int4*>(kp + 16 * (j ^ key));
         const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
 #pragma unroll
-        for (int u = 0; u < 16; ++u) s = fma(qd[16 * j + u], (double)((float)kb[u] * ks), s);
+        for (int u = 0; u < 16; ++u) s = fma(qd[16 * j + u], (double)(i8_to_f32(kb[u]) * ks), s);
     }
     s /= sqrt_d;
     return isfinite(s) ? s : 0.0;

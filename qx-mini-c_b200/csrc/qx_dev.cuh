@@ -195,6 +195,43 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
 }
 
+// ---- bulk copies on the copy engine ------------------------------------------
+// cp.async.bulk (no tensor map, no multicast): one instruction moves a
+// contiguous span global -> shared (both 16-byte aligned, size a multiple of
+// 16) and counts its bytes down on an mbarrier of this CTA.  A "group" is one
+// mbarrier phase: the issuing thread announces the group's byte total with
+// arrive.expect_tx, then issues the spans; the phase completes when all bytes
+// have landed, and every thread that waits on its parity sees them.
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// The group's byte total (one arrival of the issuing warp's lane 0).
+__device__ __forceinline__ void bulk_group_begin(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Each issuing thread: its earlier generic-proxy accesses of the destination
+// (made visible to it by a block barrier) come before the copy engine's writes.
+__device__ __forceinline__ void bulk_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Copy `bytes` (multiple of 16, both pointers 16-byte aligned) with the whole CTA.
 __device__ __forceinline__ void stage_copy(uint8_t* dst, const uint8_t* src, uint32_t bytes) {
     for (uint32_t c = threadIdx.x; c < bytes / 16u; c += blockDim.x) cp_async16(dst + 16u * c, src + 16u * c);

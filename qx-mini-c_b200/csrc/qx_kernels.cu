@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(128) k_attn(Dev d, LayerW w, int layer) {
     const int8_t* vbase = d.vcache + (size_t)layer * ctx * KV + g * D + i;
     const float* vsb = d.vscale + (size_t)layer * ctx;
     for (int t = 0; t < T; ++t) {
-        const float vv = t == pos ? (float)v8[g * D + i] * vsc : (float)vbase[(size_t)t * KV] * vsb[t];
+        const float vv = t == pos ? i8_to_f32(v8[g * D + i]) * vsc : i8_to_f32(vbase[(size_t)t * KV]) * vsb[t];
         acc += (float)(sc[t] * (double)vv);
     }
     d.ctxv[h * D + i] = acc;

@@ -142,60 +142,154 @@ __device__ __forceinline__ double tile_row(const double* part, int i, int nblk, 
     return v;
 }
 
-// ---- weight-tile issue per phase -------------------------------------------
-// The QKV and router groups also carry the layer's RMSNorm weights (H floats)
-// to offset `norm` of the buffer, behind every tile of those phases.
-__device__ void issue_qkv(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm) {
-    const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
-    stage_copy(buf + norm, reinterpret_cast<const uint8_t*>(w.attn_norm), (uint32_t)H * 4u);
-    const uint32_t rb = (uint32_t)(H / 256) * 136u, tb = (uint32_t)kTileRows * rb;
-    const int n = (Q + 2 * KV) / kTileRows, mine = my_items(n);
-    for (int k = 0; k < mine; ++k) {
-        const int r0 = item_id(k) * kTileRows;
-        const uint8_t* src = r0 < Q ? w.wq + (size_t)r0 * rb
-                             : r0 < Q + KV ? w.wk + (size_t)(r0 - Q) * rb
-                                           : w.wv + (size_t)(r0 - Q - KV) * rb;
-        stage_copy(buf + (size_t)k * tb, src, tb);
+// ---- weight-tile staging per phase -----------------------------------------
+// Each phase's weight tiles move as one bulk-copy group (qx_dev.cuh) into half
+// of a double buffer, completing on that group's mbarrier.  All threads call
+// the issue and wait functions (the bookkeeping is uniform); warp 1 issues the
+// copies (thread 0 spins on the grid barrier meanwhile): lane 0 announces the
+// group's bytes, then the lanes take the spans round-robin.
+//
+// IQ4_XS rows (1088 or 2176 bytes, 0 mod 64) are staged with a 16-byte gap
+// after each row: the 8 rows a warp reads at once then start in different
+// banks instead of the same ones.
+enum { kGQkv, kGOproj, kGRouter, kGGateup, kGDown, kGHead0, kGHead1, kGroups };
+constexpr int kIssueWarp = 1;
+constexpr uint32_t kRowPad = 16;
+
+struct Groups {
+    uint64_t* bar;       // kGroups mbarriers (static shared memory)
+    unsigned parity;     // bit g: parity of group g's next phase
+    unsigned pending;    // bit g: issued, not yet waited for
+    unsigned stuck;      // bit g: a wait gave up (error already reported)
+};
+
+// span(c, dst, src, bytes) describes copy c of `count`.
+template <class Span>
+__device__ __forceinline__ void issue_group(Groups& G, int g, uint32_t total, int count, Span span) {
+    G.pending |= 1u << g;
+    if ((int)(threadIdx.x >> 5) != kIssueWarp) return;
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) bulk_group_begin(G.bar + g, total);
+    __syncwarp();
+    bulk_fence();
+    for (int c = lane; c < count; c += 32) {
+        uint8_t* dst;
+        const void* src;
+        uint32_t bytes;
+        span(c, dst, src, bytes);
+        bulk_copy(dst, src, bytes, G.bar + g);
     }
 }
 
-__device__ void issue_oproj(const Dev& d, const LayerW& w, uint8_t* buf) {
-    const uint32_t rb = (uint32_t)(d.dm.q_dim() / 256) * 136u, tb = (uint32_t)kTileRows * rb;
-    const int mine = my_items(d.dm.hidden / kTileRows);
-    for (int k = 0; k < mine; ++k) stage_copy(buf + (size_t)k * tb, w.wo + (size_t)item_id(k) * tb, tb);
+// Wait for group g's bytes (bounded: after kBarrierTimeoutNs the error flag
+// is set and the wait returns; the group is then drained at kernel exit).
+__device__ void group_wait(Groups& G, int g, const Dev& d) {
+    if (!((G.pending >> g) & 1u)) return;
+    const unsigned par = (G.parity >> g) & 1u;
+    if (!mbar_try_wait(G.bar + g, par)) {
+        const unsigned long long t0 = global_ns();
+        while (!mbar_try_wait(G.bar + g, par)) {
+            if (global_ns() - t0 > kBarrierTimeoutNs) {
+                atomicOr(d.err, kErrTimeout);
+                G.stuck |= 1u << g;
+                break;
+            }
+        }
+    }
+    if (!((G.stuck >> g) & 1u)) G.parity ^= 1u << g;
+    G.pending &= ~(1u << g);
 }
 
-__device__ void issue_router(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm) {
+// Kernel exit: no copy may still be writing this CTA's shared memory.
+__device__ void group_drain(Groups& G, const Dev& d) {
+    for (int g = 0; g < kGroups; ++g) {
+        if (((G.pending | G.stuck) >> g) & 1u) {
+            const unsigned par = (G.parity >> g) & 1u;
+            const unsigned long long t0 = global_ns();
+            while (!mbar_try_wait(G.bar + g, par) && global_ns() - t0 < kBarrierTimeoutNs) {
+            }
+        }
+    }
+}
+
+// The QKV and router groups also carry the layer's RMSNorm weights (H floats)
+// to offset `norm` of the buffer.  QKV tiles: padded rows (rb + kRowPad).
+__device__ void issue_qkv(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm, Groups& G) {
+    const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
+    const uint32_t rb = (uint32_t)(H / 256) * 136u, rbp = rb + kRowPad;
+    const int mine = my_items((Q + 2 * KV) / kTileRows);
+    issue_group(G, kGQkv, (uint32_t)H * 4u + (uint32_t)(mine * kTileRows) * rb, 1 + mine * kTileRows,
+                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+                    if (c == 0) {
+                        dst = buf + norm, src = w.attn_norm, bytes = (uint32_t)H * 4u;
+                        return;
+                    }
+                    const int k = (c - 1) / kTileRows, r = (c - 1) % kTileRows, r0 = item_id(k) * kTileRows + r;
+                    dst = buf + (size_t)(k * kTileRows + r) * rbp;
+                    src = r0 < Q ? w.wq + (size_t)r0 * rb
+                          : r0 < Q + KV ? w.wk + (size_t)(r0 - Q) * rb
+                                        : w.wv + (size_t)(r0 - Q - KV) * rb;
+                    bytes = rb;
+                });
+}
+
+__device__ void issue_oproj(const Dev& d, const LayerW& w, uint8_t* buf, Groups& G) {
+    const uint32_t rb = (uint32_t)(d.dm.q_dim() / 256) * 136u, rbp = rb + kRowPad;
+    const int mine = my_items(d.dm.hidden / kTileRows);
+    issue_group(G, kGOproj, (uint32_t)(mine * kTileRows) * rb, mine * kTileRows,
+                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+                    const int k = c / kTileRows, r = c % kTileRows;
+                    dst = buf + (size_t)c * rbp;
+                    src = w.wo + ((size_t)item_id(k) * kTileRows + r) * rb;
+                    bytes = rb;
+                });
+}
+
+__device__ void issue_router(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm, Groups& G) {
     const uint32_t rowb = (uint32_t)d.dm.hidden * 4u;
-    stage_copy(buf + norm, reinterpret_cast<const uint8_t*>(w.ffn_norm), rowb);
     const int mine = my_items(d.dm.experts);
-    for (int k = 0; k < mine; ++k)
-        stage_copy(buf + (size_t)k * rowb, reinterpret_cast<const uint8_t*>(w.router) + (size_t)item_id(k) * rowb, rowb);
+    issue_group(G, kGRouter, rowb * (uint32_t)(1 + mine), 1 + mine,
+                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+                    bytes = rowb;
+                    if (c == 0) {
+                        dst = buf + norm, src = w.ffn_norm;
+                        return;
+                    }
+                    dst = buf + (size_t)(c - 1) * rowb;
+                    src = reinterpret_cast<const uint8_t*>(w.router) + (size_t)item_id(c - 1) * rowb;
+                });
 }
 
 // own[0..n_own): the top-8 slots (rank order) whose expert this GPU computes
 // (all 8 on one GPU).
-__device__ void issue_gateup(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf) {
+__device__ void issue_gateup(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf,
+                             Groups& G) {
     const int H = d.dm.hidden, I = d.dm.moe_inter;
     const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
     const int tpe = I / kTileRows, mine = my_items(n_own * tpe);
-    for (int k = 0; k < mine; ++k) {
-        const int it = item_id(k), e = own[it / tpe], i0 = (it % tpe) * kTileRows;
-        const size_t off = (size_t)sel[e] * ((size_t)I * rb) + (size_t)i0 * rb;
-        stage_copy(buf + (size_t)(2 * k) * tb, w.gate + off, tb);
-        stage_copy(buf + (size_t)(2 * k + 1) * tb, w.up + off, tb);
-    }
+    issue_group(G, kGGateup, 2u * (uint32_t)mine * tb, 2 * mine,
+                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+                    const int it = item_id(c >> 1), e = own[it / tpe], i0 = (it % tpe) * kTileRows;
+                    const size_t off = (size_t)sel[e] * ((size_t)I * rb) + (size_t)i0 * rb;
+                    dst = buf + (size_t)c * tb;
+                    src = ((c & 1) ? w.up : w.gate) + off;
+                    bytes = tb;
+                });
 }
 
-__device__ void issue_down(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf) {
+__device__ void issue_down(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf,
+                           Groups& G) {
     const int H = d.dm.hidden, I = d.dm.moe_inter;
     const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
     const size_t slice = (size_t)H * rb;
     const int mine = my_items(H / kTileRows);
-    for (int k = 0; k < mine; ++k)
-        for (int j = 0; j < n_own; ++j)
-            stage_copy(buf + (size_t)(n_own * k + j) * tb, w.down + (size_t)sel[own[j]] * slice + (size_t)item_id(k) * tb,
-                       tb);
+    issue_group(G, kGDown, (uint32_t)(mine * n_own) * tb, mine * n_own,
+                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+                    const int k = c / max(n_own, 1), j = c % max(n_own, 1);
+                    dst = buf + (size_t)c * tb;
+                    src = w.down + (size_t)sel[own[j]] * slice + (size_t)item_id(k) * tb;
+                    bytes = tb;
+                });
 }
 
 // ---- expert-parallel exchange ------------------------------------------------
@@ -251,9 +345,12 @@ __device__ void ep_wait_layer(const Dev& d, unsigned seqb, int prev_layer) {
 
 constexpr int kHeadGroupTiles = 2;
 
-__device__ void issue_head_group(const Dev& d, int grp, uint8_t* buf) {
+// Head groups alternate between two mbarriers (ring of two buffers).
+__device__ void issue_head_group(const Dev& d, int grp, uint8_t* buf, Groups& G, int g) {
     const uint32_t rb = (uint32_t)(d.dm.hidden / 256) * 210u, stage = (uint32_t)kHeadGroupTiles * kTileRows * rb;
-    stage_copy(buf, d.head + (size_t)grp * stage, stage);
+    issue_group(G, g, stage, 1, [&](int, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+        dst = buf, src = d.head + (size_t)grp * stage, bytes = stage;
+    });
 }
 
 // ---- attention over every CTA ---------------------------------------------
@@ -380,7 +477,7 @@ __device__ float context_chain(int T, const double* w_s, float* prod, VV vv) {
 // scratch of group * kQdStride doubles.  The staged group must be the second
 // most recent cp.async group.
 __device__ void attn_scores(const Dev& d, const LayerW& w, int layer, int pos, AttnSmem& S, double* qd,
-                            const AttnStage& st, uint8_t* router_buf, uint32_t norm, unsigned epoch) {
+                            const AttnStage& st, unsigned epoch) {
     const int D = 128, KVH = d.dm.kv_heads, group = d.dm.q_heads / KVH;
     const int Q = d.dm.q_dim(), KV = d.dm.kv_dim(), ctx = d.dm.ctx, i = threadIdx.x;
     const int warp = i >> 5, lane = i & 31, cpg = attn_cpg(d);
@@ -396,14 +493,12 @@ __device__ void attn_scores(const Dev& d, const LayerW& w, int layer, int pos, A
     }
     __syncthreads();
     mark(d, epoch, 3);
-    // the staging and router copies start once the phase's inputs are in, so
-    // they do not queue ahead of those loads
+    // the staging copies start once the phase's inputs are in, so they do not
+    // queue ahead of those loads
     issue_attn_scores(d, w, layer, pos, st);
     cp_async_commit();
-    if (router_buf) issue_router(d, w, router_buf, norm);   // none in the stand-alone kernel
-    cp_async_commit();
     if (!active) return;
-    cp_async_wait<1>();
+    cp_async_wait<0>();
     __syncthreads();
     mark(d, epoch, 4);
     for (int hh = warp; hh < KVH + group; hh += kMW) {
@@ -505,7 +600,7 @@ __device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, floa
         const int vcap = staged ? st.vcap : 0;
         __syncthreads();
         const float acc = context_chain(T, w_s, prod, [&](int t, int dd) {
-            return t < vcap ? (float)st.vrows[t * SW + dd] * st.vscl[t] : (float)vb[(size_t)t * KV + dd] * vs[t];
+            return t < vcap ? i8_to_f32(st.vrows[t * SW + dd]) * st.vscl[t] : i8_to_f32(vb[(size_t)t * KV + dd]) * vs[t];
         });
         if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
         mark(d, epoch, 1);
@@ -602,22 +697,37 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
     }
     __syncthreads();
     if (!active) return;
-    cp_async_wait<1>();
+    cp_async_wait<0>();
     __syncthreads();
     mark(d, epoch, 3);
-    if (warp <= KVH) {
-        if (warp < KVH) warp_norm_rope(S.kcur + warp * D, f.kn, f.rope, lane);
-        else warp_norm_rope(qf, f.qn, f.rope, lane);
+    // one warp per head: K heads (RMSNorm + RoPE, then max |k|), V heads
+    // (max |v|), the query head (RMSNorm + RoPE, widened to double); the
+    // row maxima (non-finite values count as 0) meet in S.sf[0..8) / [8..16)
+    for (int hh = warp; hh < 2 * KVH + 1; hh += kMW) {
+        if (hh < 2 * KVH) {
+            float* v = hh < KVH ? S.kcur + hh * D : S.vcur + (hh - KVH) * D;
+            if (hh < KVH) warp_norm_rope(v, f.kn, f.rope, lane);
+            float mx = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float e = v[lane + 32 * k];            // the lane's own dims (written by it above)
+                mx = fmaxf(mx, isfinite(e) ? fabsf(e) : 0.f);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) S.sf[hh < KVH ? hh : 8 + hh - KVH] = mx;
+        } else {
+            warp_norm_rope(qf, f.qn, f.rope, lane);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) f.qd[lane + 32 * k] = (double)qf[lane + 32 * k];
+        }
     }
     __syncthreads();
     float ka = 0.f, va = 0.f;
-    for (int j = i; j < KV; j += kMT) {
-        ka = fmaxf(ka, isfinite(S.kcur[j]) ? fabsf(S.kcur[j]) : 0.f);
-        va = fmaxf(va, isfinite(S.vcur[j]) ? fabsf(S.vcur[j]) : 0.f);
+    for (int k = 0; k < KVH; ++k) {
+        ka = fmaxf(ka, S.sf[k]);
+        va = fmaxf(va, S.sf[8 + k]);
     }
-    if (i < D) f.qd[i] = (double)qf[i];
-    ka = block_max_f(ka, S.sf);
-    va = block_max_f(va, S.sf);
     const float ksc = ka > 0.f ? ka / 127.0f : 1.0f, vsc = va > 0.f ? va / 127.0f : 1.0f;
     for (int j = i; j < KV; j += kMT) {
         const int qk = isfinite(S.kcur[j]) ? (int)lrintf(S.kcur[j] / ksc) : 0;
@@ -654,7 +764,7 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
     mark(d, epoch, 2);
     __syncthreads();
     const float acc = context_chain(T, f.w_s, prod, [&](int t, int dd) {
-        return t == pos ? (float)S.v8[g * D + sl * SW + dd] * vsc : (float)f.vrows[t * SW + dd] * f.vscl[t];
+        return t == pos ? i8_to_f32(S.v8[g * D + sl * SW + dd]) * vsc : i8_to_f32(f.vrows[t * SW + dd]) * f.vscl[t];
     });
     if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
     __syncthreads();
@@ -666,43 +776,42 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
 // (src/qx_format.c:5272-5285); the same list comes from ranking every expert
 // by (probability descending, index ascending).
 //
-// Warp 0 runs the softmax with shuffles only (each lane holds experts
-// lane + 32j); the operations are the same in every CTA, so the bits are too.  Probabilities are >= 0, so their bit patterns order like
-// the values and ranks come from integer compares.  The fast ranks count only
-// strictly larger keys; equal keys share a rank, which leaves one of the eight
-// slots empty or doubly filled, and then the exact (key, index) ranking runs.
-// A NaN makes the weight sum NaN, reported as an error in top8_weights.
-__device__ __forceinline__ int key_slot(int u) { return u + 2 * (u >> 5); }   // 32-key chunks on distinct banks
+// Softmax: thread e < E holds expert e; the first ceil(E/32) warps reduce
+// with shuffles and meet at a named barrier, in the same order in every CTA.
+// Probabilities are >= 0, so their bit patterns order like the values.  The
+// fast ranks compare only the upper 32 bits and count strictly larger keys;
+// equal upper halves share a rank, which leaves one of the eight slots empty
+// or doubly filled, and then the exact 64-bit (key, index) ranking runs.  A
+// NaN makes the weight sum NaN, reported as an error in top8_weights.
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
-__device__ void top8_select(const Dev& d, int* sel, double* wsel, long long* keys, int* cnt) {
-    const int E = d.dm.experts, t = threadIdx.x, lane = t & 31;
-    if (t < 32) {                                 // warp 0: softmax, lane holds experts lane + 32j
-        double lg[8], ex[8];
-        double m = -1.0e300;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = lane + 32 * j;
-            lg[j] = e < E ? __ldcg(d.router_logits + e) : -1.0e300;
-            m = fmax(m, lg[j]);
-        }
+__device__ void top8_select(const Dev& d, int* sel, double* wsel, long long* keys, double* red, int* cnt) {
+    const int E = d.dm.experts, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int sw = (E + 31) >> 5, st = sw * 32;       // softmax warps / threads
+    uint32_t* hk = reinterpret_cast<uint32_t*>(keys + kMT / 2);   // upper halves, after the full keys
+    if (t < st) {
+        const double lg = t < E ? __ldcg(d.router_logits + t) : -1.0e300;
+        double m = lg;
 #pragma unroll
         for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
-        double den = 0.0;
+        if (lane == 0) red[warp] = m;
+        named_sync(1, st);
+        m = red[0];
+        for (int k = 1; k < sw; ++k) m = fmax(m, red[k]);
+        const double ex = t < E ? exp(lg - m) : 0.0;
+        double s = ex;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            ex[j] = 0.0;
-            if (32 * j < E) {
-                const int e = lane + 32 * j;
-                ex[j] = e < E ? exp(lg[j] - m) : 0.0;
-                den += ex[j];
-            }
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E) keys[key_slot(e)] = __double_as_longlong(ex[j] / den);
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) red[8 + warp] = s;
+        named_sync(1, st);
+        double den = red[8];
+        for (int k = 1; k < sw; ++k) den += red[8 + k];
+        if (t < E) {
+            const long long key = __double_as_longlong(ex / den);
+            keys[t] = key;
+            hk[t] = (uint32_t)(key >> 32);
         }
         if (t == 0) cnt[0] = cnt[1] = 0;
     }
@@ -710,34 +819,35 @@ __device__ void top8_select(const Dev& d, int* sel, double* wsel, long long* key
     // P adjacent threads per expert, each over a contiguous chunk of candidates
     const int P = E <= kMT / 4 ? 4 : (E <= kMT / 2 ? 2 : 1);
     const int e = t / P, q = t % P, chunk = (E + P - 1) / P;
-    const long long ke = e < E ? keys[key_slot(e)] : 0;
+    const uint32_t he = e < E ? hk[e] : 0u;
     int rank = 0;
     if (e < E) {
         if (E == 128) {
-            const longlong2* kp = reinterpret_cast<const longlong2*>(keys + key_slot(32 * q));
+            const uint4* kp = reinterpret_cast<const uint4*>(hk + 32 * q);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const longlong2 v = kp[i];
-                rank += (v.x > ke) + (v.y > ke);
+            for (int i = 0; i < 8; ++i) {
+                const uint4 v = kp[(i + q) & 7];      // rotated start: the quad's loads hit different banks
+                rank += (v.x > he) + (v.y > he) + (v.z > he) + (v.w > he);
             }
         } else {
-            for (int u = q * chunk; u < min(E, (q + 1) * chunk); ++u) rank += keys[key_slot(u)] > ke;
+            for (int u = q * chunk; u < min(E, (q + 1) * chunk); ++u) rank += hk[u] > he;
         }
     }
     if (P >= 2) rank += __shfl_xor_sync(0xffffffffu, rank, 1);
     if (P >= 4) rank += __shfl_xor_sync(0xffffffffu, rank, 2);
     if (e < E && q == 0 && rank < 8) {
         sel[rank] = e;
-        wsel[rank] = __longlong_as_double(ke);
+        wsel[rank] = __longlong_as_double(keys[e]);
         atomicAdd(cnt, 1);
         atomicOr(cnt + 1, 1 << rank);
     }
     __syncthreads();
-    if (cnt[0] != 8 || cnt[1] != 0xff) {          // equal probabilities near the top: exact ranks
+    if (cnt[0] != 8 || cnt[1] != 0xff) {          // near-equal probabilities at the top: exact ranks
+        const long long ke = e < E ? keys[e] : 0;
         rank = 0;
         if (e < E)
             for (int u = q; u < E; u += P) {
-                const long long k2 = keys[key_slot(u)];
+                const long long k2 = keys[u];
                 rank += (k2 > ke) | ((k2 == ke) & (u < e));
             }
         if (P >= 2) rank += __shfl_xor_sync(0xffffffffu, rank, 1);
@@ -775,6 +885,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     __shared__ double scratch[kMW];
     __shared__ __align__(16) double probs[kMT];
     __shared__ int top_cnt[2];
+    __shared__ uint64_t gbar[kGroups];
     __shared__ double wsel[8];
     __shared__ int sel[8];
     __shared__ int own[8];
@@ -811,14 +922,19 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     const bool fused = pos + 1 <= fused_cap(L.sb - L.xb);
     const FusedStage fz = fused_stage(smem + L.xb, L.sb - L.xb);
     int qb = 0;
-    // cp.async groups: a buffer's next tiles are issued as soon as its last
-    // reader is done, mostly while the CTA waits at a grid barrier.  Order:
-    // QKV(l) at gate/up of l-1, O-proj(l) at down of l-1, attention staging and
-    // router(l) at QKV(l), gate/up(l) and down(l) after top-8.
-    issue_qkv(d, layers[0], buf[qb], L.norm);
-    cp_async_commit();
-    issue_oproj(d, layers[0], buf[1 - qb]);
-    cp_async_commit();
+    // Weight groups: each is issued once its buffer is free and early enough
+    // to land before use, but not ahead of the activation reads that start a
+    // phase (the fills share the SM's L2 path with them): down(l) at the end
+    // of gate/up(l), QKV(l+1) in down(l) after its input is read, O-proj(l) in
+    // QKV(l) after the norm, router(l) at the end of QKV(l), gate/up(l) after
+    // top-8.
+    Groups G{gbar, 0u, 0u, 0u};
+    if (threadIdx.x == 0) {
+        for (int g = 0; g < kGroups; ++g) mbar_init(gbar + g, 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    issue_qkv(d, layers[0], buf[qb], L.norm, G);
     // embedding (every CTA into its own xs; CTA 0 also writes the residual)
     {
         const int nblk = H / 256;
@@ -844,7 +960,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         const LayerW& w = layers[layer];
         // ---------------- QKV (weights in buf[qb]) ----------------
         {
-            cp_async_wait<1>();                  // this phase's tiles and norm vector (not O-proj's)
+            group_wait(G, kGQkv, d);             // this phase's tiles and norm vector
             if (layer > 0 && ep) {
                 ep_wait_layer(d, seqb, layer - 1);
                 ep_combine(d, layer - 1, xs);
@@ -862,10 +978,11 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
             __syncthreads();
             mark(d, epoch, 0);
+            issue_oproj(d, w, buf[1 - qb], G);  // the previous layer's down tiles are consumed
             build_xq(xs, H, xb, sb);
             __syncthreads();
             mark(d, epoch, 1);
-            const uint32_t rb = (uint32_t)(H / 256) * 136u, tb = (uint32_t)kTileRows * rb;
+            const uint32_t rb = (uint32_t)(H / 256) * 136u + kRowPad, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items((Q + 2 * KV) / kTileRows), nblk = H / 256;
             run_tasks<QXH_IQ4_XS_F>(buf[qb], tb, rb, mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
             mark(d, epoch, 3);
@@ -875,8 +992,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             grid_arrive(bar, epoch, nsync, d);
             if (fused) issue_attn_fused(d, w, layer, pos, fz);   // the activation region is free again
             cp_async_commit();
-            issue_router(d, w, buf[qb], L.norm);                  // the QKV tiles are consumed
-            cp_async_commit();
+            issue_router(d, w, buf[qb], L.norm, G);               // the QKV tiles are consumed
             grid_wait(bar, epoch, nsync, d);
         }
         // ---------------- attention (CTAs 0..Hq-1) ----------------
@@ -886,7 +1002,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             grid_sync(bar, epoch, nsync, d);
         } else {
             const AttnStage stg = attn_stage(d, pos, smem + L.xb, L.sb - L.xb);
-            attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, nullptr, 0, epoch);
+            attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + L.xs), stg, epoch);
             grid_sync(bar, epoch, nsync, d);
             attn_context(d, layer, pos, attn, reinterpret_cast<float*>(smem + L.xs), stg, epoch);
             grid_sync(bar, epoch, nsync, d);
@@ -898,10 +1014,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             build_xq(xs, Q, xb, sb);
             __syncthreads();
             mark(d, epoch, 1);
-            cp_async_wait<1>();
-            __syncthreads();
+            group_wait(G, kGOproj, d);
             mark(d, epoch, 2);
-            const uint32_t rb = (uint32_t)(Q / 256) * 136u, tb = (uint32_t)kTileRows * rb;
+            const uint32_t rb = (uint32_t)(Q / 256) * 136u + kRowPad, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = Q / 256;
             run_tasks<QXH_IQ4_XS_F>(buf[1 - qb], tb, rb, mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
             mark(d, epoch, 3);
@@ -922,7 +1037,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         }
         // ---------------- router (weights in buf[qb]) ----------------
         {
-            cp_async_wait<0>();                  // router rows and norm vector
+            group_wait(G, kGRouter, d);          // router rows and norm vector
             copy_to_smem(d.x, xs, H);
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
             double ss = 0.0;
@@ -934,7 +1049,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             if (blockIdx.x == 0)
                 for (int i = threadIdx.x; i < H; i += kMT) d.xn[i] = xs[i];
             mark(d, epoch, 0);
-            cp_async_wait<0>();
             __syncthreads();
             mark(d, epoch, 1);
             const int mine = my_items(E);
@@ -956,7 +1070,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         }
         // ---------------- top-8 + gate/up (weights in buf[1-qb]) ----------------
         {
-            top8_select(d, sel, wsel, reinterpret_cast<long long*>(probs), top_cnt);
+            top8_select(d, sel, wsel, reinterpret_cast<long long*>(probs), scratch, top_cnt);
             if (threadIdx.x < 32) {              // the slots whose expert this rank owns, in rank order
                 const unsigned mine_mask =
                     __ballot_sync(0xffffffffu, threadIdx.x < 8 && sel[threadIdx.x & 7] >= e0 && sel[threadIdx.x & 7] < e1);
@@ -967,14 +1081,10 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             __syncthreads();
             const int n_own = n_own_s;
             mark(d, epoch, 0);
-            issue_gateup(d, w, sel, own, n_own, buf[1 - qb]);
-            cp_async_commit();
-            issue_down(d, w, sel, own, n_own, buf[qb]);
-            cp_async_commit();
+            issue_gateup(d, w, sel, own, n_own, buf[1 - qb], G);
             top8_weights(d, layer, sel, wsel);  // read in the down phase, after several block syncs
             mark(d, epoch, 1);
-            cp_async_wait<1>();
-            __syncthreads();
+            group_wait(G, kGGateup, d);
             mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(n_own * (I / kTileRows)), nblk = H / 256;
@@ -989,10 +1099,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 d.hbuf[(it / tpe) * I + (it % tpe) * kTileRows + rr] = (float)(gd / (1.0 + exp(-gd)) * (double)uv);
             }
             grid_arrive(bar, epoch, nsync, d);
-            // the gate/up buffer is free: next layer's QKV tiles (or the first head group)
-            if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm);
-            else if ((int)blockIdx.x < hg1 - hg0) issue_head_group(d, hg0 + blockIdx.x, buf[1 - qb]);
-            cp_async_commit();
+            issue_down(d, w, sel, own, n_own, buf[qb], G);
             grid_wait(bar, epoch, nsync, d);
         }
         // ---------------- down (weights in buf[qb]) ----------------
@@ -1000,11 +1107,13 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             const int n_own = n_own_s;
             copy_to_smem(d.hbuf, xs, n_own * I);
             mark(d, epoch, 0);
+            // into the free gate/up buffer: next layer's QKV tiles (or the first head group)
+            if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm, G);
+            else if ((int)blockIdx.x < hg1 - hg0) issue_head_group(d, hg0 + blockIdx.x, buf[1 - qb], G, kGHead0);
             build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
             __syncthreads();
             mark(d, epoch, 1);
-            cp_async_wait<1>();
-            __syncthreads();
+            group_wait(G, kGDown, d);
             mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = I / 256;
@@ -1035,11 +1144,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 }
                 __threadfence_system();
             }
-            grid_arrive(bar, epoch, nsync, d);
-            // the down buffer is free: next layer's O-projection tiles
-            if (layer + 1 < m.layers) issue_oproj(d, layers[layer + 1], buf[qb]);
-            cp_async_commit();
-            grid_wait(bar, epoch, nsync, d);
+            grid_sync(bar, epoch, nsync, d);
             if (ep && blockIdx.x == 0 && threadIdx.x == 0) {   // every CTA's stores are ordered before the barrier
                 __threadfence_system();
                 for (int p = 0; p < d.ep_world; ++p)
@@ -1073,10 +1178,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         bool bad = false;
         for (int k = 0; k < mine; ++k) {
             uint8_t* cur = buf[(qb + k) & 1];
-            if (k + 1 < mine) issue_head_group(d, hg0 + item_id(k + 1), buf[(qb + k + 1) & 1]);
-            cp_async_commit();
-            cp_async_wait<1>();
-            __syncthreads();
+            if (k + 1 < mine) issue_head_group(d, hg0 + item_id(k + 1), buf[(qb + k + 1) & 1], G, kGHead0 + ((k + 1) & 1));
+            group_wait(G, kGHead0 + (k & 1), d);
             run_tasks<QXH_Q6_K_F>(cur, tb, rb, kHeadGroupTiles, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
             if (threadIdx.x < kHeadGroupTiles * kTileRows) {
                 const int i = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows;
@@ -1138,6 +1241,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             *d.pos = pos + 1;
         }
     }
+    group_drain(G, d);
 }
 
 // ---- the same two-phase attention as stand-alone kernels (per-stage path) ----
@@ -1156,7 +1260,7 @@ __global__ void __launch_bounds__(kMT, 1) k_attn_scores(Dev d, LayerW w, int lay
         return;
     }
     const AttnStage stg = attn_stage(d, pos, smem, kAttnStageBytes);
-    attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + kAttnStageBytes), stg, nullptr, 0, 0);
+    attn_scores(d, w, layer, pos, attn, reinterpret_cast<double*>(smem + kAttnStageBytes), stg, 0);
 }
 
 __global__ void __launch_bounds__(kMT, 1) k_attn_context(Dev d, int layer) {
@@ -1189,7 +1293,7 @@ static int mega_max_tasks(const Dims& m, int grid) {
 static MegaLayout mega_layout(const Dims& m, int grid) {
     auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
     const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter;
-    const size_t t_qkv = (size_t)kTileRows * (H / 256) * 136, t_o = (size_t)kTileRows * (Q / 256) * 136;
+    const size_t t_qkv = (size_t)kTileRows * ((H / 256) * 136 + kRowPad), t_o = (size_t)kTileRows * ((Q / 256) * 136 + kRowPad);
     const size_t t_gu = (size_t)kTileRows * (H / 256) * 74, t_dn = (size_t)kTileRows * (I / 256) * 98;
     const size_t t_hd = (size_t)kHeadGroupTiles * kTileRows * (H / 256) * 210;
     size_t bufb = 0;
@@ -1228,7 +1332,8 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
     if (L.total + a.sharedSizeBytes > (size_t)optin || !mega_tasks_fit(m, sms)) return 0;
     if ((size_t)m.ctx * 8 > L.sb - L.xb || (size_t)kVChunk * 132 > L.xb - L.xs) return 0;
     const int group = m.q_heads / m.kv_heads;
-    if (kMT % group || group * 128 > 8 * kMT || (size_t)group * kQdStride * 8 > L.xb - L.xs || sms < m.kv_heads)
+    if (kMT % group || group * 128 > 8 * kMT || (size_t)group * kQdStride * 8 > L.xb - L.xs || sms < m.kv_heads ||
+        m.kv_heads > 8)
         return 0;
     if (cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total) != cudaSuccess)
         return 0;
