@@ -116,13 +116,38 @@ __device__ __forceinline__ int item_id(int k) { return (int)blockIdx.x + k * (in
 
 // Run (tile, block) tasks over `ntile` staged 16-row tiles of row size rb with
 // nblk blocks; tile i uses activation xq[xsel(i)].  part[task][16] doubles.
+// Bounded wait on an mbarrier phase: gives up (error flag set) after
+// kBarrierTimeoutNs, or at once when another wait of the step timed out.
+__device__ __forceinline__ bool bounded_mbar_wait(uint64_t* bar, unsigned parity, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (int it = 0; !mbar_try_wait(bar, parity); ++it) {
+        if ((it & 15) == 15 && (*reinterpret_cast<volatile int*>(err) & kErrTimeout)) return false;
+        if (global_ns() - t0 > kBarrierTimeoutNs) {
+            atomicOr(err, kErrTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Tile i of a phase whose tiles each complete on their own mbarrier
+// (tbar[i], phase parity bit i of tpar): a warp waits only for the tile of
+// its current task, so work starts while later tiles are still landing.
+struct TileWait {
+    uint64_t* tbar;
+    unsigned tpar;
+    int* err;
+};
+
 template <int FMT, class XSel>
 __device__ void run_tasks(const uint8_t* tiles, uint32_t tb, uint32_t rb, int ntile, int nblk, XSel xsel,
-                          const uint32_t* K4, const IqTab* T, double* part) {
+                          const uint32_t* K4, const IqTab* T, double* part, TileWait tw = TileWait{nullptr, 0u, nullptr}) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
     const int ntask = ntile * nblk;
     for (int task = warp; task < ntask; task += kMW) {
         const int i = task / nblk, b = task % nblk;
+        if (tw.tbar) bounded_mbar_wait(tw.tbar + i, (tw.tpar >> i) & 1u, tw.err);
         const uint8_t* base = tiles + (size_t)i * tb;
         const XQ x = xsel(i);
         Acc acc{};
@@ -161,7 +186,34 @@ struct Groups {
     unsigned parity;     // bit g: parity of group g's next phase
     unsigned pending;    // bit g: issued, not yet waited for
     unsigned stuck;      // bit g: a wait gave up (error already reported)
+    uint64_t* tbar;      // kTileBars per-tile mbarriers: gate/up tiles at 0, down tiles at kTileBars / 2
+    unsigned tparity;    // bit i: parity of tile barrier i's next phase
+    unsigned tused;      // bit i: tile barrier i has been issued on
 };
+constexpr int kTileBars = 32;
+
+// One copy per tile, each completing on its own tile barrier base + c.
+template <class Span>
+__device__ __forceinline__ void issue_tiles(Groups& G, int base, int count, Span span) {
+    G.tused |= (count >= 32 ? 0xffffffffu : ((1u << count) - 1u)) << base;
+    if ((int)(threadIdx.x >> 5) != kIssueWarp) return;
+    bulk_fence();
+    for (int c = threadIdx.x & 31; c < count; c += 32) {
+        uint8_t* dst;
+        const void* src;
+        uint32_t bytes;
+        span(c, dst, src, bytes);
+        bulk_group_begin(G.tbar + base + c, bytes);
+        bulk_copy(dst, src, bytes, G.tbar + base + c);
+    }
+}
+__device__ __forceinline__ TileWait tile_waits(const Groups& G, int base, const Dev& d) {
+    return TileWait{G.tbar + base, G.tparity >> base, d.err};
+}
+// After the phase's run_tasks: every tile phase has completed (or timed out).
+__device__ __forceinline__ void tiles_done(Groups& G, int base, int count) {
+    G.tparity ^= (count >= 32 ? 0xffffffffu : ((1u << count) - 1u)) << base;
+}
 
 // span(c, dst, src, bytes) describes copy c of `count`.
 template <class Span>
@@ -186,27 +238,27 @@ __device__ __forceinline__ void issue_group(Groups& G, int g, uint32_t total, in
 __device__ void group_wait(Groups& G, int g, const Dev& d) {
     if (!((G.pending >> g) & 1u)) return;
     const unsigned par = (G.parity >> g) & 1u;
-    if (!mbar_try_wait(G.bar + g, par)) {
-        const unsigned long long t0 = global_ns();
-        while (!mbar_try_wait(G.bar + g, par)) {
-            if (global_ns() - t0 > kBarrierTimeoutNs) {
-                atomicOr(d.err, kErrTimeout);
-                G.stuck |= 1u << g;
-                break;
-            }
-        }
-    }
+    if (!bounded_mbar_wait(G.bar + g, par, d.err)) G.stuck |= 1u << g;
     if (!((G.stuck >> g) & 1u)) G.parity ^= 1u << g;
     G.pending &= ~(1u << g);
 }
 
-// Kernel exit: no copy may still be writing this CTA's shared memory.
+// Kernel exit: no copy may still be writing this CTA's shared memory.  A
+// tile barrier's last issued phase has parity (tparity bit) ^ 1.
 __device__ void group_drain(Groups& G, const Dev& d) {
     for (int g = 0; g < kGroups; ++g) {
         if (((G.pending | G.stuck) >> g) & 1u) {
             const unsigned par = (G.parity >> g) & 1u;
             const unsigned long long t0 = global_ns();
             while (!mbar_try_wait(G.bar + g, par) && global_ns() - t0 < kBarrierTimeoutNs) {
+            }
+        }
+    }
+    for (int i = 0; i < kTileBars; ++i) {
+        if ((G.tused >> i) & 1u) {
+            const unsigned par = ((G.tparity >> i) & 1u) ^ 1u;
+            const unsigned long long t0 = global_ns();
+            while (!mbar_try_wait(G.tbar + i, par) && global_ns() - t0 < kBarrierTimeoutNs) {
             }
         }
     }
@@ -267,8 +319,7 @@ __device__ void issue_gateup(const Dev& d, const LayerW& w, const int* sel, cons
     const int H = d.dm.hidden, I = d.dm.moe_inter;
     const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
     const int tpe = I / kTileRows, mine = my_items(n_own * tpe);
-    issue_group(G, kGGateup, 2u * (uint32_t)mine * tb, 2 * mine,
-                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+    issue_tiles(G, 0, 2 * mine, [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
                     const int it = item_id(c >> 1), e = own[it / tpe], i0 = (it % tpe) * kTileRows;
                     const size_t off = (size_t)sel[e] * ((size_t)I * rb) + (size_t)i0 * rb;
                     dst = buf + (size_t)c * tb;
@@ -283,8 +334,7 @@ __device__ void issue_down(const Dev& d, const LayerW& w, const int* sel, const 
     const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
     const size_t slice = (size_t)H * rb;
     const int mine = my_items(H / kTileRows);
-    issue_group(G, kGDown, (uint32_t)(mine * n_own) * tb, mine * n_own,
-                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+    issue_tiles(G, kTileBars / 2, mine * n_own, [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
                     const int k = c / max(n_own, 1), j = c % max(n_own, 1);
                     dst = buf + (size_t)c * tb;
                     src = w.down + (size_t)sel[own[j]] * slice + (size_t)item_id(k) * tb;
@@ -886,6 +936,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     __shared__ __align__(16) double probs[kMT];
     __shared__ int top_cnt[2];
     __shared__ uint64_t gbar[kGroups];
+    __shared__ uint64_t tbar_s[kTileBars];
     __shared__ double wsel[8];
     __shared__ int sel[8];
     __shared__ int own[8];
@@ -928,9 +979,10 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     // of gate/up(l), QKV(l+1) in down(l) after its input is read, O-proj(l) in
     // QKV(l) after the norm, router(l) at the end of QKV(l), gate/up(l) after
     // top-8.
-    Groups G{gbar, 0u, 0u, 0u};
+    Groups G{gbar, 0u, 0u, 0u, tbar_s, 0u, 0u};
     if (threadIdx.x == 0) {
         for (int g = 0; g < kGroups; ++g) mbar_init(gbar + g, 1);
+        for (int i = 0; i < kTileBars; ++i) mbar_init(tbar_s + i, 1);
         mbar_init_fence();
     }
     __syncthreads();
@@ -1084,11 +1136,12 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             issue_gateup(d, w, sel, own, n_own, buf[1 - qb], G);
             top8_weights(d, layer, sel, wsel);  // read in the down phase, after several block syncs
             mark(d, epoch, 1);
-            group_wait(G, kGGateup, d);
             mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(n_own * (I / kTileRows)), nblk = H / 256;
-            run_tasks<QXH_IQ2_XS_F>(buf[1 - qb], tb, rb, 2 * mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
+            run_tasks<QXH_IQ2_XS_F>(buf[1 - qb], tb, rb, 2 * mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part,
+                                    tile_waits(G, 0, d));
+            tiles_done(G, 0, 2 * mine);
             mark(d, epoch, 3);
             const int tpe = I / kTileRows;
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
@@ -1113,15 +1166,14 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
             __syncthreads();
             mark(d, epoch, 1);
-            group_wait(G, kGDown, d);
-            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = I / 256;
             run_tasks<QXH_IQ3_XXS_F>(buf[qb], tb, rb, n_own * mine, nblk,
                                      [&](int i) {
                                          return XQ{xb + (i % n_own) * xq_words(I), sb + (i % n_own) * (I / 256)};
                                      },
-                                     K4, T, part);
+                                     K4, T, part, tile_waits(G, kTileBars / 2, d));
+            tiles_done(G, kTileBars / 2, n_own * mine);
             mark(d, epoch, 3);
             if (!ep) {
                 for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
@@ -1335,6 +1387,9 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
     if (kMT % group || group * 128 > 8 * kMT || (size_t)group * kQdStride * 8 > L.xb - L.xs || sms < m.kv_heads ||
         m.kv_heads > 8)
         return 0;
+    auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
+    if (2 * cdiv(8 * (m.moe_inter / kTileRows), sms) > kTileBars / 2 || 8 * cdiv(m.hidden / kTileRows, sms) > kTileBars / 2)
+        return 0;                             // gate/up and down tiles of one CTA each fit half the tile barriers
     if (cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total) != cudaSuccess)
         return 0;
     int per = 0;
