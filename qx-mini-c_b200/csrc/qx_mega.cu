@@ -140,6 +140,12 @@ struct TileWait {
     int* err;
 };
 
+// Every tile uses the same activation (one run_tasks instantiation per format).
+struct SameXQ {
+    XQ x;
+    __device__ __forceinline__ XQ operator()(int) const { return x; }
+};
+
 template <int FMT, class XSel>
 __device__ void run_tasks(const uint8_t* tiles, uint32_t tb, uint32_t rb, int ntile, int nblk, XSel xsel,
                           const uint32_t* K4, const IqTab* T, double* part, TileWait tw = TileWait{nullptr, 0u, nullptr}) {
@@ -1036,7 +1042,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             mark(d, epoch, 1);
             const uint32_t rb = (uint32_t)(H / 256) * 136u + kRowPad, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items((Q + 2 * KV) / kTileRows), nblk = H / 256;
-            run_tasks<QXH_IQ4_XS_F>(buf[qb], tb, rb, mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
+            run_tasks<QXH_IQ4_XS_F>(buf[qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
             mark(d, epoch, 3);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT)
                 d.qkv[item_id(r / kTileRows) * kTileRows + r % kTileRows] =
@@ -1070,7 +1076,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(Q / 256) * 136u + kRowPad, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = Q / 256;
-            run_tasks<QXH_IQ4_XS_F>(buf[1 - qb], tb, rb, mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
+            run_tasks<QXH_IQ4_XS_F>(buf[1 - qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
             mark(d, epoch, 3);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
                 const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
@@ -1139,7 +1145,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(n_own * (I / kTileRows)), nblk = H / 256;
-            run_tasks<QXH_IQ2_XS_F>(buf[1 - qb], tb, rb, 2 * mine, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part,
+            run_tasks<QXH_IQ2_XS_F>(buf[1 - qb], tb, rb, 2 * mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part,
                                     tile_waits(G, 0, d));
             tiles_done(G, 0, 2 * mine);
             mark(d, epoch, 3);
@@ -1232,7 +1238,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             uint8_t* cur = buf[(qb + k) & 1];
             if (k + 1 < mine) issue_head_group(d, hg0 + item_id(k + 1), buf[(qb + k + 1) & 1], G, kGHead0 + ((k + 1) & 1));
             group_wait(G, kGHead0 + (k & 1), d);
-            run_tasks<QXH_Q6_K_F>(cur, tb, rb, kHeadGroupTiles, nblk, [&](int) { return XQ{xb, sb}; }, K4, T, part);
+            run_tasks<QXH_Q6_K_F>(cur, tb, rb, kHeadGroupTiles, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
             if (threadIdx.x < kHeadGroupTiles * kTileRows) {
                 const int i = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows;
                 const int row = (hg0 + item_id(k)) * kHeadGroupTiles * kTileRows + i * kTileRows + r;
