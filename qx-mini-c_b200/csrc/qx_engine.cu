@@ -58,6 +58,7 @@ struct qx_cuda_engine {
     bool use_graph = true;
     std::vector<Op> ops;
     LayerW* layers_dev = nullptr;   // device copy of the layer table (persistent step kernel)
+    uint8_t* iq2r = nullptr;         // gate/up re-laid for the persistent step kernel (IQ2R)
     int mega_grid = 0;               // 0 = per-stage kernels
     int* d_topi = nullptr;
     double* d_logits_d = nullptr;    // final_head: double logits for the top-N
@@ -189,6 +190,7 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->weights) cudaFree(E->weights);
     if (E->work) cudaFree(E->work);
     if (E->layers_dev) cudaFree(E->layers_dev);
+    if (E->iq2r) cudaFree(E->iq2r);
     for (void* p : E->ep_opened) cudaIpcCloseMemHandle(p);
     if (E->ep_xchg) cudaFree(E->ep_xchg);
     if (E->ep_peers_dev) cudaFree(E->ep_peers_dev);
@@ -477,6 +479,19 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     }
     if (!(o.flags & QX_CUDA_PER_STAGE) && !d.q8 && qx::benchmark_mix(E->layers.data(), dm.layers) &&
         qx::mega_setup(dev, dm, &E->mega_grid)) {
+        // the persistent kernel reads gate/up in its own layout (one lattice
+        // code per weight, decoded by a byte permute): re-lay them once here
+        const size_t rows = (size_t)dm.experts * dm.moe_inter, per = rows * qx::iq2r_row_bytes(dm.hidden);
+        ce = cudaMalloc((void**)&E->iq2r, 2 * per * (size_t)dm.layers);
+        for (int l = 0; l < dm.layers && ce == cudaSuccess; ++l) {
+            uint8_t* g = E->iq2r + (size_t)(2 * l) * per;
+            ce = qx::launch_iq2r_repack(E->layers[l].gate, g, rows, dm.hidden, E->tables, E->stream);
+            if (ce == cudaSuccess) ce = qx::launch_iq2r_repack(E->layers[l].up, g + per, rows, dm.hidden, E->tables, E->stream);
+            E->layers[l].gate_r = g;
+            E->layers[l].up_r = g + per;
+        }
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
+        if (ce != cudaSuccess) return fail(ce, "gate/up re-lay");
         ce = cudaMalloc((void**)&E->layers_dev, E->layers.size() * sizeof(LayerW));
         if (ce == cudaSuccess)
             ce = cudaMemcpy(E->layers_dev, E->layers.data(), E->layers.size() * sizeof(LayerW), cudaMemcpyHostToDevice);

@@ -257,6 +257,48 @@ __device__ __forceinline__ void dot_iq2_xs_mma(const uint8_t* r0, const uint8_t*
     }
 }
 
+// IQ2R (the persistent kernel's re-laid IQ2_XS, qx_mega.cu): row = fp16
+// block scales d (hdr bytes), then per block 16 scale bytes (1 + 2s of each
+// 16-value group) and 4 chunks of 32 bytes; chunk t holds, for groups
+// gq = 0..15, the u16 of nibble codes of values 16gq+4t..+3.  A code indexes
+// the signed lattice values {0, 8, 25, 43, 0, -8, -25, -43} (bytes of T0:T1;
+// code = 1..3 for magnitude 8, 25, 43, plus 4 when negative),
+// so one byte permute decodes 4 weights.  Same integer sums and block factors
+// as dot_iq2_xs_mma (d/8 * (1+2s) * sign * grid).
+constexpr uint32_t kIq2rT0 = 0x2b190800u, kIq2rT1 = 0xd5e7f800u;
+constexpr int kIq2rBlock = 144;
+__device__ __forceinline__ void dot_iq2r_mma(const uint8_t* r0, const uint8_t* r1, int hdr, int b0, int b1, const XQ& x,
+                                             int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3;
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + hdr + b * kIq2rBlock;
+        const uint8_t* p1 = r1 + hdr + b * kIq2rBlock;
+        const uint4 s0 = *reinterpret_cast<const uint4*>(p0), s1 = *reinterpret_cast<const uint4*>(p1);
+        const uint4 c0a = *reinterpret_cast<const uint4*>(p0 + 16 + 32 * t);
+        const uint4 c0b = *reinterpret_cast<const uint4*>(p0 + 32 + 32 * t);
+        const uint4 c1a = *reinterpret_cast<const uint4*>(p1 + 16 + 32 * t);
+        const uint4 c1b = *reinterpret_cast<const uint4*>(p1 + 32 + 32 * t);
+        const uint32_t w0[8] = {c0a.x, c0a.y, c0a.z, c0a.w, c0b.x, c0b.y, c0b.z, c0b.w};
+        const uint32_t w1[8] = {c1a.x, c1a.y, c1a.z, c1a.w, c1b.x, c1b.y, c1b.z, c1b.w};
+        const uint32_t sv0[4] = {s0.x, s0.y, s0.z, s0.w}, sv1[4] = {s1.x, s1.y, s1.z, s1.w};
+        acc.zero_block();
+#pragma unroll
+        for (int gq = 0; gq < 16; ++gq) {
+            const uint32_t q0 = (gq & 1) ? (w0[gq >> 1] >> 16) : w0[gq >> 1];
+            const uint32_t q1 = (gq & 1) ? (w1[gq >> 1] >> 16) : w1[gq >> 1];
+            const uint32_t a0 = __byte_perm(kIq2rT0, kIq2rT1, q0), a1 = __byte_perm(kIq2rT0, kIq2rT1, q1);
+            const int sc0 = (int)__byte_perm(sv0[gq >> 2], 0u, 0x4440u | (gq & 3));
+            const int sc1 = (int)__byte_perm(sv1[gq >> 2], 0u, 0x4440u | (gq & 3));
+            int D[4];
+            mma_k16(D, a0, a1, x.b[(b * 16 + gq) * kXG + lane]);
+            acc.add(D, sc0, sc1);
+        }
+        const double sc = pow2d(-x.s[b] - 3);
+        acc.flush((double)h2f(ld16(r0 + 2 * b)) * sc, (double)h2f(ld16(r1 + 2 * b)) * sc, lw);
+    }
+}
+
 // IQ3_XXS: m16n8k32 per 32-value group; lane t: grid index bytes t (values
 // 4t..) and 4+t (values 16+4t..); sign group = t>>1 resp. 2+(t>>1), half t&1.
 __device__ __forceinline__ void dot_iq3_xxs_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,

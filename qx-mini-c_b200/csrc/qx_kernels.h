@@ -27,7 +27,18 @@ struct LayerW {                  // device pointers into the weight arena (nativ
     // also take Q5_K (13) / Q6_K (14) attention, IQ2_S (22) gate/up and
     // IQ3_S (21) / IQ4_XS (23) down
     int tq, tk, tv, to, tgate, tup, tdown;
+    // IQ2_XS gate/up re-laid for the persistent step kernel (iq2r_row_bytes per
+    // row; null when that kernel is not used)
+    const uint8_t* gate_r;
+    const uint8_t* up_r;
 };
+
+// Bytes per row of the persistent kernel's IQ2_XS layout ("IQ2R") for a row of
+// H values: fp16 block scales, then per 256-value block 16 group-scale bytes
+// (1 + 2s) and 128 bytes of 3-bit signed-lattice codes in nibbles.
+size_t iq2r_row_bytes(int H);
+// Re-lay `rows` IQ2_XS rows of H values (src) into IQ2R rows (dst).
+cudaError_t launch_iq2r_repack(const uint8_t* src, uint8_t* dst, size_t rows, int H, const Tables* t, cudaStream_t st);
 
 // True when every layer uses the benchmark mix (the one-launch kernel's types).
 bool benchmark_mix(const LayerW* layers, int n);

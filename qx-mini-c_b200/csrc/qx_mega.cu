@@ -24,6 +24,7 @@ namespace qx {
 struct MegaLayout {                      // byte offsets into dynamic shared memory
     uint32_t xs, xb, sb, tab, part, buf0, buf1, total, buf_bytes;
     uint32_t norm;                       // offset inside a weight buffer of the RMSNorm vector
+    uint32_t iq2r_rb;                    // bytes per IQ2R gate/up row (tiles span buf0 + buf1)
 };
 
 namespace {
@@ -33,7 +34,7 @@ constexpr int kMW = kMT / 32;
 constexpr int kMaxTasks = 96;            // (tile, block) tasks per CTA per phase
 constexpr long long kSpinLimit = 1ll << 26;             // polls of one barrier wait, at most
 constexpr unsigned long long kBarrierTimeoutNs = 2000000000ull;   // 2 s; a healthy wait is microseconds
-enum { QXH_IQ4_XS_F = 23, QXH_IQ2_XS_F = 17, QXH_IQ3_XXS_F = 18, QXH_Q6_K_F = 14 };
+enum { QXH_IQ4_XS_F = 23, QXH_IQ2_XS_F = 17, QXH_IQ3_XXS_F = 18, QXH_Q6_K_F = 14, QXH_IQ2R_F = 117 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -159,6 +160,8 @@ __device__ void run_tasks(const uint8_t* tiles, uint32_t tb, uint32_t rb, int nt
         Acc acc{};
         if (FMT == QXH_IQ4_XS_F) dot_iq4_xs_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, K4, lane, acc);
         if (FMT == QXH_IQ2_XS_F) dot_iq2_xs_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, *T, lane, acc);
+        if (FMT == QXH_IQ2R_F)
+            dot_iq2r_mma(base + g * rb, base + (g + 8) * rb, (int)rb - nblk * kIq2rBlock, b, b + 1, x, lane, acc);
         if (FMT == QXH_IQ3_XXS_F) dot_iq3_xxs_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, *T, lane, acc);
         if (FMT == QXH_Q6_K_F) dot_q6_k_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, lane, acc);
         store_tile_rows(part, task, acc);
@@ -320,16 +323,18 @@ __device__ void issue_router(const Dev& d, const LayerW& w, uint8_t* buf, uint32
 
 // own[0..n_own): the top-8 slots (rank order) whose expert this GPU computes
 // (all 8 on one GPU).
+// Gate/up tiles in the IQ2R layout (rb = iq2r_row_bytes(H)); `buf` spans both
+// weight buffers.
 __device__ void issue_gateup(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf,
-                             Groups& G) {
-    const int H = d.dm.hidden, I = d.dm.moe_inter;
-    const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
+                             uint32_t rb, Groups& G) {
+    const int I = d.dm.moe_inter;
+    const uint32_t tb = (uint32_t)kTileRows * rb;
     const int tpe = I / kTileRows, mine = my_items(n_own * tpe);
     issue_tiles(G, 0, 2 * mine, [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
                     const int it = item_id(c >> 1), e = own[it / tpe], i0 = (it % tpe) * kTileRows;
                     const size_t off = (size_t)sel[e] * ((size_t)I * rb) + (size_t)i0 * rb;
                     dst = buf + (size_t)c * tb;
-                    src = ((c & 1) ? w.up : w.gate) + off;
+                    src = ((c & 1) ? w.up_r : w.gate_r) + off;
                     bytes = tb;
                 });
 }
@@ -1139,13 +1144,13 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             __syncthreads();
             const int n_own = n_own_s;
             mark(d, epoch, 0);
-            issue_gateup(d, w, sel, own, n_own, buf[1 - qb], G);
+            issue_gateup(d, w, sel, own, n_own, smem + L.buf0, L.iq2r_rb, G);   // both buffers: free now
             top8_weights(d, layer, sel, wsel);  // read in the down phase, after several block syncs
             mark(d, epoch, 1);
             mark(d, epoch, 2);
-            const uint32_t rb = (uint32_t)(H / 256) * 74u, tb = (uint32_t)kTileRows * rb;
+            const uint32_t rb = L.iq2r_rb, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(n_own * (I / kTileRows)), nblk = H / 256;
-            run_tasks<QXH_IQ2_XS_F>(buf[1 - qb], tb, rb, 2 * mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part,
+            run_tasks<QXH_IQ2R_F>(smem + L.buf0, tb, rb, 2 * mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part,
                                     tile_waits(G, 0, d));
             tiles_done(G, 0, 2 * mine);
             mark(d, epoch, 3);
@@ -1352,13 +1357,13 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
     const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter;
     const size_t t_qkv = (size_t)kTileRows * ((H / 256) * 136 + kRowPad), t_o = (size_t)kTileRows * ((Q / 256) * 136 + kRowPad);
-    const size_t t_gu = (size_t)kTileRows * (H / 256) * 74, t_dn = (size_t)kTileRows * (I / 256) * 98;
+    const size_t t_dn = (size_t)kTileRows * (I / 256) * 98;
     const size_t t_hd = (size_t)kHeadGroupTiles * kTileRows * (H / 256) * 210;
     size_t bufb = 0;
     bufb = std::max(bufb, cdiv((Q + 2 * KV) / kTileRows, grid) * t_qkv + (size_t)H * 4);
     bufb = std::max(bufb, cdiv(H / kTileRows, grid) * t_o);
     bufb = std::max(bufb, (size_t)cdiv(m.experts, grid) * H * 4 + (size_t)H * 4);
-    bufb = std::max(bufb, cdiv(8 * (I / kTileRows), grid) * 2 * t_gu);
+    bufb = std::max(bufb, (cdiv(8 * (I / kTileRows), grid) * 2 * kTileRows * iq2r_row_bytes(H) + 1) / 2);   // spans both
     bufb = std::max(bufb, cdiv(H / kTileRows, grid) * 8 * t_dn);
     bufb = std::max(bufb, t_hd);
     const int XS = std::max(std::max(H, Q), 8 * I);
@@ -1374,6 +1379,7 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     L.buf0 = off; off += L.buf_bytes;
     L.buf1 = off; off += L.buf_bytes;
     L.total = off;
+    L.iq2r_rb = (uint32_t)iq2r_row_bytes(H);
     return L;
 }
 
@@ -1394,7 +1400,8 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
         m.kv_heads > 8)
         return 0;
     auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
-    if (2 * cdiv(8 * (m.moe_inter / kTileRows), sms) > kTileBars / 2 || 8 * cdiv(m.hidden / kTileRows, sms) > kTileBars / 2)
+    if ((size_t)2 * cdiv(8 * (m.moe_inter / kTileRows), sms) * kTileRows * L.iq2r_rb > (size_t)2 * L.buf_bytes ||
+        2 * cdiv(8 * (m.moe_inter / kTileRows), sms) > kTileBars / 2 || 8 * cdiv(m.hidden / kTileRows, sms) > kTileBars / 2)
         return 0;                             // gate/up and down tiles of one CTA each fit half the tile barriers
     if (cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total) != cudaSuccess)
         return 0;
@@ -1414,6 +1421,55 @@ cudaError_t launch_decode_step(const Dev& d, const LayerW* layers_dev, int grid,
     const LayerW* lw = layers_dev;
     void* args[] = {&dd, &lw, &L};
     return cudaLaunchCooperativeKernel((const void*)k_decode_step, dim3(grid), dim3(kMT), args, L.total, st);
+}
+
+// ---- IQ2_XS -> IQ2R re-lay (once, at engine creation) ----------------------
+__host__ __device__ inline size_t iq2r_rb(int H) {
+    const size_t nblk = (size_t)H / 256;
+    return (2 * nblk + 15) / 16 * 16 + nblk * kIq2rBlock;
+}
+size_t iq2r_row_bytes(int H) { return iq2r_rb(H); }
+
+// One thread per (row, 256-value block).  Value v of the block comes from grid
+// entry e = v / 8 (qs[e]: 9-bit lattice index, 7 sign bits + parity from
+// ksigns), position v % 8; its code is 1..3 for magnitude 8, 25, 43, plus 4
+// when negative (src/qx_format.c:1994-2030 decodes the same fields).
+__global__ void k_iq2r_repack(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, size_t rows, int H,
+                              const Tables* __restrict__ t) {
+    const int nblk = H / 256;
+    const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (id >= rows * (size_t)nblk) return;
+    const size_t row = id / nblk;
+    const int b = (int)(id % nblk);
+    const size_t rb = iq2r_rb(H), hdr = rb - (size_t)nblk * kIq2rBlock;
+    const uint8_t* blk = src + (row * nblk + b) * 74;
+    uint8_t* orow = dst + row * rb;
+    orow[2 * b] = blk[0];
+    orow[2 * b + 1] = blk[1];
+    uint8_t* ob = orow + hdr + (size_t)b * kIq2rBlock;
+    for (int gq = 0; gq < 16; ++gq) ob[gq] = (uint8_t)(1 + 2 * ((blk[66 + (gq >> 1)] >> (4 * (gq & 1))) & 15));
+    for (int gq = 0; gq < 16; ++gq)
+        for (int tt = 0; tt < 4; ++tt) {
+            uint32_t codes = 0;
+            for (int j = 0; j < 4; ++j) {
+                const int v = 16 * gq + 4 * tt + j, e = v >> 3, k = v & 7;
+                const uint32_t q = (uint32_t)blk[2 + 2 * e] | ((uint32_t)blk[3 + 2 * e] << 8);
+                const float mag = t->iq2xs[q & 511u][k];
+                const bool neg = (t->ksigns[q >> 9] >> k) & 1u;
+                const uint32_t c = mag == 8.0f ? 1u : mag == 25.0f ? 2u : mag == 43.0f ? 3u : 0u;
+                codes |= (c | (neg && c ? 4u : 0u)) << (4 * j);
+            }
+            ob[16 + 32 * tt + 2 * gq] = (uint8_t)codes;
+            ob[16 + 32 * tt + 2 * gq + 1] = (uint8_t)(codes >> 8);
+        }
+    if (b == 0)
+        for (size_t i = 2 * (size_t)nblk; i < hdr; ++i) orow[i] = 0;
+}
+
+cudaError_t launch_iq2r_repack(const uint8_t* src, uint8_t* dst, size_t rows, int H, const Tables* t, cudaStream_t st) {
+    const size_t n = rows * (size_t)(H / 256);
+    k_iq2r_repack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, dst, rows, H, t);
+    return cudaGetLastError();
 }
 
 }  // namespace qx
