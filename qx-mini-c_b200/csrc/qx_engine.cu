@@ -58,7 +58,7 @@ struct qx_cuda_engine {
     bool use_graph = true;
     std::vector<Op> ops;
     LayerW* layers_dev = nullptr;   // device copy of the layer table (persistent step kernel)
-    uint8_t* iq2r = nullptr;         // gate/up re-laid for the persistent step kernel (IQ2R)
+    uint8_t* relay = nullptr;        // weights re-laid for the persistent step kernel (IQ2R, R4)
     int mega_grid = 0;               // 0 = per-stage kernels
     int* d_topi = nullptr;
     double* d_logits_d = nullptr;    // final_head: double logits for the top-N
@@ -190,7 +190,7 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->weights) cudaFree(E->weights);
     if (E->work) cudaFree(E->work);
     if (E->layers_dev) cudaFree(E->layers_dev);
-    if (E->iq2r) cudaFree(E->iq2r);
+    if (E->relay) cudaFree(E->relay);
     for (void* p : E->ep_opened) cudaIpcCloseMemHandle(p);
     if (E->ep_xchg) cudaFree(E->ep_xchg);
     if (E->ep_peers_dev) cudaFree(E->ep_peers_dev);
@@ -199,6 +199,23 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->own_stream && E->stream) cudaStreamDestroy(E->stream);
     cudaSetDevice(prev);
     delete E;
+}
+
+// The persistent kernel's re-laid weights store each IQ2_XS weight as an
+// index into {8, 25, 43} and each IQ3_XXS weight as an index into
+// {4, 12, ..., 52, 62} (times a sign); the lattices must hold exactly those.
+static bool relay_tables_ok(const qxh_iq_tables* T) {
+    for (int i = 0; i < 512; ++i)
+        for (int j = 0; j < 8; ++j) {
+            const int v = T->iq2xs[i][j];
+            if (v != 8 && v != 25 && v != 43) return false;
+        }
+    for (int i = 0; i < 256; ++i)
+        for (int j = 0; j < 4; ++j) {
+            const int v = T->iq3xxs[i][j];
+            if (!(v == 62 || (v >= 4 && v <= 52 && (v - 4) % 8 == 0))) return false;
+        }
+    return true;
 }
 
 QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tensor* tensors, uint32_t count,
@@ -478,20 +495,35 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         return 0;
     }
     if (!(o.flags & QX_CUDA_PER_STAGE) && !d.q8 && qx::benchmark_mix(E->layers.data(), dm.layers) &&
-        qx::mega_setup(dev, dm, &E->mega_grid)) {
-        // the persistent kernel reads gate/up in its own layout (one lattice
-        // code per weight, decoded by a byte permute): re-lay them once here
-        const size_t rows = (size_t)dm.experts * dm.moe_inter, per = rows * qx::iq2r_row_bytes(dm.hidden);
-        ce = cudaMalloc((void**)&E->iq2r, 2 * per * (size_t)dm.layers);
+        relay_tables_ok(qxh_tables()) && qx::mega_setup(dev, dm, &E->mega_grid)) {
+        // the persistent kernel reads its weights in its own layouts (one
+        // table index per weight, decoded by byte permutes): re-lay them once
+        const int H = dm.hidden, Q = dm.q_dim(), KV = dm.kv_dim(), I = dm.moe_inter;
+        const size_t gu = (size_t)dm.experts * I * qx::iq2r_row_bytes(H);
+        const size_t qkv = (size_t)(Q + 2 * KV) * qx::r4_bytes_per_row(H), wo = (size_t)H * qx::r4_bytes_per_row(Q);
+        const size_t dn = (size_t)dm.experts * H * qx::r4_bytes_per_row(I);
+        const size_t per = 2 * gu + qkv + wo + dn;
+        ce = cudaMalloc((void**)&E->relay, per * (size_t)dm.layers);
         for (int l = 0; l < dm.layers && ce == cudaSuccess; ++l) {
-            uint8_t* g = E->iq2r + (size_t)(2 * l) * per;
-            ce = qx::launch_iq2r_repack(E->layers[l].gate, g, rows, dm.hidden, E->tables, E->stream);
-            if (ce == cudaSuccess) ce = qx::launch_iq2r_repack(E->layers[l].up, g + per, rows, dm.hidden, E->tables, E->stream);
-            E->layers[l].gate_r = g;
-            E->layers[l].up_r = g + per;
+            LayerW& w = E->layers[l];
+            uint8_t* p = E->relay + (size_t)l * per;
+            const size_t rbh = qx::r4_bytes_per_row(H);
+            w.gate_r = p, w.up_r = p + gu, p += 2 * gu;
+            w.wq_r = p, w.wk_r = p + (size_t)Q * rbh, w.wv_r = p + (size_t)(Q + KV) * rbh, p += qkv;
+            w.wo_r = p, p += wo;
+            w.down_r = p;
+            const qx::Tables* T = E->tables;
+            ce = qx::launch_iq2r_repack(w.gate, const_cast<uint8_t*>(w.gate_r), (size_t)dm.experts * I, H, T, E->stream);
+            if (ce == cudaSuccess) ce = qx::launch_iq2r_repack(w.up, const_cast<uint8_t*>(w.up_r), (size_t)dm.experts * I, H, T, E->stream);
+            if (ce == cudaSuccess) ce = qx::launch_r4_repack(w.wq, const_cast<uint8_t*>(w.wq_r), Q, H, 23, T, E->stream);
+            if (ce == cudaSuccess) ce = qx::launch_r4_repack(w.wk, const_cast<uint8_t*>(w.wk_r), KV, H, 23, T, E->stream);
+            if (ce == cudaSuccess) ce = qx::launch_r4_repack(w.wv, const_cast<uint8_t*>(w.wv_r), KV, H, 23, T, E->stream);
+            if (ce == cudaSuccess) ce = qx::launch_r4_repack(w.wo, const_cast<uint8_t*>(w.wo_r), H, Q, 23, T, E->stream);
+            if (ce == cudaSuccess)
+                ce = qx::launch_r4_repack(w.down, const_cast<uint8_t*>(w.down_r), (size_t)dm.experts * H, I, 18, T, E->stream);
         }
         if (ce == cudaSuccess) ce = cudaStreamSynchronize(E->stream);
-        if (ce != cudaSuccess) return fail(ce, "gate/up re-lay");
+        if (ce != cudaSuccess) return fail(ce, "weight re-lay");
         ce = cudaMalloc((void**)&E->layers_dev, E->layers.size() * sizeof(LayerW));
         if (ce == cudaSuccess)
             ce = cudaMemcpy(E->layers_dev, E->layers.data(), E->layers.size() * sizeof(LayerW), cudaMemcpyHostToDevice);

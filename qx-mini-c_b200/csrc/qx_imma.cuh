@@ -299,6 +299,64 @@ __device__ __forceinline__ void dot_iq2r_mma(const uint8_t* r0, const uint8_t* r
     }
 }
 
+// R4 (the persistent kernel's re-laid IQ4_XS and IQ3_XXS, qx_mega.cu): each
+// weight is a 4-bit index into a 16-entry signed byte table K (IQ4_NL values,
+// or +-IQ3_XXS lattice magnitudes), every 32-value group has one scale byte
+// (IQ4_XS: ls - 32, signed; IQ3_XXS: 1 + 2s).  Row = fp16 block scales d
+// (r4_hdr bytes), the 8 scale bytes of every block, then from r4_codes
+// (16-byte aligned) per block 4 chunks
+// of 32 bytes: chunk t holds for groups ib = 0..7 the u32 whose nibbles 0..3
+// index values 32ib+4t..+3 and nibbles 4..7 values 32ib+16+4t..+3 (the A
+// fragments a0/a2 of lane t for m16n8k32).  Row bytes are 16 mod 32 so the
+// 16-byte code loads of the 8 rows a warp reads are conflict-free.
+__host__ __device__ constexpr int r4_hdr(int nblk) { return (2 * nblk + 15) / 16 * 16; }
+__host__ __device__ constexpr int r4_codes(int nblk) { return (r4_hdr(nblk) + 8 * nblk + 15) / 16 * 16; }
+__host__ __device__ constexpr size_t r4_row_bytes(int K) {
+    return ((size_t)r4_codes(K / 256) + (size_t)(K / 256) * 128 + 47) / 32 * 32 - 16;
+}
+constexpr uint32_t kIq3rK[4] = {0x1c140c04u, 0x3e342c24u, 0xe4ecf4fcu, 0xc2ccd4dcu};   // 4..62, -4..-62
+
+// 8 codes -> lo = table bytes of nibbles 0..3, hi = of nibbles 4..7.
+__device__ __forceinline__ void r4_lookup8(uint32_t q, const uint32_t K[4], uint32_t& lo, uint32_t& hi) {
+    const uint32_t pick = ((q >> 1) & 0x44444444u) | 0x32103210u;   // nibble n -> byte n or 4 + n
+    lo = __byte_perm(__byte_perm(K[0], K[1], q), __byte_perm(K[2], K[3], q), pick);
+    const uint32_t q2 = q >> 16;
+    hi = __byte_perm(__byte_perm(K[0], K[1], q2), __byte_perm(K[2], K[3], q2), pick >> 16);
+}
+
+template <bool SIGNED_SCALE>
+__device__ __forceinline__ void dot_r4_mma(const uint8_t* r0, const uint8_t* r1, int nblk, int b0, int b1, int fexp,
+                                           const XQ& x, const uint32_t K[4], int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3, hdr = r4_hdr(nblk), cod = r4_codes(nblk);
+    for (int b = b0; b < b1; ++b) {
+        const uint2 s0 = *reinterpret_cast<const uint2*>(r0 + hdr + 8 * b);
+        const uint2 s1 = *reinterpret_cast<const uint2*>(r1 + hdr + 8 * b);
+        const uint4 c0a = *reinterpret_cast<const uint4*>(r0 + cod + 128 * b + 32 * t);
+        const uint4 c0b = *reinterpret_cast<const uint4*>(r0 + cod + 128 * b + 32 * t + 16);
+        const uint4 c1a = *reinterpret_cast<const uint4*>(r1 + cod + 128 * b + 32 * t);
+        const uint4 c1b = *reinterpret_cast<const uint4*>(r1 + cod + 128 * b + 32 * t + 16);
+        const uint32_t w0[8] = {c0a.x, c0a.y, c0a.z, c0a.w, c0b.x, c0b.y, c0b.z, c0b.w};
+        const uint32_t w1[8] = {c1a.x, c1a.y, c1a.z, c1a.w, c1b.x, c1b.y, c1b.z, c1b.w};
+        acc.zero_block();
+#pragma unroll
+        for (int ib = 0; ib < 8; ++ib) {
+            uint32_t a0, a1, a2, a3;
+            r4_lookup8(w0[ib], K, a0, a2);
+            r4_lookup8(w1[ib], K, a1, a3);
+            const uint32_t v0 = ((ib < 4 ? s0.x : s0.y) >> (8 * (ib & 3))) & 0xffu;
+            const uint32_t v1 = ((ib < 4 ? s1.x : s1.y) >> (8 * (ib & 3))) & 0xffu;
+            const int sc0 = SIGNED_SCALE ? (int)(int8_t)v0 : (int)v0, sc1 = SIGNED_SCALE ? (int)(int8_t)v1 : (int)v1;
+            const int G = b * 16 + 2 * ib;
+            int D[4];
+            mma_k32(D, a0, a1, a2, a3, x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
+            acc.add(D, sc0, sc1);
+        }
+        const double sc = pow2d(-x.s[b] + fexp);
+        acc.flush((double)h2f(ld16(r0 + 2 * b)) * sc, (double)h2f(ld16(r1 + 2 * b)) * sc, lw);
+    }
+}
+
 // IQ3_XXS: m16n8k32 per 32-value group; lane t: grid index bytes t (values
 // 4t..) and 4+t (values 16+4t..); sign group = t>>1 resp. 2+(t>>1), half t&1.
 __device__ __forceinline__ void dot_iq3_xxs_mma(const uint8_t* r0, const uint8_t* r1, int b0, int b1, const XQ& x,

@@ -31,6 +31,13 @@ struct LayerW {                  // device pointers into the weight arena (nativ
     // row; null when that kernel is not used)
     const uint8_t* gate_r;
     const uint8_t* up_r;
+    // IQ4_XS attention and IQ3_XXS down re-laid for the persistent kernel
+    // (r4_bytes_per_row per row; null when that kernel is not used)
+    const uint8_t* wq_r;
+    const uint8_t* wk_r;
+    const uint8_t* wv_r;
+    const uint8_t* wo_r;
+    const uint8_t* down_r;
 };
 
 // Bytes per row of the persistent kernel's IQ2_XS layout ("IQ2R") for a row of
@@ -39,6 +46,12 @@ struct LayerW {                  // device pointers into the weight arena (nativ
 size_t iq2r_row_bytes(int H);
 // Re-lay `rows` IQ2_XS rows of H values (src) into IQ2R rows (dst).
 cudaError_t launch_iq2r_repack(const uint8_t* src, uint8_t* dst, size_t rows, int H, const Tables* t, cudaStream_t st);
+// The persistent kernel's layout ("R4") of IQ4_XS (type 23) and IQ3_XXS (18)
+// rows of K values: 4-bit indices into a 16-entry signed byte table, one scale
+// byte per 32 values, fp16 block scales.
+size_t r4_bytes_per_row(int K);
+cudaError_t launch_r4_repack(const uint8_t* src, uint8_t* dst, size_t rows, int K, int type, const Tables* t,
+                             cudaStream_t st);
 
 // True when every layer uses the benchmark mix (the one-launch kernel's types).
 bool benchmark_mix(const LayerW* layers, int n);

@@ -34,7 +34,8 @@ constexpr int kMW = kMT / 32;
 constexpr int kMaxTasks = 96;            // (tile, block) tasks per CTA per phase
 constexpr long long kSpinLimit = 1ll << 26;             // polls of one barrier wait, at most
 constexpr unsigned long long kBarrierTimeoutNs = 2000000000ull;   // 2 s; a healthy wait is microseconds
-enum { QXH_IQ4_XS_F = 23, QXH_IQ2_XS_F = 17, QXH_IQ3_XXS_F = 18, QXH_Q6_K_F = 14, QXH_IQ2R_F = 117 };
+enum { QXH_IQ4_XS_F = 23, QXH_IQ2_XS_F = 17, QXH_IQ3_XXS_F = 18, QXH_Q6_K_F = 14, QXH_IQ2R_F = 117, QXH_R4_IQ4_F = 123,
+       QXH_R4_IQ3_F = 118 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -162,6 +163,11 @@ __device__ void run_tasks(const uint8_t* tiles, uint32_t tb, uint32_t rb, int nt
         if (FMT == QXH_IQ2_XS_F) dot_iq2_xs_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, *T, lane, acc);
         if (FMT == QXH_IQ2R_F)
             dot_iq2r_mma(base + g * rb, base + (g + 8) * rb, (int)rb - nblk * kIq2rBlock, b, b + 1, x, lane, acc);
+        if (FMT == QXH_R4_IQ4_F) dot_r4_mma<true>(base + g * rb, base + (g + 8) * rb, nblk, b, b + 1, 0, x, K4, lane, acc);
+        if (FMT == QXH_R4_IQ3_F) {
+            const uint32_t K3[4] = {0x1c140c04u, 0x3e342c24u, 0xe4ecf4fcu, 0xc2ccd4dcu};   // 4..62, -4..-62
+            dot_r4_mma<false>(base + g * rb, base + (g + 8) * rb, nblk, b, b + 1, -2, x, K3, lane, acc);
+        }
         if (FMT == QXH_IQ3_XXS_F) dot_iq3_xxs_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, *T, lane, acc);
         if (FMT == QXH_Q6_K_F) dot_q6_k_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, lane, acc);
         store_tile_rows(part, task, acc);
@@ -183,12 +189,12 @@ __device__ __forceinline__ double tile_row(const double* part, int i, int nblk, 
 // copies (thread 0 spins on the grid barrier meanwhile): lane 0 announces the
 // group's bytes, then the lanes take the spans round-robin.
 //
-// IQ4_XS rows (1088 or 2176 bytes, 0 mod 64) are staged with a 16-byte gap
-// after each row: the 8 rows a warp reads at once then start in different
-// banks instead of the same ones.
+// The attention, gate/up and down tiles are in the kernel's own layouts (R4,
+// IQ2R: re-laid once at engine creation), whose row sizes keep the 8 rows a
+// warp reads at once in different shared-memory banks; a tile of 16 rows is
+// one contiguous copy.
 enum { kGQkv, kGOproj, kGRouter, kGGateup, kGDown, kGHead0, kGHead1, kGroups };
 constexpr int kIssueWarp = 1;
-constexpr uint32_t kRowPad = 16;
 
 struct Groups {
     uint64_t* bar;       // kGroups mbarriers (static shared memory)
@@ -274,36 +280,32 @@ __device__ void group_drain(Groups& G, const Dev& d) {
 }
 
 // The QKV and router groups also carry the layer's RMSNorm weights (H floats)
-// to offset `norm` of the buffer.  QKV tiles: padded rows (rb + kRowPad).
+// to offset `norm` of the buffer.
 __device__ void issue_qkv(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm, Groups& G) {
     const int H = d.dm.hidden, Q = d.dm.q_dim(), KV = d.dm.kv_dim();
-    const uint32_t rb = (uint32_t)(H / 256) * 136u, rbp = rb + kRowPad;
+    const uint32_t rb = (uint32_t)r4_row_bytes(H), tb = (uint32_t)kTileRows * rb;
     const int mine = my_items((Q + 2 * KV) / kTileRows);
-    issue_group(G, kGQkv, (uint32_t)H * 4u + (uint32_t)(mine * kTileRows) * rb, 1 + mine * kTileRows,
+    issue_group(G, kGQkv, (uint32_t)H * 4u + (uint32_t)mine * tb, 1 + mine,
                 [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
                     if (c == 0) {
                         dst = buf + norm, src = w.attn_norm, bytes = (uint32_t)H * 4u;
                         return;
                     }
-                    const int k = (c - 1) / kTileRows, r = (c - 1) % kTileRows, r0 = item_id(k) * kTileRows + r;
-                    dst = buf + (size_t)(k * kTileRows + r) * rbp;
-                    src = r0 < Q ? w.wq + (size_t)r0 * rb
-                          : r0 < Q + KV ? w.wk + (size_t)(r0 - Q) * rb
-                                        : w.wv + (size_t)(r0 - Q - KV) * rb;
-                    bytes = rb;
+                    const int r0 = item_id(c - 1) * kTileRows;
+                    dst = buf + (size_t)(c - 1) * tb;
+                    src = r0 < Q ? w.wq_r + (size_t)r0 * rb
+                          : r0 < Q + KV ? w.wk_r + (size_t)(r0 - Q) * rb
+                                        : w.wv_r + (size_t)(r0 - Q - KV) * rb;
+                    bytes = tb;
                 });
 }
 
 __device__ void issue_oproj(const Dev& d, const LayerW& w, uint8_t* buf, Groups& G) {
-    const uint32_t rb = (uint32_t)(d.dm.q_dim() / 256) * 136u, rbp = rb + kRowPad;
+    const uint32_t rb = (uint32_t)r4_row_bytes(d.dm.q_dim()), tb = (uint32_t)kTileRows * rb;
     const int mine = my_items(d.dm.hidden / kTileRows);
-    issue_group(G, kGOproj, (uint32_t)(mine * kTileRows) * rb, mine * kTileRows,
-                [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
-                    const int k = c / kTileRows, r = c % kTileRows;
-                    dst = buf + (size_t)c * rbp;
-                    src = w.wo + ((size_t)item_id(k) * kTileRows + r) * rb;
-                    bytes = rb;
-                });
+    issue_group(G, kGOproj, (uint32_t)mine * tb, mine, [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+        dst = buf + (size_t)c * tb, src = w.wo_r + (size_t)item_id(c) * tb, bytes = tb;
+    });
 }
 
 __device__ void issue_router(const Dev& d, const LayerW& w, uint8_t* buf, uint32_t norm, Groups& G) {
@@ -342,13 +344,13 @@ __device__ void issue_gateup(const Dev& d, const LayerW& w, const int* sel, cons
 __device__ void issue_down(const Dev& d, const LayerW& w, const int* sel, const int* own, int n_own, uint8_t* buf,
                            Groups& G) {
     const int H = d.dm.hidden, I = d.dm.moe_inter;
-    const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
+    const uint32_t rb = (uint32_t)r4_row_bytes(I), tb = (uint32_t)kTileRows * rb;
     const size_t slice = (size_t)H * rb;
     const int mine = my_items(H / kTileRows);
     issue_tiles(G, kTileBars / 2, mine * n_own, [&](int c, uint8_t*& dst, const void*& src, uint32_t& bytes) {
                     const int k = c / max(n_own, 1), j = c % max(n_own, 1);
                     dst = buf + (size_t)c * tb;
-                    src = w.down + (size_t)sel[own[j]] * slice + (size_t)item_id(k) * tb;
+                    src = w.down_r + (size_t)sel[own[j]] * slice + (size_t)item_id(k) * tb;
                     bytes = tb;
                 });
 }
@@ -1045,9 +1047,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             build_xq(xs, H, xb, sb);
             __syncthreads();
             mark(d, epoch, 1);
-            const uint32_t rb = (uint32_t)(H / 256) * 136u + kRowPad, tb = (uint32_t)kTileRows * rb;
+            const uint32_t rb = (uint32_t)r4_row_bytes(H), tb = (uint32_t)kTileRows * rb;
             const int mine = my_items((Q + 2 * KV) / kTileRows), nblk = H / 256;
-            run_tasks<QXH_IQ4_XS_F>(buf[qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
+            run_tasks<QXH_R4_IQ4_F>(buf[qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
             mark(d, epoch, 3);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT)
                 d.qkv[item_id(r / kTileRows) * kTileRows + r % kTileRows] =
@@ -1079,9 +1081,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             mark(d, epoch, 1);
             group_wait(G, kGOproj, d);
             mark(d, epoch, 2);
-            const uint32_t rb = (uint32_t)(Q / 256) * 136u + kRowPad, tb = (uint32_t)kTileRows * rb;
+            const uint32_t rb = (uint32_t)r4_row_bytes(Q), tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = Q / 256;
-            run_tasks<QXH_IQ4_XS_F>(buf[1 - qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
+            run_tasks<QXH_R4_IQ4_F>(buf[1 - qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
             mark(d, epoch, 3);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
                 const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
@@ -1177,9 +1179,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
             __syncthreads();
             mark(d, epoch, 1);
-            const uint32_t rb = (uint32_t)(I / 256) * 98u, tb = (uint32_t)kTileRows * rb;
+            const uint32_t rb = (uint32_t)r4_row_bytes(I), tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = I / 256;
-            run_tasks<QXH_IQ3_XXS_F>(buf[qb], tb, rb, n_own * mine, nblk,
+            run_tasks<QXH_R4_IQ3_F>(buf[qb], tb, rb, n_own * mine, nblk,
                                      [&](int i) {
                                          return XQ{xb + (i % n_own) * xq_words(I), sb + (i % n_own) * (I / 256)};
                                      },
@@ -1356,8 +1358,8 @@ static int mega_max_tasks(const Dims& m, int grid) {
 static MegaLayout mega_layout(const Dims& m, int grid) {
     auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
     const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter;
-    const size_t t_qkv = (size_t)kTileRows * ((H / 256) * 136 + kRowPad), t_o = (size_t)kTileRows * ((Q / 256) * 136 + kRowPad);
-    const size_t t_dn = (size_t)kTileRows * (I / 256) * 98;
+    const size_t t_qkv = (size_t)kTileRows * r4_row_bytes(H), t_o = (size_t)kTileRows * r4_row_bytes(Q);
+    const size_t t_dn = (size_t)kTileRows * r4_row_bytes(I);
     const size_t t_hd = (size_t)kHeadGroupTiles * kTileRows * (H / 256) * 210;
     size_t bufb = 0;
     bufb = std::max(bufb, cdiv((Q + 2 * KV) / kTileRows, grid) * t_qkv + (size_t)H * 4);
@@ -1464,6 +1466,88 @@ __global__ void k_iq2r_repack(const uint8_t* __restrict__ src, uint8_t* __restri
         }
     if (b == 0)
         for (size_t i = 2 * (size_t)nblk; i < hdr; ++i) orow[i] = 0;
+}
+
+size_t r4_bytes_per_row(int K) { return r4_row_bytes(K); }
+
+// One thread per (row, 256-value block).  IQ4_XS (136 B: d, scales_h, scales_l,
+// 128 B of nibbles: byte j of group ib holds values 32ib + j (low) and
+// 32ib + 16 + j (high)): the code is the nibble, the group scale ls - 32.
+// IQ3_XXS (98 B: d, 64 lattice indices of 4 values, 8 x u32 of four 7-bit
+// sign codes and the group scale nibble): the code is the magnitude's index in
+// {4, 12, ..., 52, 62} plus 8 when negative, the group scale 1 + 2s
+// (src/qx_format.c:1914-1960, 2060-2110 decode the same fields).
+__global__ void k_r4_repack(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, size_t rows, int K, int type,
+                            const Tables* __restrict__ t) {
+    const int nblk = K / 256;
+    const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (id >= rows * (size_t)nblk) return;
+    const size_t row = id / nblk;
+    const int b = (int)(id % nblk);
+    const size_t rb = r4_row_bytes(K);
+    const int hdr = r4_hdr(nblk), cod = r4_codes(nblk);
+    uint8_t* orow = dst + row * rb;
+    uint8_t code[256];
+    uint8_t scale[8];
+    if (type == QXH_IQ4_XS_F) {
+        const uint8_t* blk = src + (row * nblk + b) * 136;
+        orow[2 * b] = blk[0];
+        orow[2 * b + 1] = blk[1];
+        const uint32_t sh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8);
+        const uint32_t sl = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) | ((uint32_t)blk[6] << 16) | ((uint32_t)blk[7] << 24);
+        for (int ib = 0; ib < 8; ++ib) {
+            const int ls = (int)(((sl >> (4 * ib)) & 15u) | (((sh >> (2 * ib)) & 3u) << 4));
+            scale[ib] = (uint8_t)(int8_t)(ls - 32);
+            for (int j = 0; j < 16; ++j) {
+                const uint8_t q = blk[8 + 16 * ib + j];
+                code[32 * ib + j] = q & 15u;
+                code[32 * ib + 16 + j] = q >> 4;
+            }
+        }
+    } else {
+        const uint8_t* blk = src + (row * nblk + b) * 98;
+        orow[2 * b] = blk[0];
+        orow[2 * b + 1] = blk[1];
+        for (int ib = 0; ib < 8; ++ib) {
+            const uint8_t* a = blk + 66 + 4 * ib;
+            const uint32_t aux = (uint32_t)a[0] | ((uint32_t)a[1] << 8) | ((uint32_t)a[2] << 16) | ((uint32_t)a[3] << 24);
+            scale[ib] = (uint8_t)(1 + 2 * (aux >> 28));
+            for (int k = 0; k < 8; ++k) {
+                const int idx = blk[2 + 8 * ib + k];
+                const uint32_t signs = t->ksigns[(aux >> (7 * (k >> 1))) & 127u];
+                for (int j = 0; j < 4; ++j) {
+                    const int mag = (int)t->iq3xxs[idx][j];
+                    const int mi = mag == 62 ? 7 : (mag - 4) / 8;
+                    const uint32_t neg = (signs >> (4 * (k & 1) + j)) & 1u;
+                    code[32 * ib + 4 * k + j] = (uint8_t)(mi + 8 * neg);
+                }
+            }
+        }
+    }
+    for (int ib = 0; ib < 8; ++ib) orow[hdr + 8 * b + ib] = scale[ib];
+    for (int tt = 0; tt < 4; ++tt)
+        for (int ib = 0; ib < 8; ++ib) {
+            uint32_t w = 0;
+            for (int j = 0; j < 4; ++j) {
+                w |= (uint32_t)code[32 * ib + 4 * tt + j] << (4 * j);
+                w |= (uint32_t)code[32 * ib + 16 + 4 * tt + j] << (16 + 4 * j);
+            }
+            uint8_t* o = orow + cod + 128 * b + 32 * tt + 4 * ib;
+            o[0] = (uint8_t)w, o[1] = (uint8_t)(w >> 8), o[2] = (uint8_t)(w >> 16), o[3] = (uint8_t)(w >> 24);
+        }
+    if (b == 0) {                              // the row's padding
+        for (int i = 2 * nblk; i < hdr; ++i) orow[i] = 0;
+        for (int i = hdr + 8 * nblk; i < cod; ++i) orow[i] = 0;
+        for (size_t i = (size_t)cod + 128 * (size_t)nblk; i < rb; ++i) orow[i] = 0;
+    }
+}
+
+cudaError_t launch_r4_repack(const uint8_t* src, uint8_t* dst, size_t rows, int K, int type, const Tables* t,
+                             cudaStream_t st) {
+    if (type != QXH_IQ4_XS_F && type != QXH_IQ3_XXS_F) return cudaErrorInvalidValue;
+    const size_t n = rows * (size_t)(K / 256);
+    k_r4_repack<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(src, dst, rows, K, type, t);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_iq2r_repack(const uint8_t* src, uint8_t* dst, size_t rows, int H, const Tables* t, cudaStream_t st) {
