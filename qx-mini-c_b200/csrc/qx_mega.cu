@@ -1021,6 +1021,11 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         }
         __syncthreads();
     }
+    // The residual rows this CTA updates in the O-projection and down
+    // epilogues (the same 16-row items in both phases): thread r keeps row
+    // item_id(0) * 16 + r in a register, so the epilogues need no L2 read.
+    const int own_rows = my_items(H / kTileRows) * kTileRows;
+    float xown = threadIdx.x < own_rows ? xs[item_id(threadIdx.x / kTileRows) * kTileRows + threadIdx.x % kTileRows] : 0.0f;
     for (int layer = 0; layer < m.layers; ++layer) {
         const LayerW& w = layers[layer];
         // ---------------- QKV (weights in buf[qb]) ----------------
@@ -1089,14 +1094,15 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
                 const float o = finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
                 d.attn_out[row] = o;
-                float xr = d.x[row];
+                float xr = xown;                 // == d.x[row]
                 if (ep && layer > 0) {           // the previous layer's MoE add, as ep_combine does it
                     float moe = 0.0f;
 #pragma unroll
                     for (int k = 0; k < 8; ++k) moe += __ldcg(ep_terms(d.ep_local, (layer - 1) & 1, k, H) + row);
                     xr = xr + moe;
                 }
-                d.x[row] = xr + o;
+                xown = xr + o;
+                d.x[row] = xown;
             }
             grid_sync(bar, epoch, nsync, d);
         }
@@ -1195,7 +1201,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                     for (int j = 0; j < n_own; ++j)
                         moe += (float)(wsel[own[j]] * (double)finite_or_zero_d(tile_row(part, n_own * k + j, nblk, rr)));
                     d.moe_out[row] = moe;
-                    d.x[row] = d.x[row] + moe;
+                    xown = xown + moe;
+                    d.x[row] = xown;
                 }
             } else {
                 // this rank's slots, weighted, into every rank's exchange buffer
@@ -1405,6 +1412,7 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
     if ((size_t)2 * cdiv(8 * (m.moe_inter / kTileRows), sms) * kTileRows * L.iq2r_rb > (size_t)2 * L.buf_bytes ||
         2 * cdiv(8 * (m.moe_inter / kTileRows), sms) > kTileBars / 2 || 8 * cdiv(m.hidden / kTileRows, sms) > kTileBars / 2)
         return 0;                             // gate/up and down tiles of one CTA each fit half the tile barriers
+    if (cdiv(m.hidden / kTileRows, sms) * kTileRows > kMT) return 0;   // one residual row per thread (xown)
     if (cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total) != cudaSuccess)
         return 0;
     int per = 0;
