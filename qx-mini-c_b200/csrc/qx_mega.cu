@@ -1194,26 +1194,31 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                                      K4, T, part, tile_waits(G, kTileBars / 2, d));
             tiles_done(G, kTileBars / 2, n_own * mine);
             mark(d, epoch, 3);
+            // the weighted terms (float)(w_j * y_j) of every (row, slot) in
+            // parallel (xs is free again), then per row in rank order
+            float* terms = xs;
+            for (int u = threadIdx.x; u < mine * kTileRows * n_own; u += kMT) {
+                const int r = u / n_own, j = u % n_own;
+                const float term = (float)(wsel[own[j]] *
+                                           (double)finite_or_zero_d(tile_row(part, n_own * (r / kTileRows) + j, nblk, r % kTileRows)));
+                if (!ep) {
+                    terms[u] = term;
+                } else {                         // this rank's slots into every rank's exchange buffer
+                    const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
+                    for (int p = 0; p < d.ep_world; ++p) ep_terms(d.ep_peers[p], layer & 1, own[j], H)[row] = term;
+                }
+            }
             if (!ep) {
+                __syncthreads();
                 for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
-                    const int k = r / kTileRows, rr = r % kTileRows, row = item_id(k) * kTileRows + rr;
+                    const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
                     float moe = 0.0f;
-                    for (int j = 0; j < n_own; ++j)
-                        moe += (float)(wsel[own[j]] * (double)finite_or_zero_d(tile_row(part, n_own * k + j, nblk, rr)));
+                    for (int j = 0; j < n_own; ++j) moe += terms[r * n_own + j];
                     d.moe_out[row] = moe;
                     xown = xown + moe;
                     d.x[row] = xown;
                 }
             } else {
-                // this rank's slots, weighted, into every rank's exchange buffer
-                for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
-                    const int k = r / kTileRows, rr = r % kTileRows, row = item_id(k) * kTileRows + rr;
-                    for (int j = 0; j < n_own; ++j) {
-                        const float term =
-                            (float)(wsel[own[j]] * (double)finite_or_zero_d(tile_row(part, n_own * k + j, nblk, rr)));
-                        for (int p = 0; p < d.ep_world; ++p) ep_terms(d.ep_peers[p], layer & 1, own[j], H)[row] = term;
-                    }
-                }
                 __threadfence_system();
             }
             grid_sync(bar, epoch, nsync, d);
