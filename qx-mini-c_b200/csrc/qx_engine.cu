@@ -58,7 +58,7 @@ struct qx_cuda_engine {
     bool use_graph = true;
     std::vector<Op> ops;
     LayerW* layers_dev = nullptr;   // device copy of the layer table (persistent step kernel)
-    uint8_t* relay = nullptr;        // weights re-laid for the persistent step kernel (IQ2R, R4)
+    uint8_t* relay = nullptr;        // weights re-laid for the persistent step kernel (IQ2R, R4, R8)
     int mega_grid = 0;               // 0 = per-stage kernels
     int* d_topi = nullptr;
     double* d_logits_d = nullptr;    // final_head: double logits for the top-N
@@ -502,8 +502,12 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         const size_t gu = (size_t)dm.experts * I * qx::iq2r_row_bytes(H);
         const size_t qkv = (size_t)(Q + 2 * KV) * qx::r4_bytes_per_row(H), wo = (size_t)H * qx::r4_bytes_per_row(Q);
         const size_t dn = (size_t)dm.experts * H * qx::r4_bytes_per_row(I);
-        const size_t per = 2 * gu + qkv + wo + dn;
-        ce = cudaMalloc((void**)&E->relay, per * (size_t)dm.layers);
+        const size_t per = 2 * gu + qkv + wo + dn, head = (size_t)dm.vocab * qx::r8_bytes_per_row(H);
+        ce = cudaMalloc((void**)&E->relay, per * (size_t)dm.layers + head);
+        if (ce == cudaSuccess) {
+            d.head_r = E->relay + per * (size_t)dm.layers;
+            ce = qx::launch_r8_repack(d.head, const_cast<uint8_t*>(d.head_r), (size_t)dm.vocab, H, E->stream);
+        }
         for (int l = 0; l < dm.layers && ce == cudaSuccess; ++l) {
             LayerW& w = E->layers[l];
             uint8_t* p = E->relay + (size_t)l * per;

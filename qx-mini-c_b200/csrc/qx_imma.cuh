@@ -489,6 +489,45 @@ __device__ inline double dot_q5_k_row(const uint8_t* row, int nblk, const float*
     return acc;
 }
 
+// R8 (the persistent kernel's re-laid Q6_K head, qx_mega.cu): row = fp16
+// block scales d (r4_hdr bytes), then per block 16 int8 group scales and 4
+// chunks of 64 bytes; chunk t holds for groups gq = 0..15 the int8 weights
+// q - 32 of values 16gq+4t..+3 (lane t's A fragment of m16n8k16).  Block =
+// 272 bytes; row bytes 16 mod 32.  The same integer weights, group scales and
+// block factors as dot_q6_k_mma, with no decoding.
+__host__ __device__ constexpr size_t r8_row_bytes(int K) {
+    return ((size_t)r4_hdr(K / 256) + (size_t)(K / 256) * 272 + 47) / 32 * 32 - 16;
+}
+__device__ __forceinline__ void dot_r8_mma(const uint8_t* r0, const uint8_t* r1, int nblk, int b0, int b1, const XQ& x,
+                                           int lane, Acc& acc) {
+    const double lw[2] = {limb_weight(lane, 0), limb_weight(lane, 1)};
+    const int t = lane & 3, hdr = r4_hdr(nblk);
+    for (int b = b0; b < b1; ++b) {
+        const uint8_t* p0 = r0 + hdr + 272 * b;
+        const uint8_t* p1 = r1 + hdr + 272 * b;
+        const uint4 s0 = *reinterpret_cast<const uint4*>(p0), s1 = *reinterpret_cast<const uint4*>(p1);
+        const uint32_t sv0[4] = {s0.x, s0.y, s0.z, s0.w}, sv1[4] = {s1.x, s1.y, s1.z, s1.w};
+        acc.zero_block();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+            const uint4 v0 = *reinterpret_cast<const uint4*>(p0 + 16 + 64 * t + 16 * q4);
+            const uint4 v1 = *reinterpret_cast<const uint4*>(p1 + 16 + 64 * t + 16 * q4);
+            const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w}, w1[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int gq = 4 * q4 + j;
+                const int sc0 = (int)(int8_t)((sv0[q4] >> (8 * j)) & 0xffu);
+                const int sc1 = (int)(int8_t)((sv1[q4] >> (8 * j)) & 0xffu);
+                int D[4];
+                mma_k16(D, w0[j], w1[j], x.b[(b * 16 + gq) * kXG + lane]);
+                acc.add(D, sc0, sc1);
+            }
+        }
+        const double sc = pow2d(-x.s[b]);
+        acc.flush((double)h2f(ld16(r0 + 2 * b)) * sc, (double)h2f(ld16(r1 + 2 * b)) * sc, lw);
+    }
+}
+
 // Q6_K: m16n8k16 per 16-value scale group.  Values of a 128-value half:
 // pos = 32*s + l (section s, l in 0..31); lane t takes l = 16*lh + 4t .. +3.
 __device__ __forceinline__ uint32_t q6_word(uint32_t ql, uint32_t qh, int s) {

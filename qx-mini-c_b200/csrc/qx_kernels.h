@@ -50,6 +50,10 @@ cudaError_t launch_iq2r_repack(const uint8_t* src, uint8_t* dst, size_t rows, in
 // rows of K values: 4-bit indices into a 16-entry signed byte table, one scale
 // byte per 32 values, fp16 block scales.
 size_t r4_bytes_per_row(int K);
+// The persistent kernel's layout ("R8") of Q6_K rows of K values: int8 weights
+// q - 32 in per-lane chunks, int8 group scales, fp16 block scales.
+size_t r8_bytes_per_row(int K);
+cudaError_t launch_r8_repack(const uint8_t* src, uint8_t* dst, size_t rows, int K, cudaStream_t st);
 cudaError_t launch_r4_repack(const uint8_t* src, uint8_t* dst, size_t rows, int K, int type, const Tables* t,
                              cudaStream_t st);
 
@@ -69,6 +73,7 @@ struct Dev {
     const uint8_t* tok_embd;     // Q4_K [V rows][H]
     const float* out_norm;       // F32 [H]
     const uint8_t* head;         // Q6_K [V rows][H]
+    const uint8_t* head_r;       // the head re-laid for the persistent kernel (R8; null otherwise)
     const double* rope;          // [ctx][D/2][2] cos, sin (host libm, double)
     float* x;                    // residual [H]
     float* xn;                   // normed input of the current projection [max(H,Q)]

@@ -35,7 +35,7 @@ constexpr int kMaxTasks = 96;            // (tile, block) tasks per CTA per phas
 constexpr long long kSpinLimit = 1ll << 26;             // polls of one barrier wait, at most
 constexpr unsigned long long kBarrierTimeoutNs = 2000000000ull;   // 2 s; a healthy wait is microseconds
 enum { QXH_IQ4_XS_F = 23, QXH_IQ2_XS_F = 17, QXH_IQ3_XXS_F = 18, QXH_Q6_K_F = 14, QXH_IQ2R_F = 117, QXH_R4_IQ4_F = 123,
-       QXH_R4_IQ3_F = 118 };
+       QXH_R4_IQ3_F = 118, QXH_R8_F = 114 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -170,6 +170,7 @@ __device__ void run_tasks(const uint8_t* tiles, uint32_t tb, uint32_t rb, int nt
         }
         if (FMT == QXH_IQ3_XXS_F) dot_iq3_xxs_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, *T, lane, acc);
         if (FMT == QXH_Q6_K_F) dot_q6_k_mma(base + g * rb, base + (g + 8) * rb, b, b + 1, x, lane, acc);
+        if (FMT == QXH_R8_F) dot_r8_mma(base + g * rb, base + (g + 8) * rb, nblk, b, b + 1, x, lane, acc);
         store_tile_rows(part, task, acc);
     }
     __syncthreads();
@@ -193,7 +194,8 @@ __device__ __forceinline__ double tile_row(const double* part, int i, int nblk, 
 // IQ2R: re-laid once at engine creation), whose row sizes keep the 8 rows a
 // warp reads at once in different shared-memory banks; a tile of 16 rows is
 // one contiguous copy.
-enum { kGQkv, kGOproj, kGRouter, kGGateup, kGDown, kGHead0, kGHead1, kGroups };
+enum { kGQkv, kGOproj, kGRouter, kGGateup, kGDown, kGHead0, kGHead1, kGHead2, kGroups };
+constexpr int kHeadStages = 3;             // head tiles in flight: a ring of 3 one-tile stages
 constexpr int kIssueWarp = 1;
 
 struct Groups {
@@ -406,13 +408,12 @@ __device__ void ep_wait_layer(const Dev& d, unsigned seqb, int prev_layer) {
     __syncthreads();
 }
 
-constexpr int kHeadGroupTiles = 2;
 
-// Head groups alternate between two mbarriers (ring of two buffers).
-__device__ void issue_head_group(const Dev& d, int grp, uint8_t* buf, Groups& G, int g) {
-    const uint32_t rb = (uint32_t)(d.dm.hidden / 256) * 210u, stage = (uint32_t)kHeadGroupTiles * kTileRows * rb;
-    issue_group(G, g, stage, 1, [&](int, uint8_t*& dst, const void*& src, uint32_t& bytes) {
-        dst = buf, src = d.head + (size_t)grp * stage, bytes = stage;
+// Head tile `tile` (16 R8 rows) into ring stage `st` (mbarrier kGHead0 + st).
+__device__ void issue_head_tile(const Dev& d, int tile, uint8_t* ring, int st, Groups& G) {
+    const uint32_t tb = (uint32_t)kTileRows * (uint32_t)r8_row_bytes(d.dm.hidden);
+    issue_group(G, kGHead0 + st, tb, 1, [&](int, uint8_t*& dst, const void*& src, uint32_t& bytes) {
+        dst = ring + (size_t)st * tb, src = d.head_r + (size_t)tile * tb, bytes = tb;
     });
 }
 
@@ -1181,7 +1182,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             mark(d, epoch, 0);
             // into the free gate/up buffer: next layer's QKV tiles (or the first head group)
             if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm, G);
-            else if ((int)blockIdx.x < hg1 - hg0) issue_head_group(d, hg0 + blockIdx.x, buf[1 - qb], G, kGHead0);
             build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
             __syncthreads();
             mark(d, epoch, 1);
@@ -1230,7 +1230,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         }
         qb = 1 - qb;
     }
-    // ---------------- head (2-stage ring over buf[qb], buf[1-qb]) ----------------
+    // ---------------- head (R8 tiles through a ring of kHeadStages stages) ----------------
     {
         if (ep) {
             ep_wait_layer(d, seqb, m.layers - 1);
@@ -1248,25 +1248,29 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         __syncthreads();
         build_xq(xs, H, xb, sb);
         __syncthreads();
-        const int mine = my_items(hg1 - hg0), nblk = H / 256;
-        const uint32_t rb = (uint32_t)nblk * 210u, tb = (uint32_t)kTileRows * rb;
+        // this rank's head rows [32 hg0, 32 hg1) as 16-row tiles; the ring spans
+        // both weight buffers (free: no layer tiles are in flight)
+        const int t0 = 2 * hg0, mine = my_items(2 * (hg1 - hg0)), nblk = H / 256;
+        const uint32_t rb = (uint32_t)r8_row_bytes(H), tb = (uint32_t)kTileRows * rb;
+        uint8_t* ring = smem + L.buf0;
+        for (int k = 0; k < kHeadStages - 1 && k < mine; ++k) issue_head_tile(d, t0 + item_id(k), ring, k, G);
         double bv = -1.0e300;
         int bi = 0x7fffffff;
         bool bad = false;
         for (int k = 0; k < mine; ++k) {
-            uint8_t* cur = buf[(qb + k) & 1];
-            if (k + 1 < mine) issue_head_group(d, hg0 + item_id(k + 1), buf[(qb + k + 1) & 1], G, kGHead0 + ((k + 1) & 1));
-            group_wait(G, kGHead0 + (k & 1), d);
-            run_tasks<QXH_Q6_K_F>(cur, tb, rb, kHeadGroupTiles, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
-            if (threadIdx.x < kHeadGroupTiles * kTileRows) {
-                const int i = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows;
-                const int row = (hg0 + item_id(k)) * kHeadGroupTiles * kTileRows + i * kTileRows + r;
-                const double v = tile_row(part, i, nblk, r);
+            const int st = k % kHeadStages;
+            if (k + kHeadStages - 1 < mine)    // the stage freed by tile k - 1 (synced below)
+                issue_head_tile(d, t0 + item_id(k + kHeadStages - 1), ring, (k + kHeadStages - 1) % kHeadStages, G);
+            group_wait(G, kGHead0 + st, d);
+            run_tasks<QXH_R8_F>(ring + (size_t)st * tb, tb, rb, 1, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
+            if (threadIdx.x < kTileRows) {
+                const int r = threadIdx.x, row = (t0 + item_id(k)) * kTileRows + r;
+                const double v = tile_row(part, 0, nblk, r);
                 if (!isfinite(v)) bad = true;
                 d.logits[row] = (float)v;
                 if (v > bv || (v == bv && row < bi)) { bv = v; bi = row; }
             }
-            __syncthreads();   // the buffer is refilled two iterations later
+            __syncthreads();   // stage st is refilled in the next iteration
         }
         if (bad) atomicOr(d.err, kErrNonFinite);
         for (int o = 16; o; o >>= 1) {
@@ -1360,7 +1364,7 @@ static int mega_max_tasks(const Dims& m, int grid) {
     const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter;
     const int t[] = {cdiv((Q + 2 * KV) / kTileRows, grid) * (H / 256), cdiv(H / kTileRows, grid) * (Q / 256),
                      cdiv(8 * (I / kTileRows), grid) * 2 * (H / 256), cdiv(H / kTileRows, grid) * 8 * (I / 256),
-                     kHeadGroupTiles * (H / 256)};
+                     H / 256};
     int mx = 0;
     for (int v : t) mx = std::max(mx, v);
     return mx;
@@ -1372,7 +1376,7 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     const int H = m.hidden, Q = m.q_dim(), KV = m.kv_dim(), I = m.moe_inter;
     const size_t t_qkv = (size_t)kTileRows * r4_row_bytes(H), t_o = (size_t)kTileRows * r4_row_bytes(Q);
     const size_t t_dn = (size_t)kTileRows * r4_row_bytes(I);
-    const size_t t_hd = (size_t)kHeadGroupTiles * kTileRows * (H / 256) * 210;
+    const size_t t_hd = ((size_t)kHeadStages * kTileRows * r8_row_bytes(H) + 1) / 2;   // the ring spans both buffers
     size_t bufb = 0;
     bufb = std::max(bufb, cdiv((Q + 2 * KV) / kTileRows, grid) * t_qkv + (size_t)H * 4);
     bufb = std::max(bufb, cdiv(H / kTileRows, grid) * t_o);
@@ -1482,6 +1486,46 @@ __global__ void k_iq2r_repack(const uint8_t* __restrict__ src, uint8_t* __restri
 }
 
 size_t r4_bytes_per_row(int K) { return r4_row_bytes(K); }
+size_t r8_bytes_per_row(int K) { return r8_row_bytes(K); }
+
+// One thread per (row, 256-value block) of Q6_K (210 B: ql[128], qh[64],
+// int8 scales[16], fp16 d).  Value v = 128h + 32s + l has the low 4 bits from
+// ql[64h + 32(s & 1) + l] (high nibble for s >= 2) and the high 2 bits from
+// qh[32h + l] >> 2s, weight q - 32, group scale scales[v / 16]
+// (src/qx_format.c decodes the same fields; so does dot_q6_k_mma).
+__global__ void k_r8_repack(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, size_t rows, int K) {
+    const int nblk = K / 256;
+    const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (id >= rows * (size_t)nblk) return;
+    const size_t row = id / nblk;
+    const int b = (int)(id % nblk);
+    const size_t rb = r8_row_bytes(K);
+    const int hdr = r4_hdr(nblk);
+    const uint8_t* blk = src + (row * nblk + b) * 210;
+    uint8_t* orow = dst + row * rb;
+    orow[2 * b] = blk[208];
+    orow[2 * b + 1] = blk[209];
+    uint8_t* ob = orow + hdr + 272 * b;
+    for (int gq = 0; gq < 16; ++gq) ob[gq] = blk[192 + gq];
+    for (int v = 0; v < 256; ++v) {
+        const int h = v >> 7, sct = (v >> 5) & 3, l = v & 31;
+        const uint8_t qlb = blk[64 * h + 32 * (sct & 1) + l];
+        const int lo = sct >= 2 ? (qlb >> 4) : (qlb & 15);
+        const int hi = (blk[128 + 32 * h + l] >> (2 * sct)) & 3;
+        const int gq = v >> 4, t = (v >> 2) & 3, j = v & 3;
+        ob[16 + 64 * t + 4 * gq + j] = (uint8_t)(int8_t)((lo | (hi << 4)) - 32);
+    }
+    if (b == 0) {
+        for (int i = 2 * nblk; i < hdr; ++i) orow[i] = 0;
+        for (size_t i = (size_t)hdr + 272 * (size_t)nblk; i < rb; ++i) orow[i] = 0;
+    }
+}
+
+cudaError_t launch_r8_repack(const uint8_t* src, uint8_t* dst, size_t rows, int K, cudaStream_t st) {
+    const size_t n = rows * (size_t)(K / 256);
+    k_r8_repack<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(src, dst, rows, K);
+    return cudaGetLastError();
+}
 
 // One thread per (row, 256-value block).  IQ4_XS (136 B: d, scales_h, scales_l,
 // 128 B of nibbles: byte j of group ib holds values 32ib + j (low) and
