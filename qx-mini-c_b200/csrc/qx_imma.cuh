@@ -490,13 +490,15 @@ __device__ inline double dot_q5_k_row(const uint8_t* row, int nblk, const float*
 }
 
 // R8 (the persistent kernel's re-laid Q6_K head, qx_mega.cu): row = fp16
-// block scales d (r4_hdr bytes), then per block 16 int8 group scales and 4
-// chunks of 64 bytes; chunk t holds for groups gq = 0..15 the int8 weights
-// q - 32 of values 16gq+4t..+3 (lane t's A fragment of m16n8k16).  Block =
-// 272 bytes; row bytes 16 mod 32.  The same integer weights, group scales and
-// block factors as dot_q6_k_mma, with no decoding.
+// block scales d (r4_hdr bytes), then per block 16 int8 group scales and 16
+// units of 16 bytes; unit 4 q4 + t holds for groups gq = 4q4..4q4+3 the int8
+// weights q - 32 of values 16gq+4t..+3 (lane t's A fragments of m16n8k16).
+// Block = 272 bytes; row bytes 64 mod 128, so the 8 units a quarter warp
+// loads (rows g, g+1; t = 0..3) fall in 8 different bank groups.  The same
+// integer weights, group scales and block factors as dot_q6_k_mma, with no
+// decoding.
 __host__ __device__ constexpr size_t r8_row_bytes(int K) {
-    return ((size_t)r4_hdr(K / 256) + (size_t)(K / 256) * 272 + 47) / 32 * 32 - 16;
+    return ((size_t)r4_hdr(K / 256) + (size_t)(K / 256) * 272 + 63) / 128 * 128 + 64;
 }
 __device__ __forceinline__ void dot_r8_mma(const uint8_t* r0, const uint8_t* r1, int nblk, int b0, int b1, const XQ& x,
                                            int lane, Acc& acc) {
@@ -510,8 +512,8 @@ __device__ __forceinline__ void dot_r8_mma(const uint8_t* r0, const uint8_t* r1,
         acc.zero_block();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-            const uint4 v0 = *reinterpret_cast<const uint4*>(p0 + 16 + 64 * t + 16 * q4);
-            const uint4 v1 = *reinterpret_cast<const uint4*>(p1 + 16 + 64 * t + 16 * q4);
+            const uint4 v0 = *reinterpret_cast<const uint4*>(p0 + 16 + 64 * q4 + 16 * t);
+            const uint4 v1 = *reinterpret_cast<const uint4*>(p1 + 16 + 64 * q4 + 16 * t);
             const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w}, w1[4] = {v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {

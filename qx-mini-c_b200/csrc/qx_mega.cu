@@ -1513,7 +1513,7 @@ __global__ void k_r8_repack(const uint8_t* __restrict__ src, uint8_t* __restrict
         const int lo = sct >= 2 ? (qlb >> 4) : (qlb & 15);
         const int hi = (blk[128 + 32 * h + l] >> (2 * sct)) & 3;
         const int gq = v >> 4, t = (v >> 2) & 3, j = v & 3;
-        ob[16 + 64 * t + 4 * gq + j] = (uint8_t)(int8_t)((lo | (hi << 4)) - 32);
+        ob[16 + 64 * (gq >> 2) + 16 * t + 4 * (gq & 3) + j] = (uint8_t)(int8_t)((lo | (hi << 4)) - 32);
     }
     if (b == 0) {
         for (int i = 2 * nblk; i < hdr; ++i) orow[i] = 0;
