@@ -4,12 +4,14 @@
 // layer QKV -> attention -> O projection -> router -> gate/up -> down, then
 // the head.  Phases are separated by a grid barrier (bounded spin, error flag
 // on timeout).  Work items of a phase (16-row weight tiles) are assigned to
-// CTAs round-robin; a CTA issues the cp.async copies of its NEXT phase's
-// weight tiles into the other half of a double buffer before it computes the
-// current phase, so the DRAM latency of the next phase and the barrier wait
-// overlap.  The arithmetic is the same exact-integer tensor-core dot product
-// and double-precision elementwise code as the per-stage kernels, so results
-// are bit-identical to them (and to the reference's double accumulation).
+// CTAs round-robin; a CTA's tiles of a later phase are copied into a free
+// weight buffer by bulk copies (mbarrier completion) while it computes and
+// waits, so the DRAM latency of a phase overlaps the ones before it.  The
+// weights are in the kernel's own layouts (IQ2R, R4, R8: re-laid once at
+// engine creation, same integers and scales as the GGUF blocks); the
+// arithmetic is the same exact-integer tensor-core dot product and
+// double-precision elementwise code as the per-stage kernels, so results are
+// bit-identical to them (and agree with the reference's double accumulation).
 #include <algorithm>
 #include <cfloat>
 
