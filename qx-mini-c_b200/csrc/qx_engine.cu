@@ -538,7 +538,9 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     d.ep_world = o.ep_world > 1 ? (int)o.ep_world : 1;
     d.ep_rank = o.ep_world > 1 ? (int)o.ep_rank : 0;
     {
-        uint32_t r[4];
+        // all experts and head rows when the partition does not apply (the
+        // persistent kernel, the only user, requires vocab % 32 == 0)
+        uint32_t r[4] = {0u, (uint32_t)dm.experts, 0u, (uint32_t)dm.vocab / 32u * 32u};
         qx_cuda_ep_partition((uint32_t)dm.experts, (uint32_t)dm.vocab, (uint32_t)d.ep_world, (uint32_t)d.ep_rank, r);
         d.ep_e0 = (int)r[0];
         d.ep_e1 = (int)r[1];

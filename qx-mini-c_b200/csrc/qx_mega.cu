@@ -1411,6 +1411,7 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
     cudaFuncAttributes a{};
     if (cudaFuncGetAttributes(&a, k_decode_step) != cudaSuccess) return 0;
+    if (m.vocab % 32) return 0;               // head rows in groups of 32 (the expert-parallel unit)
     const MegaLayout L = mega_layout(m, sms);
     if (L.total + a.sharedSizeBytes > (size_t)optin || !mega_tasks_fit(m, sms)) return 0;
     if ((size_t)m.ctx * 8 > L.sb - L.xb || (size_t)kVChunk * 132 > L.xb - L.xs) return 0;
