@@ -494,20 +494,31 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         qx_cuda_engine_destroy(E);
         return 0;
     }
-    if (!(o.flags & QX_CUDA_PER_STAGE) && !d.q8 && qx::benchmark_mix(E->layers.data(), dm.layers) &&
-        relay_tables_ok(qxh_tables()) && qx::mega_setup(dev, dm, &E->mega_grid)) {
+    bool mega = !(o.flags & QX_CUDA_PER_STAGE) && !d.q8 && qx::benchmark_mix(E->layers.data(), dm.layers) &&
+                relay_tables_ok(qxh_tables()) && qx::mega_setup(dev, dm, &E->mega_grid);
+    size_t relay_per = 0;                    // re-laid bytes per layer
+    if (mega) {
+        // the re-laid copies need ~17 GB for the full model: without the room,
+        // the engine runs the per-stage path on the GGUF layouts instead
+        const int H = dm.hidden, Q = dm.q_dim(), KV = dm.kv_dim(), I = dm.moe_inter;
+        relay_per = 2 * (size_t)dm.experts * I * qx::iq2r_row_bytes(H) + (size_t)(Q + 2 * KV) * qx::r4_bytes_per_row(H) +
+                    (size_t)H * qx::r4_bytes_per_row(Q) + (size_t)dm.experts * H * qx::r4_bytes_per_row(I);
+        const size_t relay_bytes = relay_per * (size_t)dm.layers + (size_t)dm.vocab * qx::r8_bytes_per_row(H);
+        if (cudaMalloc((void**)&E->relay, relay_bytes) != cudaSuccess) {
+            (void)cudaGetLastError();
+            E->relay = nullptr;
+            mega = false;
+        }
+    }
+    if (mega) {
         // the persistent kernel reads its weights in its own layouts (one
         // table index per weight, decoded by byte permutes): re-lay them once
         const int H = dm.hidden, Q = dm.q_dim(), KV = dm.kv_dim(), I = dm.moe_inter;
         const size_t gu = (size_t)dm.experts * I * qx::iq2r_row_bytes(H);
         const size_t qkv = (size_t)(Q + 2 * KV) * qx::r4_bytes_per_row(H), wo = (size_t)H * qx::r4_bytes_per_row(Q);
-        const size_t dn = (size_t)dm.experts * H * qx::r4_bytes_per_row(I);
-        const size_t per = 2 * gu + qkv + wo + dn, head = (size_t)dm.vocab * qx::r8_bytes_per_row(H);
-        ce = cudaMalloc((void**)&E->relay, per * (size_t)dm.layers + head);
-        if (ce == cudaSuccess) {
-            d.head_r = E->relay + per * (size_t)dm.layers;
-            ce = qx::launch_r8_repack(d.head, const_cast<uint8_t*>(d.head_r), (size_t)dm.vocab, H, E->stream);
-        }
+        const size_t per = relay_per;            // = 2 gu + qkv + wo + down
+        d.head_r = E->relay + per * (size_t)dm.layers;
+        ce = qx::launch_r8_repack(d.head, const_cast<uint8_t*>(d.head_r), (size_t)dm.vocab, H, E->stream);
         for (int l = 0; l < dm.layers && ce == cudaSuccess; ++l) {
             LayerW& w = E->layers[l];
             uint8_t* p = E->relay + (size_t)l * per;
