@@ -963,7 +963,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     float* xs = reinterpret_cast<float*>(smem + L.xs);
     uint32_t* xb = reinterpret_cast<uint32_t*>(smem + L.xb);
     int* sb = reinterpret_cast<int*>(smem + L.sb);
-    const IqTab* T = nullptr;              // the re-laid formats need no lattice tables
+    IqTab* T = reinterpret_cast<IqTab*>(smem + L.tab);
     double* part = reinterpret_cast<double*>(smem + L.part);
     uint8_t* buf[2] = {smem + L.buf0, smem + L.buf1};
     const Dims& m = d.dm;
@@ -984,6 +984,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
     const int e0 = d.ep_e0, e1 = d.ep_e1, hg0 = d.ep_hg0, hg1 = d.ep_hg1;
     uint32_t K4[4];
     load_kv_regs(d.tables, K4);
+    load_iq_tables(T, d.tables, true, true);
     // attention in one phase when the whole history of a head fits in shared memory
     const bool fused = pos + 1 <= fused_cap(L.sb - L.xb);
     const FusedStage fz = fused_stage(smem + L.xb, L.sb - L.xb);
@@ -1391,7 +1392,7 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     L.xs = off; off += a16u(std::max((size_t)XS * 4, (size_t)kVChunk * 132));
     L.xb = off; off += a16u(xq_words(XS) * 4);
     L.sb = off; off += a16u((size_t)XS / 256 * 4 + 32);
-    L.tab = off;                            // no lattice tables in shared memory (re-laid weights)
+    L.tab = off; off += a16u(sizeof(IqTab));
     L.part = off; off += a16u((size_t)mega_max_tasks(m, grid) * kTileRows * 8);
     L.buf_bytes = a16u(bufb);
     L.norm = L.buf_bytes - (uint32_t)H * 4u;
