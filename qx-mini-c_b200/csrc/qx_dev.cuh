@@ -237,28 +237,5 @@ __device__ __forceinline__ void stage_copy(uint8_t* dst, const uint8_t* src, uin
     for (uint32_t c = threadIdx.x; c < bytes / 16u; c += blockDim.x) cp_async16(dst + 16u * c, src + 16u * c);
 }
 
-// Stream this CTA's tiles (t = blockIdx.x + k*gridDim.x < ntiles) through a
-// STAGES-deep ring in shared memory.  issue(t, dst) starts the copies of tile
-// t; compute(t, smem) consumes it.  All threads of the CTA must call this.
-template <int STAGES, class Issue, class Compute>
-__device__ __forceinline__ void tile_pipeline(int ntiles, uint32_t stage_bytes, uint8_t* ring, Issue issue,
-                                              Compute compute) {
-    const int first = blockIdx.x, step = gridDim.x;
-    const int mine = first < ntiles ? (ntiles - first + step - 1) / step : 0;
-#pragma unroll
-    for (int s = 0; s < STAGES - 1; ++s) {
-        if (s < mine) issue(first + s * step, ring + (uint32_t)s * stage_bytes);
-        cp_async_commit();
-    }
-    for (int i = 0; i < mine; ++i) {
-        const int nx = i + STAGES - 1;
-        if (nx < mine) issue(first + nx * step, ring + (uint32_t)(nx % STAGES) * stage_bytes);
-        cp_async_commit();
-        cp_async_wait<STAGES - 1>();
-        __syncthreads();
-        compute(first + i * step, ring + (uint32_t)(i % STAGES) * stage_bytes);
-        __syncthreads();
-    }
-}
 
 }  // namespace qx
