@@ -10,9 +10,11 @@ per-token C-ABI call qx_cuda_decode_step with host token in / host token out.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
-Under torchrun (N > 1) every rank runs its own engine replica on its GPU (the
-expert-parallel engine is not in this build yet); value = tokens of all ranks
-/ max-over-ranks time.
+Under torchrun (N > 1) the ranks run one expert-parallel engine: every rank
+holds the model, computes its share of the experts and of the head rows, and
+the ranks exchange MoE terms and head maxima over NVLink inside the step
+kernel.  They decode one shared token stream, so value = tokens of that
+stream / max-over-ranks time ("scaling": "strong").
 """
 import argparse
 import ctypes as C
@@ -108,31 +110,43 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU arms
+REF_SAMPLE_POSITION = 128   # the middle of the GPU arm's positions 0..255
+
+
 def cpu_reference_sample(image, processes, tokens_per_process=1):
     """Time the reference's own C decode (oracle/_ref/libqxref.so, src/qx_format.c
-    compiled unchanged) for one greedy token from START_TOKEN at position 0 in
-    `processes` forked workers sharing the model image; returns tokens/s."""
+    compiled unchanged) for one greedy token at position REF_SAMPLE_POSITION,
+    over a seeded INT8 KV history of that length, in `processes` forked
+    workers sharing the model image; returns tokens/s.  The library is loaded
+    and the model opened in this (parent) process before the fork."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle_bind
     if not oracle_bind.available("ref"):
         return None, "reference checker oracle/_ref/libqxref.so not built"
+    model = oracle_bind.Checker("ref").open_image(image)
+    P = REF_SAMPLE_POSITION
+    rng = np.random.default_rng(11)
+    kv = model.new_kv(P + tokens_per_process + 1)
+    kv["k"][:, :P] = rng.integers(-127, 128, kv["k"][:, :P].shape, dtype=np.int8)
+    kv["v"][:, :P] = rng.integers(-127, 128, kv["v"][:, :P].shape, dtype=np.int8)
+    kv["ks"][:, :P] = 0.02
+    kv["vs"][:, :P] = 0.02
     pids = []
     t0 = time.perf_counter()
     for _ in range(processes):
         pid = os.fork()
         if pid == 0:
             try:
-                m = oracle_bind.Checker("ref").open_image(image)
-                kv = m.new_kv(tokens_per_process + 1)
                 tok = W.START_TOKEN
                 for s in range(tokens_per_process):
-                    tok = m.decode_step(tok, s, kv)["token"]
+                    tok = model.decode_step(tok, P + s, kv)["token"]
                 os._exit(0)
             except Exception:
                 os._exit(1)
         pids.append(pid)
     ok = all(os.waitpid(p, 0)[1] == 0 for p in pids)
     dt = time.perf_counter() - t0
+    model.close()
     if not ok:
         return None, "reference worker failed"
     return processes * tokens_per_process / dt, None
@@ -160,10 +174,10 @@ def run_reference_arm(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded random-quant model; no real checkpoint available)",
-        "config": {"workload": WORKLOAD, "sample": "one greedy token (48 layers + head) per process",
+        "config": {"workload": WORKLOAD, "sample": "one greedy token (48 layers + head) at position %d per process" % REF_SAMPLE_POSITION,
                    "parallelism": "%d independent CPU processes" % cores},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "reference",
-                         "sample": "%d processes x 1 greedy token of config 4 per step" % cores},
+                         "sample": "%d processes x 1 greedy token of config 4 at position %d per step" % (cores, REF_SAMPLE_POSITION)},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -420,7 +434,10 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f64",
+        "arithmetic": ("exact int32 tensor-core block sums (s8 weights x u8 limbs of a 56-bit fixed-point "
+                       "activation) folded into f64 accumulators; norms, RoPE, scores and softmax in f64, as the "
+                       "reference"),
         "data": "synthetic (seeded random-quant model and inputs; no real checkpoint available)",
         "config": {"workload": WORKLOAD if not args.layers else "profiling case: %d layers" % cfg.layers,
                    "tokens_per_step": steps_tok, "batch": 1,
@@ -442,7 +459,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, why = cpu_reference_sample(img, 1)
         line["cpu_baseline"] = ({"value": v, "unit": "tok/s", "cores": 1, "kind": "reference",
-                                 "sample": "1 greedy token of config 4 (48 layers + head) on one core"}
+                                 "sample": "1 greedy token of config 4 (48 layers + head) at position %d on one core" % REF_SAMPLE_POSITION}
                                 if v is not None else {"value": None, "unavailable": why})
     if rank == 0:
         print(json.dumps(line))

@@ -6,9 +6,8 @@
  * `--cuda-policy` other than "none" (src/qx_format.c:6004-6005, CLI
  * src/qx_qxf_main.c:443,512-514) and reserves a `cuda_profile` JSON block
  * (src/qx_format.c:6683).  This header is the seam: a patched state loop calls
- * these functions when cuda_policy == "b200" (INTEGRATION.md shows the
- * binding).  Each entry point below names the reference function whose work
- * it replaces.
+ * these functions when cuda_policy == "b200".  Each entry point below names
+ * the reference function whose work it replaces.
  *
  * Conventions (same as the reference's public API, include/qx_format.h):
  *   - every function returns 1 on success, 0 on failure, and then writes a

@@ -1,6 +1,6 @@
-// Device-side building blocks of the decode engine: GGUF block decoders that
-// reproduce the reference's float weight values, warp row-dot products over
-// row tiles staged in shared memory, and the cp.async tile pipeline.
+// Device-side building blocks of the decode engine: error bits, the lattice
+// tables, the reference's fp16 conversion, warp/block reductions, and the
+// asynchronous copy primitives (cp.async, bulk copies on mbarriers).
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -64,124 +64,7 @@ __device__ __forceinline__ double block_sum_d(double v, double* scratch) {
     return t;
 }
 
-// ---- row dots: one warp, one row staged in shared memory ------------------
-// Each lane owns 8 consecutive input positions (8*lane .. 8*lane+7) of every
-// 256-value block, so x reads are contiguous per lane.
-
-// IQ2_XS (74 B/block), src/qx_format.c:1914-1933.
-__device__ __forceinline__ float dot_iq2_xs(const uint8_t* row, const float* x, int nblk, const Tables& T, int lane) {
-    float acc = 0.f;
-    const int ib = lane >> 2, sub = lane & 3;
-    for (int b = 0; b < nblk; ++b) {
-        const uint8_t* blk = row + b * 74;
-        const float d = h2f(ld16(blk));
-        const uint8_t sc = blk[66 + ib];
-        const float db = d * (0.5f + (float)(sub < 2 ? (sc & 15) : (sc >> 4))) * 0.25f;
-        const uint16_t q = ld16(blk + 2 + 2 * lane);
-        const float* g = T.iq2xs[q & 511u];
-        const uint32_t s = T.ksigns[q >> 9];
-        const float4 x0 = *reinterpret_cast<const float4*>(x + b * 256 + 8 * lane);
-        const float4 x1 = *reinterpret_cast<const float4*>(x + b * 256 + 8 * lane + 4);
-        const float4 g0 = *reinterpret_cast<const float4*>(g);
-        const float4 g1 = *reinterpret_cast<const float4*>(g + 4);
-        float t = 0.f;
-        t = fmaf(g0.x, (s & 1u) ? -x0.x : x0.x, t);
-        t = fmaf(g0.y, (s & 2u) ? -x0.y : x0.y, t);
-        t = fmaf(g0.z, (s & 4u) ? -x0.z : x0.z, t);
-        t = fmaf(g0.w, (s & 8u) ? -x0.w : x0.w, t);
-        t = fmaf(g1.x, (s & 16u) ? -x1.x : x1.x, t);
-        t = fmaf(g1.y, (s & 32u) ? -x1.y : x1.y, t);
-        t = fmaf(g1.z, (s & 64u) ? -x1.z : x1.z, t);
-        t = fmaf(g1.w, (s & 128u) ? -x1.w : x1.w, t);
-        acc = fmaf(db, t, acc);
-    }
-    return warp_sum(acc);
-}
-
-// IQ3_XXS (98 B/block), src/qx_format.c:1935-1959.
-__device__ __forceinline__ float dot_iq3_xxs(const uint8_t* row, const float* x, int nblk, const Tables& T, int lane) {
-    float acc = 0.f;
-    const int ib = lane >> 2, l = lane & 3;
-    for (int b = 0; b < nblk; ++b) {
-        const uint8_t* blk = row + b * 98;
-        const float d = h2f(ld16(blk));
-        const uint32_t aux = ld32u(blk + 66 + 4 * ib);
-        const float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
-        const uint32_t s = T.ksigns[(aux >> (7 * l)) & 127u];
-        const float* g1 = T.iq3xxs[blk[2 + 8 * ib + 2 * l]];
-        const float* g2 = T.iq3xxs[blk[2 + 8 * ib + 2 * l + 1]];
-        const float4 x0 = *reinterpret_cast<const float4*>(x + b * 256 + 8 * lane);
-        const float4 x1 = *reinterpret_cast<const float4*>(x + b * 256 + 8 * lane + 4);
-        const float4 a = *reinterpret_cast<const float4*>(g1);
-        const float4 c = *reinterpret_cast<const float4*>(g2);
-        float t = 0.f;
-        t = fmaf(a.x, (s & 1u) ? -x0.x : x0.x, t);
-        t = fmaf(a.y, (s & 2u) ? -x0.y : x0.y, t);
-        t = fmaf(a.z, (s & 4u) ? -x0.z : x0.z, t);
-        t = fmaf(a.w, (s & 8u) ? -x0.w : x0.w, t);
-        t = fmaf(c.x, (s & 16u) ? -x1.x : x1.x, t);
-        t = fmaf(c.y, (s & 32u) ? -x1.y : x1.y, t);
-        t = fmaf(c.z, (s & 64u) ? -x1.z : x1.z, t);
-        t = fmaf(c.w, (s & 128u) ? -x1.w : x1.w, t);
-        acc = fmaf(db, t, acc);
-    }
-    return warp_sum(acc);
-}
-
-// IQ4_XS (136 B/block), src/qx_format.c:2036-2077.
-__device__ __forceinline__ float dot_iq4_xs(const uint8_t* row, const float* x, int nblk, const float* kv, int lane) {
-    float acc = 0.f;
-    const int ib = lane >> 2, part = lane & 3;
-    for (int b = 0; b < nblk; ++b) {
-        const uint8_t* blk = row + b * 136;
-        const float d = h2f(ld16(blk));
-        const uint32_t sh = ld16(blk + 2);
-        const int ls = ((blk[4 + (ib >> 1)] >> (4 * (ib & 1))) & 15) | (((sh >> (2 * ib)) & 3) << 4);
-        const float dl = d * (float)(ls - 32);
-        const uint32_t q = *reinterpret_cast<const uint32_t*>(blk + 8 + 16 * ib + 4 * part);
-        const float4 xl = *reinterpret_cast<const float4*>(x + b * 256 + 32 * ib + 4 * part);
-        const float4 xh = *reinterpret_cast<const float4*>(x + b * 256 + 32 * ib + 16 + 4 * part);
-        float t = 0.f;
-        t = fmaf(kv[q & 15u], xl.x, t);
-        t = fmaf(kv[(q >> 8) & 15u], xl.y, t);
-        t = fmaf(kv[(q >> 16) & 15u], xl.z, t);
-        t = fmaf(kv[(q >> 24) & 15u], xl.w, t);
-        t = fmaf(kv[(q >> 4) & 15u], xh.x, t);
-        t = fmaf(kv[(q >> 12) & 15u], xh.y, t);
-        t = fmaf(kv[(q >> 20) & 15u], xh.z, t);
-        t = fmaf(kv[(q >> 28) & 15u], xh.w, t);
-        acc = fmaf(dl, t, acc);
-    }
-    return warp_sum(acc);
-}
-
-// Q6_K (210 B/block), src/qx_format.c:2147-2169.  Lane l owns position l of
-// each 32-value section of each 128-value half.
-__device__ __forceinline__ float dot_q6_k(const uint8_t* row, const float* x, int nblk, int lane) {
-    float acc = 0.f;
-    for (int b = 0; b < nblk; ++b) {
-        const uint8_t* blk = row + b * 210;
-        const float d = h2f(ld16(blk + 208));
-        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t l0 = blk[64 * h + lane], l1 = blk[64 * h + 32 + lane], qh = blk[128 + 32 * h + lane];
-            const float* xv = x + b * 256 + 128 * h + lane;
-            const int si = 8 * h + (lane >> 4);
-            const int q1 = (int)((l0 & 15u) | ((qh & 3u) << 4)) - 32;
-            const int q2 = (int)((l1 & 15u) | (((qh >> 2) & 3u) << 4)) - 32;
-            const int q3 = (int)((l0 >> 4) | (((qh >> 4) & 3u) << 4)) - 32;
-            const int q4 = (int)((l1 >> 4) | (((qh >> 6) & 3u) << 4)) - 32;
-            acc = fmaf(d * (float)sc[si], (float)q1 * xv[0], acc);
-            acc = fmaf(d * (float)sc[si + 2], (float)q2 * xv[32], acc);
-            acc = fmaf(d * (float)sc[si + 4], (float)q3 * xv[64], acc);
-            acc = fmaf(d * (float)sc[si + 6], (float)q4 * xv[96], acc);
-        }
-    }
-    return warp_sum(acc);
-}
-
-// ---- cp.async row-tile pipeline --------------------------------------------
+// ---- asynchronous copies into shared memory ------------------------------
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");

@@ -10,7 +10,9 @@ for p in (PKG, ORACLE, os.path.join(ROOT, "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-REFERENCE_TREE = "/root/reference"
+# The reference source tree (read-only); only the checker build and the
+# fixture generator use it.
+REFERENCE_TREE = os.environ.get("QX_REFERENCE_TREE", "/root/reference")
 
 
 def pytest_configure(config):

@@ -9,6 +9,7 @@ restatement in oracle/ without the reference tree.
 
     python tests/golden/make_golden.py            # mini + full-size fixtures
     python tests/golden/make_golden.py --mini     # mini only (seconds)
+    python tests/golden/make_golden.py --state-loop   # add the state-loop pin to golden_full.json
 """
 import argparse
 import json
@@ -134,11 +135,80 @@ def rope_golden(ref):
     return outs
 
 
+def state_loop_fixture(ref, img, steps):
+    """The reference's own, unmodified state loop (src/qx_format.c:6721, the
+    CLI's `state-loop-probe --full-moe --final-head --dump-residuals`) on the
+    image written to disk.  Records per step the greedy token, per layer the
+    selected experts, routing weights, K/V row checksums and scales, and the
+    final residual and logits sample from the dump files.  The shim's composed
+    decode step (oracle/ref_shim.c) must reproduce every one of them."""
+    import ctypes
+    import glob
+    import shutil
+    tmp = tempfile.mkdtemp(prefix="qxsl")
+    try:
+        path = os.path.join(tmp, "model.qxf")
+        img.tofile(path)
+        dump = os.path.join(tmp, "dump")
+        os.mkdir(dump)
+        js_path = os.path.join(tmp, "out.json")
+        err = ctypes.create_string_buffer(512)
+        ok = ref.lib.qxref_state_loop_json(path.encode(), W.START_TOKEN, steps, steps + 1, js_path.encode(),
+                                           dump.encode(), err, 512)
+        assert ok, err.value
+        with open(js_path) as fh:
+            js = json.load(fh)
+        m = ref.open_image(img)
+        V = m.vocab
+        sample = list(range(0, V, max(1, V // 512)))
+        out = {"steps": [], "k_cache_checksum": js["k_cache_checksum"], "v_cache_checksum": js["v_cache_checksum"],
+               "final_token": js["final_token"], "logits_sample_idx": sample}
+        kv = m.new_kv(steps + 1)
+        tok = W.START_TOKEN
+        for s, st in enumerate(js["steps"]):
+            layers = st["layers"]
+            res = np.fromfile(os.path.join(dump, "step-%d-layer-%d-output.f32" % (s, m.layers - 1)), np.float32)
+            logits = np.fromfile(os.path.join(dump, "step-%d-logits.f32" % s), np.float32)
+            rec = {"position": s, "input": tok, "token": st["selected_token"],
+                   "experts": [l["selected_experts"] for l in layers],
+                   "routing": [l["routing_weights"] for l in layers],
+                   "k_checksum": [l["k_checksum"] for l in layers], "v_checksum": [l["v_checksum"] for l in layers],
+                   "k_scale": [l["k_scale"] for l in layers], "v_scale": [l["v_scale"] for l in layers],
+                   "residual": fl(res), "logits_sample": fl(logits[sample]), "argmax": int(np.argmax(logits))}
+            # the shim's decode step must agree with the unmodified loop
+            r = m.decode_step(tok, s, kv, want_logits=True)
+            assert r["token"] == rec["token"], (s, r["token"], rec["token"])
+            assert r["experts"].tolist() == rec["experts"], s
+            assert np.array_equal(r["residual"].view(np.uint32), res.view(np.uint32)), s
+            assert np.array_equal(r["logits"].view(np.uint32), logits.view(np.uint32)), s
+            for layer in range(m.layers):
+                assert ref.f["fnv1a64"](kv["k"][layer, s].ctypes.data, kv["k"].shape[2]) == rec["k_checksum"][layer]
+                assert ref.f["fnv1a64"](kv["v"][layer, s].ctypes.data, kv["v"].shape[2]) == rec["v_checksum"][layer]
+                assert np.float32(kv["ks"][layer, s]) == np.float32(rec["k_scale"][layer])
+            out["steps"].append(rec)
+            tok = rec["token"]
+        m.close()
+        assert len(glob.glob(os.path.join(dump, "*.f32"))) > 0
+        return out
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--mini", action="store_true")
+    ap.add_argument("--state-loop", action="store_true")
     a = ap.parse_args()
     ref = oracle_bind.Checker("ref")
+    if a.state_loop:
+        path = os.path.join(HERE, "golden_full.json")
+        with open(path) as f:
+            fx = json.load(f)
+        fx["state_loop"] = state_loop_fixture(ref, qxlib.build_image(W.model_config(full=True)), steps=4)
+        with open(path, "w") as f:
+            json.dump(fx, f)
+        print("added state_loop to golden_full.json")
+        return
     mini = qxlib.build_image(W.model_config(full=False))
     fx = model_fixture(ref, mini, False, decode_steps=8, attn_positions=[0, 1, 63, 64, 130])
     fx["decoders"] = decoder_fixture(ref, mini)
@@ -151,6 +221,7 @@ def main():
     full = qxlib.build_image(W.model_config(full=True))
     fx = model_fixture(ref, full, True, decode_steps=3, attn_positions=[511, 4095])
     fx["decoders"] = decoder_fixture(ref, full)
+    fx["state_loop"] = state_loop_fixture(ref, full, steps=4)
     with open(os.path.join(HERE, "golden_full.json"), "w") as f:
         json.dump(fx, f)
     print("wrote golden_full.json")

@@ -118,8 +118,14 @@ def _entry_off(img, i):
     return diro + 208 * i
 
 
+# The structure-size check: qx_open_file has its own "unsupported QXF structure
+# size" (src/qx_format.c:720-721), but qx_read_header (:443-445) runs first and
+# rejects the same fields as "QXF struct size mismatch", so that is the message
+# the reference's loader gives (test_loader_messages_match_reference below).
 CORRUPTIONS = {
     "bad QXF magic": lambda b: b.__setitem__(0, ord("X")),
+    "QXF struct size mismatch": lambda b: b.__setitem__(8, b[8] ^ 1),
+    "empty tensor directory": lambda b: b.__setitem__(slice(16, 20), np.zeros(4, np.uint8)),
     "unsupported QXF version": lambda b: b.__setitem__(4, 2),
     "manifest checksum mismatch": lambda b: b.__setitem__(60, b[60] ^ 1),
     "invalid tensor dimensions": lambda b: b.__setitem__(slice(_entry_off(b, 3) + 112, _entry_off(b, 3) + 120),
