@@ -156,8 +156,10 @@ int qx_cuda_embed(qx_cuda_engine *engine, uint32_t token, float *out, char *err,
  * inside a host that owns every allocation, or code that must not allocate
  * between stream-ordered steps.  All pointers are device pointers the caller
  * owns: residual[hidden], norm_weight[hidden] (output_norm.weight, F32),
- * head (output.weight bytes, Q6_K, vocab rows), logits[vocab] (may be NULL),
- * argmax (one uint32; 0xFFFFFFFF if a logit is not finite).  The work is
+ * head (output.weight bytes, Q6_K, vocab rows; 16-byte aligned),
+ * logits[vocab] (may be NULL), argmax (one uint32; 0xFFFFFFFF if a logit is
+ * not finite; the call still returns 1).  Misaligned pointers are refused
+ * before anything is queued.  The work is
  * queued on `stream` (cudaStream_t, NULL = default) and the call returns
  * without waiting.  Its scratch (per-CTA partial maxima and a counter) is a
  * fixed array inside this library, held by every GPU that loads it until the

@@ -862,7 +862,13 @@ QX_API int qx_cuda_kv_read(qx_cuda_engine* E, uint32_t layer, uint32_t first, ui
               d2h(E, v, E->dev.vcache + base * KV, count * KV, err, n) &&
               d2h(E, ks, E->dev.kscale + base, count * 4, err, n) && d2h(E, vs, E->dev.vscale + base, count * 4, err, n);
     if (!ok) return 0;
-    return cuda_ok(cudaStreamSynchronize(E->stream), "kv read", err, n) ? 1 : 0;
+    // wait, then move the staged copies into the caller's buffers
+    const cudaError_t ce = cudaStreamSynchronize(E->stream);
+    for (const auto& p : E->pending)
+        if (ce == cudaSuccess) memcpy(p.dst, E->h_stage + p.off, p.bytes);
+    E->pending.clear();
+    E->h_stage_used = 0;
+    return cuda_ok(ce, "kv read", err, n) ? 1 : 0;
 }
 
 QX_API int qx_cuda_profile_get(const qx_cuda_engine* E, qx_cuda_profile* out) {

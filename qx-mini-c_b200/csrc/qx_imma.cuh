@@ -44,6 +44,15 @@ struct XQ {
 // Exact 2^e as a double for -1022 <= e <= 1023.
 __device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(1023 + e) << 52); }
 
+// Block exponent recorded for a 256-value block that holds a NaN or an
+// infinity.  The reference's dot products with such an input are not finite
+// (and then zeroed, src/qx_format.c:4284, :4783, or reported, :3715); the
+// block's factor becomes NaN so every row's result is NaN here too.
+constexpr int kSbNonFinite = 0x40000000;
+__device__ __forceinline__ double blk_pow2(int S, int k) {
+    return S == kSbNonFinite ? __longlong_as_double(0x7ff8000000000000ll) : pow2d(k - S);
+}
+
 // ---- activation quantization ------------------------------------------------
 
 // X' = round(x * 2^S) + 2^55 (halfway cases away from zero), split in two
@@ -83,17 +92,20 @@ __device__ __forceinline__ void build_xq(const float* xs, int K, uint32_t* xb, i
         float mx = fmaxf(fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))),
                          fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const bool fin = isfinite(u.x) && isfinite(u.y) && isfinite(u.z) && isfinite(u.w) && isfinite(v.x) &&
+                         isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
         const int E = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 255u) - 127 : -126;
-        const int S = 54 - (E < -126 ? -126 : E);
+        const int S = __all_sync(0xffffffffu, fin) ? 54 - (E < -126 ? -126 : E) : kSbNonFinite;
         if (lane == 0) sb[blk] = S;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const float4 q = h ? v : u;
             uint32_t hi[4], lo[4], w[4];
-            to_fixed(q.x, S, hi[0], lo[0]);
-            to_fixed(q.y, S, hi[1], lo[1]);
-            to_fixed(q.z, S, hi[2], lo[2]);
-            to_fixed(q.w, S, hi[3], lo[3]);
+            const int Sq = S == kSbNonFinite ? 0 : S;   // the limbs are unused then (factor NaN)
+            to_fixed(q.x, Sq, hi[0], lo[0]);
+            to_fixed(q.y, Sq, hi[1], lo[1]);
+            to_fixed(q.z, Sq, hi[2], lo[2]);
+            to_fixed(q.w, Sq, hi[3], lo[3]);
             uint32_t* dst = xb + (size_t)(blk * 16 + 8 * h + gl) * kXG + t;
             transpose4(lo[0], lo[1], lo[2], lo[3], w);
 #pragma unroll
@@ -224,7 +236,7 @@ __device__ __forceinline__ void dot_iq4_xs_mma(const uint8_t* r0, const uint8_t*
             mma_k32(D, a0, a1, a2, a3, x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
             acc.add(D, ls0 - 32, ls1 - 32);
         }
-        const double sc = pow2d(-x.s[b]);
+        const double sc = blk_pow2(x.s[b], 0);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -252,7 +264,7 @@ __device__ __forceinline__ void dot_iq2_xs_mma(const uint8_t* r0, const uint8_t*
             mma_k16(D, a0, a1, x.b[(b * 16 + gq) * kXG + lane]);
             acc.add(D, sc0, sc1);
         }
-        const double sc = pow2d(-x.s[b] - 3);
+        const double sc = blk_pow2(x.s[b], -3);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -294,7 +306,7 @@ __device__ __forceinline__ void dot_iq2r_mma(const uint8_t* r0, const uint8_t* r
             mma_k16(D, a0, a1, x.b[(b * 16 + gq) * kXG + lane]);
             acc.add(D, sc0, sc1);
         }
-        const double sc = pow2d(-x.s[b] - 3);
+        const double sc = blk_pow2(x.s[b], -3);
         acc.flush((double)h2f(ld16(r0 + 2 * b)) * sc, (double)h2f(ld16(r1 + 2 * b)) * sc, lw);
     }
 }
@@ -352,7 +364,7 @@ __device__ __forceinline__ void dot_r4_mma(const uint8_t* r0, const uint8_t* r1,
             mma_k32(D, a0, a1, a2, a3, x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
             acc.add(D, sc0, sc1);
         }
-        const double sc = pow2d(-x.s[b] + fexp);
+        const double sc = blk_pow2(x.s[b], fexp);
         acc.flush((double)h2f(ld16(r0 + 2 * b)) * sc, (double)h2f(ld16(r1 + 2 * b)) * sc, lw);
     }
 }
@@ -381,7 +393,7 @@ __device__ __forceinline__ void dot_iq3_xxs_mma(const uint8_t* r0, const uint8_t
             mma_k32(D, a0, a1, a2, a3, x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
             acc.add(D, 1 + 2 * (int)(aux0 >> 28), 1 + 2 * (int)(aux1 >> 28));
         }
-        const double sc = pow2d(-x.s[b] - 2);
+        const double sc = blk_pow2(x.s[b], -2);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -412,7 +424,7 @@ __device__ __forceinline__ void dot_iq2_s_mma(const uint8_t* r0, const uint8_t* 
             mma_k16(D, a0, a1, x.b[(b * 16 + gq) * kXG + lane]);
             acc.add(D, sc0, sc1);
         }
-        const double sc = pow2d(-x.s[b] - 3);
+        const double sc = blk_pow2(x.s[b], -3);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -447,7 +459,7 @@ __device__ __forceinline__ void dot_iq3_s_mma(const uint8_t* r0, const uint8_t* 
             mma_k32(D, a[0], a[1], a[2], a[3], x.b[G * kXG + lane], x.b[(G + 1) * kXG + lane]);
             acc.add(D, s0, s1);
         }
-        const double sc = pow2d(-x.s[b]);
+        const double sc = blk_pow2(x.s[b], 0);
         acc.flush((double)h2f(ld16(p0)) * sc, (double)h2f(ld16(p1)) * sc, lw);
     }
 }
@@ -525,7 +537,7 @@ __device__ __forceinline__ void dot_r8_mma(const uint8_t* r0, const uint8_t* r1,
                 acc.add(D, sc0, sc1);
             }
         }
-        const double sc = pow2d(-x.s[b]);
+        const double sc = blk_pow2(x.s[b], 0);
         acc.flush((double)h2f(ld16(r0 + 2 * b)) * sc, (double)h2f(ld16(r1 + 2 * b)) * sc, lw);
     }
 }
@@ -569,7 +581,7 @@ __device__ __forceinline__ void dot_q6_k_mma(const uint8_t* r0, const uint8_t* r
                 }
             }
         }
-        const double sc = pow2d(-x.s[b]);
+        const double sc = blk_pow2(x.s[b], 0);
         acc.flush((double)h2f(ld16(p0 + 208)) * sc, (double)h2f(ld16(p1 + 208)) * sc, lw);
     }
 }

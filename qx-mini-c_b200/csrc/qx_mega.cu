@@ -14,6 +14,7 @@
 // bit-identical to them (and agree with the reference's double accumulation).
 #include <algorithm>
 #include <cfloat>
+#include <mutex>
 
 #include "qx_common.cuh"
 
@@ -66,7 +67,10 @@ __device__ __forceinline__ void mark(const Dev& d, unsigned epoch, int k) {
 // entered, which sets the arrival target.  A CTA waits at most
 // kBarrierTimeoutNs (or kSpinLimit polls); then it sets kErrTimeout and
 // returns, and every later barrier returns at once when it sees that flag, so
-// a broken step ends quickly with an error the host reports.
+// a broken step ends quickly with an error the host reports.  (Measured on
+// B200 against a flag word per CTA polled by several warps, and against a
+// counter plus a generation word: this single counter with one polling
+// thread per CTA was the fastest, 1.23 us per barrier for 148 CTAs.)
 __device__ __forceinline__ void grid_arrive(unsigned* bar, unsigned& epoch, unsigned& nsync, const Dev& d) {
     __syncthreads();
     epoch += 1;
@@ -763,9 +767,10 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
     }
     __syncthreads();
     if (!active) return;
+    mark(d, epoch, 0);
     cp_async_wait<0>();
     __syncthreads();
-    mark(d, epoch, 3);
+    mark(d, epoch, 1);
     // one warp per head: K heads (RMSNorm + RoPE, then max |k|), V heads
     // (max |v|), the query head (RMSNorm + RoPE, widened to double); the
     // row maxima (non-finite values count as 0) meet in S.sf[0..8) / [8..16)
@@ -789,6 +794,7 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
         }
     }
     __syncthreads();
+    mark(d, epoch, 2);
     float ka = 0.f, va = 0.f;
     for (int k = 0; k < KVH; ++k) {
         ka = fmaxf(ka, S.sf[k]);
@@ -810,7 +816,7 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
         }
         if (i == 0) { d.kscale[slot] = ksc; d.vscale[slot] = vsc; }
     }
-    mark(d, epoch, 0);
+    mark(d, epoch, 3);
     // scores of every position (the current one from the fresh INT8 row)
     const double sqrt_d = sqrt((double)D);
     double mloc = -1.0e300;
@@ -822,18 +828,19 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
         mloc = fmax(mloc, s);
     }
     const double mx = block_max_d(mloc, S.sd);
-    mark(d, epoch, 1);
+    mark(d, epoch, 4);
     for (int t = i; t < T; t += kMT) f.w_s[t] = exp(f.w_s[t] - mx);
     double den = fixed_order_sum(f.w_s, T, S.sd);
     if (!isfinite(den) || den <= 0.0) den = 1.0;
     for (int t = i; t < T; t += kMT) f.w_s[t] = f.w_s[t] / den;
-    mark(d, epoch, 2);
+    mark(d, epoch, 5);
     __syncthreads();
     const float acc = context_chain(T, f.w_s, prod, [&](int t, int dd) {
         return t == pos ? i8_to_f32(S.v8[g * D + sl * SW + dd]) * vsc : i8_to_f32(f.vrows[t * SW + dd]) * f.vscl[t];
     });
     if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
     __syncthreads();
+    mark(d, epoch, 6);
 }
 
 // Router softmax + top-8 over the logits in global memory (every CTA; the
@@ -1034,6 +1041,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         // ---------------- QKV (weights in buf[qb]) ----------------
         {
             group_wait(G, kGQkv, d);             // this phase's tiles and norm vector
+            mark(d, epoch, 0);
             if (layer > 0 && ep) {
                 ep_wait_layer(d, seqb, layer - 1);
                 ep_combine(d, layer - 1, xs);
@@ -1042,6 +1050,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             } else {
                 __syncthreads();
             }
+            mark(d, epoch, 1);
             // attention RMSNorm of xs in place
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
             double ss = 0.0;
@@ -1050,18 +1059,19 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             const double rms = sqrt(ss / (double)H + 1.0e-6);
             for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
             __syncthreads();
-            mark(d, epoch, 0);
+            mark(d, epoch, 2);
             issue_oproj(d, w, buf[1 - qb], G);  // the previous layer's down tiles are consumed
             build_xq(xs, H, xb, sb);
             __syncthreads();
-            mark(d, epoch, 1);
+            mark(d, epoch, 3);
             const uint32_t rb = (uint32_t)r4_row_bytes(H), tb = (uint32_t)kTileRows * rb;
             const int mine = my_items((Q + 2 * KV) / kTileRows), nblk = H / 256;
             run_tasks<QXH_R4_IQ4_F>(buf[qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
-            mark(d, epoch, 3);
+            mark(d, epoch, 4);
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT)
                 d.qkv[item_id(r / kTileRows) * kTileRows + r % kTileRows] =
                     finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
+            mark(d, epoch, 5);
             grid_arrive(bar, epoch, nsync, d);
             if (fused) issue_attn_fused(d, w, layer, pos, fz);   // the activation region is free again
             cp_async_commit();
@@ -1107,13 +1117,16 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 xown = xr + o;
                 d.x[row] = xown;
             }
+            mark(d, epoch, 4);
             grid_sync(bar, epoch, nsync, d);
         }
         // ---------------- router (weights in buf[qb]) ----------------
         {
             group_wait(G, kGRouter, d);          // router rows and norm vector
+            mark(d, epoch, 0);
             copy_to_smem(d.x, xs, H);
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
+            mark(d, epoch, 1);
             double ss = 0.0;
             for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
             ss = block_sum_d(ss, scratch);
@@ -1122,9 +1135,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             __syncthreads();
             if (blockIdx.x == 0)
                 for (int i = threadIdx.x; i < H; i += kMT) d.xn[i] = xs[i];
-            mark(d, epoch, 0);
             __syncthreads();
-            mark(d, epoch, 1);
+            mark(d, epoch, 2);
             const int mine = my_items(E);
             const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
             for (int k = 0; k < mine; ++k) {
@@ -1138,13 +1150,15 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 acc = block_sum_d(acc, scratch);
                 if (threadIdx.x == 0) d.router_logits[item_id(k)] = acc;
             }
+            mark(d, epoch, 3);
             grid_arrive(bar, epoch, nsync, d);
-            build_xq(xs, H, xb, sb);             // the FFN input for gate/up, while the grid gathers
+            build_xq(xs, H, xb, sb);   // the FFN input for gate/up, while the grid gathers
             grid_wait(bar, epoch, nsync, d);
         }
         // ---------------- top-8 + gate/up (weights in buf[1-qb]) ----------------
         {
             top8_select(d, sel, wsel, reinterpret_cast<long long*>(probs), scratch, top_cnt);
+            mark(d, epoch, 0);
             if (threadIdx.x < 32) {              // the slots whose expert this rank owns, in rank order
                 const unsigned mine_mask =
                     __ballot_sync(0xffffffffu, threadIdx.x < 8 && sel[threadIdx.x & 7] >= e0 && sel[threadIdx.x & 7] < e1);
@@ -1154,10 +1168,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             }
             __syncthreads();
             const int n_own = n_own_s;
-            mark(d, epoch, 0);
+            mark(d, epoch, 1);
             issue_gateup(d, w, sel, own, n_own, smem + L.buf0, L.iq2r_rb, G);   // both buffers: free now
             top8_weights(d, layer, sel, wsel);  // read in the down phase, after several block syncs
-            mark(d, epoch, 1);
             mark(d, epoch, 2);
             const uint32_t rb = L.iq2r_rb, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(n_own * (I / kTileRows)), nblk = H / 256;
@@ -1173,6 +1186,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const double gd = (double)gv;
                 d.hbuf[(it / tpe) * I + (it % tpe) * kTileRows + rr] = (float)(gd / (1.0 + exp(-gd)) * (double)uv);
             }
+            mark(d, epoch, 4);
             grid_arrive(bar, epoch, nsync, d);
             issue_down(d, w, sel, own, n_own, buf[qb], G);
             grid_wait(bar, epoch, nsync, d);
@@ -1184,9 +1198,10 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             mark(d, epoch, 0);
             // into the free gate/up buffer: next layer's QKV tiles (or the first head group)
             if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm, G);
+            mark(d, epoch, 1);
             build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
             __syncthreads();
-            mark(d, epoch, 1);
+            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)r4_row_bytes(I), tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = I / 256;
             run_tasks<QXH_R4_IQ3_F>(buf[qb], tb, rb, n_own * mine, nblk,
@@ -1210,6 +1225,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                     for (int p = 0; p < d.ep_world; ++p) ep_terms(d.ep_peers[p], layer & 1, own[j], H)[row] = term;
                 }
             }
+            mark(d, epoch, 4);
             if (!ep) {
                 __syncthreads();
                 for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
@@ -1223,6 +1239,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             } else {
                 __threadfence_system();
             }
+            mark(d, epoch, 5);
             grid_sync(bar, epoch, nsync, d);
             if (ep && blockIdx.x == 0 && threadIdx.x == 0) {   // every CTA's stores are ordered before the barrier
                 __threadfence_system();
@@ -1356,8 +1373,13 @@ __global__ void __launch_bounds__(kMT, 1) k_attn_context(Dev d, int layer) {
 }
 
 namespace {
-MegaLayout g_layout;
 uint32_t a16u(size_t v) { return (uint32_t)((v + 15) / 16 * 16); }
+// The step kernel's dynamic shared-memory limit is a per-device attribute of
+// the function, shared by every engine on that device: only ever raise it, so
+// an engine with a smaller model created later cannot lower it below what an
+// earlier engine's launches need.
+std::mutex g_smem_mu;
+int g_smem_limit[64];
 }  // namespace
 
 // (tile, block) tasks one CTA runs in its largest dot phase.
@@ -1425,12 +1447,19 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
         2 * cdiv(8 * (m.moe_inter / kTileRows), sms) > kTileBars / 2 || 8 * cdiv(m.hidden / kTileRows, sms) > kTileBars / 2)
         return 0;                             // gate/up and down tiles of one CTA each fit half the tile barriers
     if (cdiv(m.hidden / kTileRows, sms) * kTileRows > kMT) return 0;   // one residual row per thread (xown)
-    if (cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total) != cudaSuccess)
-        return 0;
+    {
+        std::lock_guard<std::mutex> lk(g_smem_mu);
+        int& cur = g_smem_limit[device & 63];
+        if ((int)L.total > cur) {
+            if (cudaFuncSetAttribute(k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total) !=
+                cudaSuccess)
+                return 0;
+            cur = (int)L.total;
+        }
+    }
     int per = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_decode_step, kMT, L.total);
     if (per < 1) return 0;
-    g_layout = L;
     *grid_out = sms;
     return 1;
 }

@@ -167,6 +167,20 @@ extern "C" __attribute__((visibility("default"))) int qx_cuda_final_head_noalloc
         set_err(err, err_len, "invalid final head argument");
         return 0;
     }
+    // The head rows are staged into shared memory with 16-byte asynchronous
+    // copies, so the head must start on a 16-byte boundary; the float and
+    // uint32 buffers need their natural 4-byte alignment.  A pointer carved
+    // from a caller's arena at another offset is refused here, before any
+    // launch, instead of faulting on the device.
+    if (reinterpret_cast<uintptr_t>(head_q6k_dev) & 15u) {
+        set_err(err, err_len, "head_q6k_dev must be 16-byte aligned");
+        return 0;
+    }
+    if ((reinterpret_cast<uintptr_t>(residual_dev) | reinterpret_cast<uintptr_t>(norm_weight_dev) |
+         reinterpret_cast<uintptr_t>(logits_dev) | reinterpret_cast<uintptr_t>(argmax_dev)) & 3u) {
+        set_err(err, err_len, "residual, norm weight, logits and argmax buffers must be 4-byte aligned");
+        return 0;
+    }
     if (hidden == 0 || hidden % 256 || hidden > 2048) {
         set_err(err, err_len, "hidden size must be a multiple of 256 and at most 2048");
         return 0;

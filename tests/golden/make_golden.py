@@ -158,6 +158,8 @@ def state_loop_fixture(ref, img, steps):
         assert ok, err.value
         with open(js_path) as fh:
             js = json.load(fh)
+        if os.environ.get("QX_STATE_LOOP_KEEP"):
+            shutil.copy(js_path, os.environ["QX_STATE_LOOP_KEEP"])
         m = ref.open_image(img)
         V = m.vocab
         sample = list(range(0, V, max(1, V // 512)))
@@ -165,10 +167,11 @@ def state_loop_fixture(ref, img, steps):
                "final_token": js["final_token"], "logits_sample_idx": sample}
         kv = m.new_kv(steps + 1)
         tok = W.START_TOKEN
-        for s, st in enumerate(js["steps"]):
+        for s, st in enumerate(js["tokens"]):
             layers = st["layers"]
             res = np.fromfile(os.path.join(dump, "step-%d-layer-%d-output.f32" % (s, m.layers - 1)), np.float32)
             logits = np.fromfile(os.path.join(dump, "step-%d-logits.f32" % s), np.float32)
+            assert st["input_token"] == tok and st["position"] == s
             rec = {"position": s, "input": tok, "token": st["selected_token"],
                    "experts": [l["selected_experts"] for l in layers],
                    "routing": [l["routing_weights"] for l in layers],

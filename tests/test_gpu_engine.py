@@ -95,11 +95,11 @@ def test_attention_mini_history(mini):
         assert_close(ctxv, case["context"], what="context P=%d" % P)
         assert_close(ao, case["attn_out"], what="attention output P=%d" % P)
         assert_close(res, case["residual"], what="residual P=%d" % P)
+        # the appended INT8 row and its scale are integer work: bit-exact
         k, v, ks, vs = mini.kv_read(layer, P, 1)
-        assert abs(ks[0] - case["k_scale"]) <= 1e-5 * case["k_scale"]
-        assert abs(vs[0] - case["v_scale"]) <= 1e-5 * case["v_scale"]
-        assert np.max(np.abs(k[0].astype(int) - np.asarray(case["k_row"]))) <= 1
-        assert np.max(np.abs(v[0].astype(int) - np.asarray(case["v_row"]))) <= 1
+        assert ks[0] == np.float32(case["k_scale"]) and vs[0] == np.float32(case["v_scale"])
+        np.testing.assert_array_equal(k[0], np.asarray(case["k_row"], np.int8))
+        np.testing.assert_array_equal(v[0], np.asarray(case["v_row"], np.int8))
 
 
 def test_attention_mini_matches_port_over_many_positions(mini, port, mini_image):
@@ -212,6 +212,10 @@ def test_config3_attention_with_history(full, port, case_index):
     assert_close(ctxv, case["context"], what="context ctx=%d" % (P + 1))
     assert_close(ao, case["attn_out"], what="attention output ctx=%d" % (P + 1))
     assert_close(res, case["residual"], what="residual ctx=%d" % (P + 1))
+    k, v, ks, vs = full.kv_read(layer, P, 1)
+    assert ks[0] == np.float32(case["k_scale"]) and vs[0] == np.float32(case["v_scale"])
+    np.testing.assert_array_equal(k[0], np.asarray(case["k_row"], np.int8))
+    np.testing.assert_array_equal(v[0], np.asarray(case["v_row"], np.int8))
 
 
 def test_full_model_runs_the_one_launch_step(full):
@@ -239,28 +243,46 @@ def test_config4_first_steps_match_reference(full):
 
 
 def test_config4_256_steps_teacher_forced(full, full_image, port):
-    """256 greedy steps on the device; then, at sampled positions, the CPU
-    checker continues from the engine's own KV and token and must pick the same
-    token and the same top-8 experts in every layer."""
+    """Config 4: 256 greedy steps on the device, then at EVERY position the CPU
+    checker continues from the engine's own KV history and token: it must pick
+    the same token and the same top-8 experts in every layer, and the K/V row
+    and scales it appends must equal the engine's byte for byte."""
     full.reset()
-    toks = full.generate(W.START_TOKEN, 0, W.DECODE_STEPS)
-    assert len(set(toks.tolist())) > 1
+    steps = []
+    tok = W.START_TOKEN
+    for s in range(W.DECODE_STEPS):
+        r = full.decode_step(tok, s, want_experts=True)
+        steps.append(r)
+        tok = r["token"]
+    toks = [r["token"] for r in steps]
+    assert len(set(toks)) > 1
+    full.reset()
+    assert list(full.generate(W.START_TOKEN, 0, W.DECODE_STEPS)) == toks   # the graph path picks the same
     P = port.open_image(full_image)
-    inputs = [W.START_TOKEN] + toks.tolist()
-    snap = [full.kv_read(layer, 0, W.DECODE_STEPS) for layer in range(full.layers)]
-    for s in (0, 17, 128, 255):
-        kv = P.new_kv(s + 1)
-        full.reset()
-        for layer in range(full.layers):
-            if s:
-                k, v, ks, vs = (a[:s] for a in snap[layer])
-                kv["k"][layer, :s], kv["v"][layer, :s], kv["ks"][layer, :s], kv["vs"][layer, :s] = k, v, ks, vs
-                full.kv_write(layer, 0, k, v, ks, vs)
-        r = P.decode_step(inputs[s], s, kv)
+    inputs = [W.START_TOKEN] + toks
+    kv = P.new_kv(W.DECODE_STEPS)
+    for layer in range(full.layers):
+        kv["k"][layer], kv["v"][layer], kv["ks"][layer], kv["vs"][layer] = full.kv_read(layer, 0, W.DECODE_STEPS)
+    eng_kv = {k: v.copy() for k, v in kv.items() if k != "ctx"}
+    flips, values, scale_diffs = 0, 0, 0
+    for s in range(W.DECODE_STEPS):
+        r = P.decode_step(inputs[s], s, kv)          # reads rows < s (the engine's), writes row s
         assert r["token"] == toks[s], "step %d" % s
-        e = full.decode_step(inputs[s], s, want_experts=True)
-        np.testing.assert_array_equal(e["experts"], r["experts"], err_msg="experts at step %d" % s)
-        assert e["token"] == r["token"]
+        np.testing.assert_array_equal(steps[s]["experts"], r["experts"], err_msg="experts at step %d" % s)
+        for name in ("k", "v"):
+            d = kv[name][:, s].astype(int) - eng_kv[name][:, s].astype(int)
+            assert np.max(np.abs(d)) <= 1, "%s row at step %d" % (name, s)
+            flips += int(np.count_nonzero(d))
+            values += d.size
+        for name in ("ks", "vs"):
+            scale_diffs += int(np.count_nonzero(kv[name][:, s].view(np.uint32) != eng_kv[name][:, s].view(np.uint32)))
+    # The appended INT8 values are lrintf(x / scale) of float projections.  The
+    # engine's projections agree with the reference's double sums to ~1e-16
+    # but are not formed in the same order, so a value that lands within that
+    # distance of a float rounding boundary can differ by one float ulp, and
+    # an INT8 value at a .5 boundary then by one.  Such flips must stay rare.
+    print("KV INT8 values differing by one: %d of %d; scales differing: %d" % (flips, values, scale_diffs))
+    assert flips <= values * 1e-6 and scale_diffs == 0
 
 
 def test_persistent_step_matches_per_stage_kernels(mini, mini_image):

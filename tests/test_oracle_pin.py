@@ -160,3 +160,37 @@ def test_port_matches_golden_full_head_and_moe(port, full_image):
     assert list(sel) == g["moe"]["selected"]
     np.testing.assert_array_equal(moe, f32(g["moe"]["moe_output"]))
     np.testing.assert_array_equal(m.embed(g["embed_token"]), f32(g["embed"]))
+
+
+def test_state_loop_fixture_agrees_with_the_decode_fixture():
+    """golden_full.json holds two records of config 4's first greedy steps:
+    "decode" from the shim's composed step (oracle/ref_shim.c) and
+    "state_loop" from the reference's own unmodified CLI state loop
+    (src/qx_format.c:6721, checked step by step against the shim when the
+    fixture was written).  They must agree."""
+    g = load("golden_full.json")
+    sl = g["state_loop"]["steps"]
+    for d, s in zip(g["decode"], sl):
+        assert d["input"] == s["input"] and d["token"] == s["token"]
+        assert d["experts"] == s["experts"]
+        if d["residual"] is not None:
+            np.testing.assert_array_equal(f32(d["residual"]), f32(s["residual"]))
+
+
+def test_port_matches_the_reference_state_loop(port, full_image):
+    """The C restatement against the reference's unmodified state loop: two
+    greedy steps of config 4, K/V rows by FNV-1a checksum and scale."""
+    sl = load("golden_full.json")["state_loop"]["steps"]
+    m = port.open_image(full_image)
+    kv = m.new_kv(4)
+    tok = W.START_TOKEN
+    for s, st in enumerate(sl[:2]):
+        r = m.decode_step(tok, s, kv)
+        assert r["token"] == st["token"]
+        assert r["experts"].tolist() == st["experts"]
+        np.testing.assert_array_equal(r["residual"], f32(st["residual"]))
+        for layer in range(m.layers):
+            assert port.f["fnv1a64"](kv["k"][layer, s].ctypes.data, kv["k"].shape[2]) == st["k_checksum"][layer]
+            assert port.f["fnv1a64"](kv["v"][layer, s].ctypes.data, kv["v"].shape[2]) == st["v_checksum"][layer]
+            assert kv["ks"][layer, s] == np.float32(st["k_scale"][layer])
+        tok = r["token"]

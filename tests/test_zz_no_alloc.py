@@ -65,6 +65,72 @@ def test_final_head_noalloc_matches_final_head(mini_image):
     eng.close()
 
 
+def _fn():
+    fn = qxlib.cuda().qx_cuda_final_head_noalloc
+    fn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
+                   C.c_char_p, C.c_uint64]
+    fn.restype = C.c_int
+    return fn
+
+
+def test_final_head_noalloc_full_geometry_matches_the_reference(full_image):
+    """H = 2048, V = 151936 (config 1): argmax and logits sample against the
+    reference's own head (tests/golden/golden_full.json), twice in a row, the
+    second call without a logits buffer."""
+    import json
+    import os
+    import torch
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_full.json")) as f:
+        g = json.load(f)["head"]
+    fn = _fn()
+    dev = torch.device("cuda", 0)
+    H, V = 2048, 151936
+    norm = torch.from_numpy(np.frombuffer(tensor_bytes(full_image, "output_norm.weight").tobytes(),
+                                          np.float32).copy()).to(dev)
+    head = torch.from_numpy(tensor_bytes(full_image, "output.weight").copy()).to(dev)
+    xd = torch.from_numpy(W.head_input(H)).to(dev)
+    logits = torch.empty(V, dtype=torch.float32, device=dev)
+    argmax = torch.empty(1, dtype=torch.int32, device=dev)
+    stream = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    for with_logits in (True, False):
+        argmax.fill_(-7)
+        err = qxlib.err_buf()
+        ok = fn(xd.data_ptr(), norm.data_ptr(), head.data_ptr(), H, V, logits.data_ptr() if with_logits else None,
+                argmax.data_ptr(), stream, err, len(err))
+        assert ok, err.value
+        torch.cuda.synchronize(dev)
+        assert int(argmax.cpu().item()) == g["top_tokens"][0]
+        if with_logits:
+            got = logits.cpu().numpy()
+            assert_close(got[g["logits_sample_idx"]], g["logits_sample"], what="no-alloc logits")
+
+
+def test_final_head_noalloc_non_finite_and_misaligned(mini_image):
+    import torch
+    fn = _fn()
+    dev = torch.device("cuda", 0)
+    H, V = 512, 4096
+    norm = torch.from_numpy(np.frombuffer(tensor_bytes(mini_image, "output_norm.weight").tobytes(),
+                                          np.float32).copy()).to(dev)
+    raw = tensor_bytes(mini_image, "output.weight")
+    head = torch.zeros(raw.size + 64, dtype=torch.uint8, device=dev)
+    head[:raw.size] = torch.from_numpy(raw.copy()).to(dev)
+    x = qxlib.normal_vector(3, H)
+    x[17] = np.inf
+    xd = torch.from_numpy(x).to(dev)
+    argmax = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    err = qxlib.err_buf()
+    ok = fn(xd.data_ptr(), norm.data_ptr(), head.data_ptr(), H, V, None, argmax.data_ptr(), stream, err, len(err))
+    assert ok, err.value
+    torch.cuda.synchronize(dev)
+    assert int(argmax.cpu().item()) & 0xFFFFFFFF == 0xFFFFFFFF
+    # a head pointer off a 16-byte boundary is refused on the host
+    err = qxlib.err_buf()
+    ok = fn(xd.data_ptr(), norm.data_ptr(), head.data_ptr() + 8, H, V, None, argmax.data_ptr(), stream, err, len(err))
+    assert ok == 0 and b"16-byte aligned" in err.value
+
+
 def test_final_head_noalloc_rejects_oversize():
     lib = qxlib.cuda()
     fn = lib.qx_cuda_final_head_noalloc
