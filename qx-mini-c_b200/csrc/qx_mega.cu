@@ -597,9 +597,12 @@ __device__ void attn_scores(const Dev& d, const LayerW& w, int layer, int pos, A
     }
     mark(d, epoch, 0);
     const float ksc = ka > 0.f ? ka / 127.0f : 1.0f, vsc = va > 0.f ? va / 127.0f : 1.0f;
+    const float krc = 1.0f / ksc, vrc = 1.0f / vsc;   // one division each; divf_by per value
     for (int j = i; j < KV; j += kMT) {
-        const int qk = isfinite(S.kcur[j]) ? (int)lrintf(S.kcur[j] / ksc) : 0;
-        const int qq = isfinite(S.vcur[j]) ? (int)lrintf(S.vcur[j] / vsc) : 0;
+        const float kq = ksc >= FLT_MIN ? divf_by(S.kcur[j], ksc, krc) : S.kcur[j] / ksc;
+        const float vq = vsc >= FLT_MIN ? divf_by(S.vcur[j], vsc, vrc) : S.vcur[j] / vsc;
+        const int qk = isfinite(S.kcur[j]) ? (int)lrintf(kq) : 0;
+        const int qq = isfinite(S.vcur[j]) ? (int)lrintf(vq) : 0;
         S.k8[j] = (int8_t)max(-127, min(127, qk));
         S.v8[j] = (int8_t)max(-127, min(127, qq));
     }
@@ -801,9 +804,12 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
         va = fmaxf(va, S.sf[8 + k]);
     }
     const float ksc = ka > 0.f ? ka / 127.0f : 1.0f, vsc = va > 0.f ? va / 127.0f : 1.0f;
+    const float krc = 1.0f / ksc, vrc = 1.0f / vsc;   // one division each; divf_by per value
     for (int j = i; j < KV; j += kMT) {
-        const int qk = isfinite(S.kcur[j]) ? (int)lrintf(S.kcur[j] / ksc) : 0;
-        const int qq = isfinite(S.vcur[j]) ? (int)lrintf(S.vcur[j] / vsc) : 0;
+        const float kq = ksc >= FLT_MIN ? divf_by(S.kcur[j], ksc, krc) : S.kcur[j] / ksc;
+        const float vq = vsc >= FLT_MIN ? divf_by(S.vcur[j], vsc, vrc) : S.vcur[j] / vsc;
+        const int qk = isfinite(S.kcur[j]) ? (int)lrintf(kq) : 0;
+        const int qq = isfinite(S.vcur[j]) ? (int)lrintf(vq) : 0;
         S.k8[j] = (int8_t)max(-127, min(127, qk));
         S.v8[j] = (int8_t)max(-127, min(127, qq));
     }
@@ -1056,8 +1062,11 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             double ss = 0.0;
             for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
             ss = block_sum_d(ss, scratch);
-            const double rms = sqrt(ss / (double)H + 1.0e-6);
-            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
+            const double rms = sqrt(ss / (double)H + 1.0e-6), rinv = 1.0 / rms;
+            if (isfinite(rms))
+                for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)div_by((double)xs[i], rms, rinv) * nw[i];
+            else
+                for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
             __syncthreads();
             mark(d, epoch, 2);
             issue_oproj(d, w, buf[1 - qb], G);  // the previous layer's down tiles are consumed
@@ -1130,8 +1139,11 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             double ss = 0.0;
             for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
             ss = block_sum_d(ss, scratch);
-            const double rms = sqrt(ss / (double)H + 1.0e-6);
-            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
+            const double rms = sqrt(ss / (double)H + 1.0e-6), rinv = 1.0 / rms;
+            if (isfinite(rms))
+                for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)div_by((double)xs[i], rms, rinv) * nw[i];
+            else
+                for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * nw[i];
             __syncthreads();
             if (blockIdx.x == 0)
                 for (int i = threadIdx.x; i < H; i += kMT) d.xn[i] = xs[i];
@@ -1262,8 +1274,11 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         double ss = 0.0;
         for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
         ss = block_sum_d(ss, scratch);
-        const double rms = sqrt(ss / (double)H + 1.0e-6);
-        for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * d.out_norm[i];
+        const double rms = sqrt(ss / (double)H + 1.0e-6), rinv = 1.0 / rms;
+        if (isfinite(rms))
+            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)div_by((double)xs[i], rms, rinv) * d.out_norm[i];
+        else
+            for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)((double)xs[i] / rms) * d.out_norm[i];
         __syncthreads();
         build_xq(xs, H, xb, sb);
         __syncthreads();
