@@ -137,6 +137,23 @@ int qx_cuda_moe_layer(qx_cuda_engine *engine, uint32_t layer, const float *resid
                       float *layer_output, float *moe_output, uint32_t selected[8], float weights[8],
                       char *err, uint64_t err_len);
 
+/* One MoE FFN layer for `tokens` independent tokens at once - the batched /
+ * prefill counterpart of qx_cuda_moe_layer.  The reference has no batched
+ * path: its prompt prefill and decode call qx_apply_real_moe_layer
+ * (src/qx_format.c:5198-5317) once per token (the prefill loop
+ * :6250-6547).  Per token t: layer_output[t] = residual[t] + moe_output[t]
+ * with the reference's router, top-8 and rank-order sum; the expert
+ * projections run as grouped GEMMs over the tokens routed to each expert on
+ * the tcgen05 tensor cores (exact integer contraction).  residual / outputs
+ * are [tokens][hidden] host floats; selected / weights are [tokens][8]
+ * (either may be NULL, moe_output too).  tokens <= QX_CUDA_MAX_BATCH.  Needs
+ * the benchmark quant mix (IQ2_XS gate/up, IQ3_XXS down) in the one-launch
+ * step kernel's layouts. */
+#define QX_CUDA_MAX_BATCH 4096u
+int qx_cuda_moe_batch(qx_cuda_engine *engine, uint32_t layer, uint32_t tokens, const float *residual,
+                      float *layer_output, float *moe_output, uint32_t *selected, float *weights, char *err,
+                      uint64_t err_len);
+
 /* The attention half of one layer at `position`, state-loop order
  * (src/qx_format.c:6283-6423 with qx_rope_gqa_attention_partial, :5051-5196):
  * attn RMSNorm, K/V projection, K head norm + RoPE, INT8 append at

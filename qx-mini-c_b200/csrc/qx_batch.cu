@@ -1,0 +1,507 @@
+// Batched MoE FFN for many tokens at once (prefill / batched decode): the
+// grouped-expert contraction on the 5th-generation tensor cores.
+//
+// The reference has no batched path: its prefill and decode run
+// qx_apply_real_moe_layer (src/qx_format.c:5198-5310) one token at a time.
+// For N tokens this file computes the same per-token result -
+//   RMSNorm(ffn_norm) -> F32 router in double -> softmax -> top-8 (strict >,
+//   lowest index on ties) -> renormalised weights -> per selected expert
+//   IQ2_XS gate/up, SwiGLU in double, IQ3_XXS down -> rank-order weighted sum
+//   -> residual add
+// - with the expert projections done as grouped GEMMs: the tokens routed to
+// an expert form the columns of one contraction against that expert's rows.
+//
+// Exact integer contraction (the same arithmetic as the decode path,
+// qx_imma.cuh): each weight is an integer A = (1 + 2s) * g times the block
+// factor d; each activation block is a 56-bit fixed-point integer split into
+// 7 unsigned byte limbs plus a column of ones.  A (up to +-1922) does not fit
+// an int8 operand, so it is split into two int8 digits, A = 64 * hi + lo
+// (hi = A >> 6, lo = A & 63), and tcgen05.mma kind::i8 (s8 x u8 -> s32)
+// forms both digit products for a 128-row x 16-token tile (N = 16 x 8 limb
+// columns) of one 256-value block into two TMEM accumulators.  The epilogue
+// reads them back (tcgen05.ld), rebuilds the exact block integer per row and
+// token, and folds it into a double accumulator with the block factor
+// d * 2^-S.  Operands are staged in shared memory in the UMMA K-major
+// no-swizzle layout: core matrices of 8 rows x 16 bytes, 128 B apart along K
+// (LBO) and 256 B apart along M/N (SBO), one 4 KB slab per 32 values of K.
+//
+// The weights come from the step kernel's re-laid copies (IQ2R gate/up, R4
+// down: the same integers and scales as the GGUF blocks); each CTA decodes
+// its 128 rows of one block into the hi/lo slabs with byte-permute table
+// lookups, stages its tokens' limbs, and one thread issues the MMAs.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstdio>
+#include <vector>
+
+#include "qx_batch.h"
+#include "qx_common.cuh"
+
+namespace qx {
+namespace {
+
+constexpr int kGemmThreads = 128;   // 4 warps: one TMEM lane quarter each
+constexpr int kTokTile = 16;        // tokens (or expert slots) per tile: N = 128 columns
+constexpr int kRowTile = 128;       // weight rows per tile: M = 128
+constexpr int kSlab = 4096;         // bytes of one 32-value K step of a 128-row operand
+constexpr int kTmemCols = 256;      // hi accumulator in columns [0, 128), lo in [128, 256)
+constexpr uint32_t kSmemGemm = 3 * 8 * kSlab + 1024;   // A hi, A lo, B (8 K steps each) + barrier
+
+// ---- tcgen05 primitives (PTX ISA 8.7, sm_100a) ------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Shared-memory matrix descriptor, K-major, no swizzle: start address, leading
+// byte offset (next core matrix along K), stride byte offset (next 8-row group
+// along M/N), version 1 (bits 46-47), layout type 0.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor for kind::i8: D s32 (bits 4-5 = 2), A s8 (bits 7-9 =
+// 1), B u8 (bits 10-12 = 0), both K-major, N >> 3 at bits 17-22, M >> 4 at 24-28.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- operand decoding ---------------------------------------------------------
+// Byte offset of (row r, value k) of a 128-row x 256-value operand in the
+// K-major no-swizzle layout: slab k / 32, 8-row group r / 8 (256 B), core
+// matrix (k % 32) / 16 (128 B), row r % 8 (16 B), byte k % 16.
+__device__ __forceinline__ uint32_t op_off(int r, int k) {
+    return (uint32_t)((k >> 5) * kSlab + (r >> 3) * 256 + ((k >> 4) & 1) * 128 + (r & 7) * 16 + (k & 15));
+}
+
+// Word w (a compile-time index once unrolled) of a register array of uint4.
+template <int N>
+__device__ __forceinline__ uint32_t word_of(const uint4 (&v)[N], int w) {
+    const uint4 q = v[w >> 2];
+    return (w & 3) == 0 ? q.x : (w & 3) == 1 ? q.y : (w & 3) == 2 ? q.z : q.w;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
+}
+
+// IQ2R block (16 group-scale bytes 1 + 2s, then for tt = 0..3 and group gq a
+// u16 of four 3-bit codes: magnitude index 1..3 for {8, 25, 43} plus 4 when
+// negative, of values 16 gq + 4 tt + j): the 256 integers (1 + 2s) * g of one
+// row as hi/lo digits into the operand slabs.
+__device__ __forceinline__ void decode_iq2r_row(const uint8_t* blk, int r, uint8_t* ahi, uint8_t* alo) {
+    const uint4 sv = *reinterpret_cast<const uint4*>(blk);
+    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+    uint4 cw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cw[i] = *reinterpret_cast<const uint4*>(blk + 16 + 16 * i);
+    // u16 (tt, gq) at halfword 16 tt + gq
+#pragma unroll
+    for (int gq = 0; gq < 16; ++gq) {
+        const int s = (int)((sw[gq >> 2] >> (8 * (gq & 3))) & 255u);
+        const int v1 = s * 8, v2 = s * 25, v3 = s * 43;
+        const uint32_t h0 = pack4(0, v1 >> 6, v2 >> 6, v3 >> 6), h1 = pack4(0, (-v1) >> 6, (-v2) >> 6, (-v3) >> 6);
+        const uint32_t l0 = pack4(0, v1 & 63, v2 & 63, v3 & 63), l1 = pack4(0, (-v1) & 63, (-v2) & 63, (-v3) & 63);
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt) {
+            const int hwi = 16 * tt + gq;   // halfword index
+            const uint32_t q = (word_of(cw, hwi >> 1) >> (16 * (hwi & 1))) & 0xffffu;
+            hw[tt] = __byte_perm(h0, h1, q);
+            lw[tt] = __byte_perm(l0, l1, q);
+        }
+        const uint32_t o = op_off(r, 16 * gq);
+        *reinterpret_cast<uint4*>(ahi + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(alo + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+}
+
+// R4 block of IQ3_XXS origin (8 group-scale bytes 1 + 2s; then for tt = 0..3
+// and group ib a u32 whose nibbles 0..3 / 4..7 index values 32 ib + 4 tt + j /
+// 32 ib + 16 + 4 tt + j in {4, 12, ..., 52, 62} plus 8 when negative).
+__device__ __forceinline__ void lut16(uint32_t q, const uint32_t T[4], uint32_t& lo, uint32_t& hi) {
+    const uint32_t pick = ((q >> 1) & 0x44444444u) | 0x32103210u;
+    lo = __byte_perm(__byte_perm(T[0], T[1], q), __byte_perm(T[2], T[3], q), pick);
+    const uint32_t q2 = q >> 16;
+    hi = __byte_perm(__byte_perm(T[0], T[1], q2), __byte_perm(T[2], T[3], q2), pick >> 16);
+}
+
+__device__ __forceinline__ void decode_r4iq3_row(const uint8_t* scales, const uint8_t* codes, int r, uint8_t* ahi,
+                                                 uint8_t* alo) {
+    const uint2 sv = *reinterpret_cast<const uint2*>(scales);
+    uint4 cw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cw[i] = *reinterpret_cast<const uint4*>(codes + 16 * i);
+    // u32 (tt, ib) at word 8 tt + ib
+    constexpr int kMag[8] = {4, 12, 20, 28, 36, 44, 52, 62};
+#pragma unroll
+    for (int ib = 0; ib < 8; ++ib) {
+        const int s = (int)(((ib < 4 ? sv.x : sv.y) >> (8 * (ib & 3))) & 255u);
+        int v[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) v[c] = s * kMag[c];
+        const uint32_t Th[4] = {pack4(v[0] >> 6, v[1] >> 6, v[2] >> 6, v[3] >> 6),
+                                pack4(v[4] >> 6, v[5] >> 6, v[6] >> 6, v[7] >> 6),
+                                pack4((-v[0]) >> 6, (-v[1]) >> 6, (-v[2]) >> 6, (-v[3]) >> 6),
+                                pack4((-v[4]) >> 6, (-v[5]) >> 6, (-v[6]) >> 6, (-v[7]) >> 6)};
+        const uint32_t Tl[4] = {pack4(v[0] & 63, v[1] & 63, v[2] & 63, v[3] & 63),
+                                pack4(v[4] & 63, v[5] & 63, v[6] & 63, v[7] & 63),
+                                pack4((-v[0]) & 63, (-v[1]) & 63, (-v[2]) & 63, (-v[3]) & 63),
+                                pack4((-v[4]) & 63, (-v[5]) & 63, (-v[6]) & 63, (-v[7]) & 63)};
+        uint32_t h0[4], h1[4], l0[4], l1[4];
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt) {
+            const uint32_t q = word_of(cw, 8 * tt + ib);
+            lut16(q, Th, h0[tt], h1[tt]);
+            lut16(q, Tl, l0[tt], l1[tt]);
+        }
+        const uint32_t o = op_off(r, 32 * ib);
+        *reinterpret_cast<uint4*>(ahi + o) = make_uint4(h0[0], h0[1], h0[2], h0[3]);
+        *reinterpret_cast<uint4*>(ahi + o + 128) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
+        *reinterpret_cast<uint4*>(alo + o) = make_uint4(l0[0], l0[1], l0[2], l0[3]);
+        *reinterpret_cast<uint4*>(alo + o + 128) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
+    }
+}
+
+// ---- the grouped GEMM ---------------------------------------------------------
+// One CTA: 128 rows [row0, row0 + 128) of one expert matrix against up to 16
+// columns (expert slots, or tokens for gate/up) of the item.  Per 256-value
+// block: decode A (hi/lo), stage B, 16 MMAs (8 K steps x 2 digits), commit,
+// fold the accumulators.  Output out[col * out_stride + row] = the dot
+// product as a float (non-finite -> 0, src/qx_format.c:4783).
+__global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~(uintptr_t)1023);
+    uint8_t* ahi = base;
+    uint8_t* alo = base + 8 * kSlab;
+    uint8_t* bop = base + 16 * kSlab;
+    __shared__ __align__(8) uint64_t mbar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int cols_s[kTokTile], bidx_s[kTokTile];
+    __shared__ int sexp_s[kTokTile][8];
+    const GemmItem it = a.items[blockIdx.x];
+    const int r = threadIdx.x, warp = r >> 5, ncol = it.ncols;
+    if (r < kTokTile) {
+        const int c = r < ncol ? a.cols[it.col0 + r] : -1;
+        cols_s[r] = c;
+        bidx_s[r] = c < 0 ? -1 : (a.b_by_token ? c / 8 : c);
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base_s)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (r == 0) {
+        asm volatile("mbarrier.init.shared.b64 [%0], 1;" ::"r"(smem_addr(&mbar)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // columns beyond the item stay zero in every block (no limbs, no ones)
+    for (int i = r; i < 8 * kSlab / 16; i += kGemmThreads) reinterpret_cast<uint4*>(bop)[i] = make_uint4(0, 0, 0, 0);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = tmem_base_s;
+    for (int i = r; i < kTokTile * a.nblk; i += kGemmThreads) {
+        const int j = i / a.nblk, b = i % a.nblk;
+        sexp_s[j][b] = bidx_s[j] < 0 ? 0 : a.sexp[(size_t)bidx_s[j] * a.nblk + b];
+    }
+    const uint8_t* mat = a.weights + (size_t)it.expert * a.expert_stride + (size_t)(it.row0 + r) * a.row_bytes;
+    const uint32_t idesc = idesc_i8(kRowTile, 8 * kTokTile);
+    double acc[kTokTile];
+#pragma unroll
+    for (int j = 0; j < kTokTile; ++j) acc[j] = 0.0;
+    unsigned phase = 0;
+    bool ok = true;
+    for (int b = 0; b < a.nblk && ok; ++b) {
+        // B: each column's 2 KB of block b (8 slabs x 256 B: limbs 0-6 and the
+        // ones column of 32 values) to slab s, 8-row group j
+        for (int i = r; i < kTokTile * 128; i += kGemmThreads) {
+            const int j = i >> 7, c16 = i & 127;
+            if (bidx_s[j] < 0) continue;
+            const int s = c16 >> 4, w = c16 & 15;
+            cp_async16(bop + s * kSlab + j * 256 + w * 16,
+                       a.bq + ((size_t)bidx_s[j] * a.nblk + b) * 2048 + s * 256 + w * 16);
+        }
+        cp_async_commit();
+        // A: this thread's row of block b
+        if (a.fmt == kGemmIq2r) {
+            decode_iq2r_row(mat + a.hdr + (size_t)b * 144, r, ahi, alo);
+        } else {
+            decode_r4iq3_row(mat + a.hdr + 8 * b, mat + a.codes + 128 * b, r, ahi, alo);
+        }
+        cp_async_wait<0>();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core
+        __syncthreads();
+        if (r == 0) {
+            tc_fence_after();
+            const uint32_t ah = smem_addr(ahi), al = smem_addr(alo), bb = smem_addr(bop);
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+                const uint64_t bd = umma_desc(bb + s * kSlab, 128, 256);
+                mma_i8(tbase, umma_desc(ah + s * kSlab, 128, 256), bd, idesc, s > 0);
+                mma_i8(tbase + 128, umma_desc(al + s * kSlab, 128, 256), bd, idesc, s > 0);
+            }
+            mma_commit(&mbar);
+        }
+        // bounded wait for the MMAs (2 s; a healthy block takes microseconds);
+        // every thread agrees on the outcome before it touches TMEM
+        {
+            const unsigned long long t0 = gtimer();
+            uint32_t done = 0;
+            while (!done) {
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+                    : "=r"(done)
+                    : "r"(smem_addr(&mbar)), "r"(phase)
+                    : "memory");
+                if (!done && gtimer() - t0 > 2000000000ull) break;
+            }
+            ok = __syncthreads_and((int)done) != 0;
+            if (!ok && r == 0) atomicOr(a.err, kErrTimeout);
+            phase ^= 1u;
+        }
+        tc_fence_after();
+        if (ok) {
+            // fold: column j's exact block integer X = sum_n c_n 2^(8n) (limb 6
+            // minus 128 x the ones column removes the 2^55 offset) times
+            // d * 2^(fexp - S_j)
+            const double dfac = (double)h2f(*reinterpret_cast<const uint16_t*>(mat + 2 * b));
+            const uint32_t lane_addr = tbase + ((uint32_t)(32 * warp) << 16);
+#pragma unroll
+            for (int p = 0; p < kTokTile / 2; ++p) {
+                uint32_t hv[16], lv[16];
+                tmem_ld16(lane_addr + 16 * p, hv);
+                tmem_ld16(lane_addr + 128 + 16 * p, lv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    int c[8];
+#pragma unroll
+                    for (int n = 0; n < 8; ++n) c[n] = 64 * (int)hv[8 * h + n] + (int)lv[8 * h + n];
+                    c[6] -= 128 * c[7];
+                    const long long plo = (long long)c[0] + ((long long)c[1] << 8) + ((long long)c[2] << 16) +
+                                          ((long long)c[3] << 24);
+                    const long long phi = (long long)c[4] + ((long long)c[5] << 8) + ((long long)c[6] << 16);
+                    const int j = 2 * p + h;
+                    const double f = dfac * blk_pow2(sexp_s[j][b], a.fexp);
+                    acc[j] = fma((double)phi, f * 4294967296.0, acc[j]);
+                    acc[j] = fma((double)plo, f, acc[j]);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();   // the accumulators and slabs are free for the next block
+    }
+    if (ok) {
+#pragma unroll
+        for (int j = 0; j < kTokTile; ++j) {
+            const double v = acc[j];
+            if (j < ncol) a.out[(size_t)cols_s[j] * a.out_stride + a.out_off + it.row0 + r] = isfinite(v) ? (float)v : 0.0f;
+        }
+    }
+    tc_fence_after();
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTmemCols) : "memory");
+}
+
+// ---- activations -------------------------------------------------------------
+// RMSNorm (ffn_norm, src/qx_format.c:3358-3371) of every token, CTA per token.
+__global__ void __launch_bounds__(256) k_batch_norm(const float* x, const float* w, float* xn, int H) {
+    __shared__ double scratch[8];
+    const float* xt = x + (size_t)blockIdx.x * H;
+    float* yt = xn + (size_t)blockIdx.x * H;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += (double)xt[i] * (double)xt[i];
+    ss = block_sum_d(ss, scratch);
+    const double rms = sqrt(ss / (double)H + 1.0e-6);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) yt[i] = (float)((double)xt[i] / rms) * w[i];
+}
+
+// Fixed-point limbs of every 256-value block of rows x[n][K] in the GEMM's B
+// layout: per row and block 2 KB = 8 slabs (32 values) of 8 limb rows x 32
+// bytes (two 16-byte core-matrix rows), limb 7 the ones column; one warp per
+// (row, half block), the same rounding as build_xq.
+__global__ void __launch_bounds__(256) k_batch_limbs(const float* x, int K, int nrows, uint8_t* bq, int* sexp) {
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nblk = K / 256;
+    if (item >= nrows * nblk * 2) return;
+    const int h = item & 1, b = (item >> 1) % nblk, t = (item >> 1) / nblk;
+    const float* xs = x + (size_t)t * K + b * 256;
+    const float4 u = reinterpret_cast<const float4*>(xs)[lane];
+    const float4 v = reinterpret_cast<const float4*>(xs + 128)[lane];
+    float mx = fmaxf(fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))),
+                     fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const bool fin = isfinite(u.x) && isfinite(u.y) && isfinite(u.z) && isfinite(u.w) && isfinite(v.x) &&
+                     isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+    const int E = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 255u) - 127 : -126;
+    const int S = __all_sync(0xffffffffu, fin) ? 54 - (E < -126 ? -126 : E) : kSbNonFinite;
+    if (lane == 0 && h == 0) sexp[(size_t)t * nblk + b] = S;
+    const float4 q = h ? v : u;
+    const int Sq = S == kSbNonFinite ? 0 : S;
+    uint32_t hi[4], lo[4], w[4];
+    to_fixed(q.x, Sq, hi[0], lo[0]);
+    to_fixed(q.y, Sq, hi[1], lo[1]);
+    to_fixed(q.z, Sq, hi[2], lo[2]);
+    to_fixed(q.w, Sq, hi[3], lo[3]);
+    const int k0 = 128 * h + 4 * lane;   // values k0 .. k0 + 3 of the block
+    uint8_t* dst = bq + ((size_t)t * nblk + b) * 2048 + (k0 >> 5) * 256 + ((k0 >> 4) & 1) * 128 + (k0 & 15);
+    transpose4(lo[0], lo[1], lo[2], lo[3], w);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) *reinterpret_cast<uint32_t*>(dst + 16 * n) = w[n];
+    transpose4(hi[0], hi[1], hi[2], hi[3], w);
+#pragma unroll
+    for (int n = 0; n < 3; ++n) *reinterpret_cast<uint32_t*>(dst + 16 * (4 + n)) = w[n];
+    *reinterpret_cast<uint32_t*>(dst + 16 * 7) = 0x01010101u;
+}
+
+// F32 router in double, softmax in double, top-8 by repeated strict-> scans
+// (lowest index on ties) and renormalisation, per token
+// (src/qx_format.c:5253-5287): one CTA per token, one warp per expert row.
+__global__ void __launch_bounds__(256) k_batch_router(const float* xn, const float* router, int H, int E, int* sel,
+                                                      double* wsel, int* err) {
+    __shared__ double logit[256];
+    __shared__ double prob[256];
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* x = xn + (size_t)t * H;
+    for (int e = warp; e < E; e += blockDim.x >> 5) {
+        const float* row = router + (size_t)e * H;
+        double acc = 0.0;
+        for (int i = lane; i < H; i += 32) acc = fma((double)row[i], (double)x[i], acc);
+        acc = warp_sum_d(acc);
+        if (lane == 0) logit[e] = acc;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    double m = -1.0e300;
+    for (int e = lane; e < E; e += 32) m = fmax(m, logit[e]);
+    for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+    double s = 0.0;
+    for (int e = lane; e < E; e += 32) {
+        const double p = exp(logit[e] - m);
+        prob[e] = p;
+        s += p;
+    }
+    s = warp_sum_d(s);
+    for (int e = lane; e < E; e += 32) prob[e] /= s;
+    __syncwarp();
+    double ws[8];
+    int picked = 0;   // bit per lane-held expert e = lane + 32 k (k < 8)
+    double sum = 0.0;
+    for (int k = 0; k < 8; ++k) {
+        double bv = -1.0;
+        int bi = 0x7fffffff;
+        for (int e = lane, q = 0; e < E; e += 32, ++q)
+            if (!((picked >> q) & 1) && (prob[e] > bv || (prob[e] == bv && e < bi))) { bv = prob[e]; bi = e; }
+        for (int o = 16; o; o >>= 1) {
+            const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if ((bi & 31) == lane) picked |= 1 << (bi >> 5);
+        ws[k] = bv;
+        sum += bv;
+        if (lane == 0) sel[t * 8 + k] = bi;
+    }
+    if (lane == 0) {
+        if (!(sum > 0.0) || !isfinite(sum)) atomicOr(err, kErrRouter);
+        for (int k = 0; k < 8; ++k) wsel[t * 8 + k] = ws[k] / sum;
+    }
+}
+
+// SwiGLU in double (src/qx_format.c:5297, qx_silu :2511-2513) of every expert
+// slot: gu[slot][0 .. I) = gate, [I .. 2I) = up.
+__global__ void k_batch_swiglu(const float* gu, int I, int nslots, float* h) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)nslots * I) return;
+    const size_t s = i / I, k = i % I;
+    const double gd = (double)gu[s * 2 * I + k];
+    h[i] = (float)(gd / (1.0 + exp(-gd)) * (double)gu[s * 2 * I + I + k]);
+}
+
+// out = residual + sum over ranks k = 0..7 (in order) of (float)(w_k * y_k)
+// (src/qx_format.c:5303-5309).
+__global__ void k_batch_combine(const float* x, const float* y, const double* wsel, int H, int ntok, float* moe,
+                                float* out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)ntok * H) return;
+    const size_t t = i / H, c = i % H;
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m += (float)(wsel[t * 8 + k] * (double)y[(t * 8 + k) * H + c]);
+    if (moe) moe[i] = m;
+    out[i] = x[i] + m;
+}
+
+}  // namespace
+
+uint32_t moe_gemm_smem_bytes() { return kSmemGemm; }
+
+cudaError_t moe_batch_configure() {
+    return cudaFuncSetAttribute(k_moe_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemGemm);
+}
+
+void launch_batch_norm(const float* x, const float* w, float* xn, int H, int ntok, cudaStream_t st) {
+    k_batch_norm<<<ntok, 256, 0, st>>>(x, w, xn, H);
+}
+
+void launch_batch_limbs(const float* x, int K, int nrows, uint8_t* bq, int* sexp, cudaStream_t st) {
+    const int warps = nrows * (K / 256) * 2;
+    k_batch_limbs<<<(warps + 7) / 8, 256, 0, st>>>(x, K, nrows, bq, sexp);
+}
+
+void launch_batch_router(const float* xn, const float* router, int H, int E, int ntok, int* sel, double* wsel, int* err,
+                         cudaStream_t st) {
+    k_batch_router<<<ntok, 256, 0, st>>>(xn, router, H, E, sel, wsel, err);
+}
+
+void launch_moe_gemm(const GemmArgs& a, int nitems, cudaStream_t st) {
+    if (nitems > 0) k_moe_gemm<<<nitems, kGemmThreads, kSmemGemm, st>>>(a);
+}
+
+void launch_batch_swiglu(const float* gu, int I, int nslots, float* h, cudaStream_t st) {
+    const size_t n = (size_t)nslots * I;
+    k_batch_swiglu<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(gu, I, nslots, h);
+}
+
+void launch_batch_combine(const float* x, const float* y, const double* wsel, int H, int ntok, float* moe, float* out,
+                          cudaStream_t st) {
+    const size_t n = (size_t)ntok * H;
+    k_batch_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, wsel, H, ntok, moe, out);
+}
+
+}  // namespace qx

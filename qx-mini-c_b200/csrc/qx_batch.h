@@ -1,0 +1,48 @@
+// Batched MoE FFN (qx_batch.cu): the grouped-expert GEMMs on tcgen05 and the
+// per-token kernels around them.  Internal to the engine; not part of the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace qx {
+
+// One CTA of the grouped GEMM: rows [row0, row0 + 128) of expert `expert`
+// against the columns cols[col0 .. col0 + ncols) (ncols <= 16).
+struct GemmItem {
+    int expert, col0, ncols, row0;
+};
+enum { kGemmIq2r = 0, kGemmR4Iq3 = 1 };
+
+struct GemmArgs {
+    const GemmItem* items;
+    const int* cols;              // column ids: expert slots t * 8 + k, grouped by expert
+    const uint8_t* weights;       // re-laid expert stack (IQ2R or R4 rows)
+    size_t expert_stride;         // bytes per expert
+    uint32_t row_bytes;
+    int hdr;                      // IQ2R: first block; R4: first scale byte
+    int codes;                    // R4: first code byte
+    int nblk;                     // 256-value blocks per row (K / 256)
+    int fmt;                      // kGemmIq2r or kGemmR4Iq3
+    int fexp;                     // block factor d * 2^(fexp - S): -3 (IQ2_XS), -2 (IQ3_XXS)
+    const uint8_t* bq;            // limbs [rows][nblk][2048 B] (k_batch_limbs)
+    const int* sexp;              // block exponents [rows][nblk]
+    int b_by_token;               // 1: B row = column id / 8 (the token), 0: B row = column id
+    float* out;                   // out[col * out_stride + out_off + row]
+    size_t out_stride;
+    int out_off;
+    int* err;
+};
+
+uint32_t moe_gemm_smem_bytes();
+cudaError_t moe_batch_configure();
+void launch_batch_norm(const float* x, const float* w, float* xn, int H, int ntok, cudaStream_t st);
+void launch_batch_limbs(const float* x, int K, int nrows, uint8_t* bq, int* sexp, cudaStream_t st);
+void launch_batch_router(const float* xn, const float* router, int H, int E, int ntok, int* sel, double* wsel, int* err,
+                         cudaStream_t st);
+void launch_moe_gemm(const GemmArgs& a, int nitems, cudaStream_t st);
+void launch_batch_swiglu(const float* gu, int I, int nslots, float* h, cudaStream_t st);
+void launch_batch_combine(const float* x, const float* y, const double* wsel, int H, int ntok, float* moe, float* out,
+                          cudaStream_t st);
+
+}  // namespace qx

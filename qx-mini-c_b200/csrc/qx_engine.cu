@@ -18,6 +18,7 @@
 
 #include "qx_cuda.h"
 #include "qx_host.h"
+#include "qx_batch.h"
 #include "qx_kernels.h"
 
 #define QX_API extern "C" __attribute__((visibility("default")))
@@ -76,6 +77,17 @@ struct qx_cuda_engine {
     float* d_topv = nullptr;
     float* d_norm = nullptr;
     qx_cuda_profile prof{};
+    // batched MoE (qx_cuda_moe_batch): one allocation sized for `cap` tokens
+    struct Batch {
+        size_t cap = 0;
+        void* mem = nullptr;
+        float *x, *xn, *gu, *h, *y, *out, *moe;
+        uint8_t *bqx, *bqh;
+        int *sx, *sh, *sel, *cols;
+        double* wsel;
+        qx::GemmItem* items;
+        size_t item_cap;
+    } batch;
 };
 
 namespace {
@@ -191,6 +203,7 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->work) cudaFree(E->work);
     if (E->layers_dev) cudaFree(E->layers_dev);
     if (E->relay) cudaFree(E->relay);
+    if (E->batch.mem) cudaFree(E->batch.mem);
     for (void* p : E->ep_opened) cudaIpcCloseMemHandle(p);
     if (E->ep_xchg) cudaFree(E->ep_xchg);
     if (E->ep_peers_dev) cudaFree(E->ep_peers_dev);
@@ -320,6 +333,7 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
         E->own_stream = true;
     }
     ce = qx::configure_kernels();
+    if (ce == cudaSuccess) ce = qx::moe_batch_configure();
     if (ce != cudaSuccess) return fail(ce, "cudaFuncSetAttribute");
 
     // weight arena: every tensor, 256-byte aligned, in its native layout
@@ -801,6 +815,150 @@ QX_API int qx_cuda_moe_layer(qx_cuda_engine* E, uint32_t layer, const float* x, 
         !d2h(E, moe_output, E->dev.moe_out, (size_t)E->dm.hidden * 4, err, n) ||
         !d2h(E, selected, E->dev.sel + layer * 8, 32, err, n) || !d2h(E, weights, E->dev.selw + layer * 8, 32, err, n))
         return 0;
+    return finish(E, err, n) ? 1 : 0;
+}
+
+// ---- batched MoE: N tokens through one MoE layer on the grouped tcgen05 GEMM ----
+namespace {
+
+bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
+    auto& B = E->batch;
+    if (B.cap >= ntok) return true;
+    if (B.mem) { cudaFree(B.mem); B.mem = nullptr; B.cap = 0; }
+    const size_t H = E->dm.hidden, I = E->dm.moe_inter, S = ntok * 8;
+    const size_t items = (S / 16 + (size_t)E->dm.experts) * std::max(2 * I / 128, H / 128);
+    size_t off = 0;
+    std::vector<std::pair<void**, size_t>> parts = {
+        {(void**)&B.x, ntok * H * 4}, {(void**)&B.xn, ntok * H * 4}, {(void**)&B.out, ntok * H * 4},
+        {(void**)&B.moe, ntok * H * 4}, {(void**)&B.gu, S * 2 * I * 4}, {(void**)&B.h, S * I * 4},
+        {(void**)&B.y, S * H * 4}, {(void**)&B.bqx, ntok * (H / 256) * 2048}, {(void**)&B.bqh, S * (I / 256) * 2048},
+        {(void**)&B.sx, ntok * (H / 256) * 4}, {(void**)&B.sh, S * (I / 256) * 4}, {(void**)&B.sel, S * 4},
+        {(void**)&B.cols, S * 4}, {(void**)&B.wsel, S * 8}, {(void**)&B.items, items * sizeof(qx::GemmItem)}};
+    for (auto& p : parts) off = align_up(off + p.second, 256);
+    if (!cuda_ok(cudaMalloc(&B.mem, off), "cudaMalloc(batch)", err, n)) return false;
+    off = 0;
+    for (auto& p : parts) {
+        *p.first = (uint8_t*)B.mem + off;
+        off = align_up(off + p.second, 256);
+    }
+    B.cap = ntok;
+    B.item_cap = items;
+    return true;
+}
+
+}  // namespace
+
+QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, const float* x, float* layer_output,
+                             float* moe_output, uint32_t* selected, float* weights, char* err, uint64_t n) {
+    if (!E || !x || !layer_output || layer >= (uint32_t)E->dm.layers || ntok == 0 || ntok > QX_CUDA_MAX_BATCH) {
+        set_err(err, n, "invalid batched expert argument");
+        return 0;
+    }
+    const LayerW& w = E->layers[layer];
+    const int H = E->dm.hidden, I = E->dm.moe_inter, EX = E->dm.experts;
+    if (!w.gate_r || !w.up_r || !w.down_r || w.tgate != 17 || w.tup != 17 || w.tdown != 18 || H % 128 || I % 128) {
+        set_err(err, n, "batched experts need the IQ2_XS/IQ3_XXS mix in the one-launch step kernel's layouts");
+        return 0;
+    }
+    DeviceGuard g(E->device);
+    if (!batch_reserve(E, ntok, err, n)) return 0;
+    auto& B = E->batch;
+    const int N = (int)ntok, S = N * 8;
+    if (!h2d(E, B.x, x, (size_t)N * H * 4, err, n)) return 0;
+    // norm, activation limbs, router + top-8 (every token)
+    qx::launch_batch_norm(B.x, w.ffn_norm, B.xn, H, N, E->stream);
+    qx::launch_batch_limbs(B.xn, H, N, B.bqx, B.sx, E->stream);
+    qx::launch_batch_router(B.xn, w.router, H, EX, N, B.sel, B.wsel, E->dev.err, E->stream);
+    E->prof.kernel_launches += 3;
+    // the slots (token, rank) of every expert, in token order
+    std::vector<int> sel(S);
+    if (!cuda_ok(cudaMemcpyAsync(sel.data(), B.sel, (size_t)S * 4, cudaMemcpyDeviceToHost, E->stream), "d2h", err, n) ||
+        !cuda_ok(cudaStreamSynchronize(E->stream), "router", err, n))
+        return 0;
+    E->prof.device_to_host_bytes += (uint64_t)S * 4;
+    std::vector<int> count(EX, 0), start(EX + 1, 0), cols(S);
+    for (int s = 0; s < S; ++s) {
+        if (sel[s] < 0 || sel[s] >= EX) { set_err(err, n, "invalid selected router weights"); return 0; }
+        count[sel[s]]++;
+    }
+    for (int e = 0; e < EX; ++e) start[e + 1] = start[e] + count[e];
+    {
+        std::vector<int> fill(start.begin(), start.end() - 1);
+        for (int s = 0; s < S; ++s) cols[fill[sel[s]]++] = s;
+    }
+    std::vector<qx::GemmItem> items;
+    auto make_items = [&](int rows) {
+        items.clear();
+        for (int e = 0; e < EX; ++e)
+            for (int c0 = start[e]; c0 < start[e + 1]; c0 += 16)
+                for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({e, c0, std::min(16, start[e + 1] - c0), r0});
+    };
+    if (!h2d(E, B.cols, cols.data(), (size_t)S * 4, err, n)) return 0;
+    // gate and up: rows of I values of K = H, columns = slots, B = the token's limbs
+    make_items(I);
+    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return 0; }
+    if (!h2d(E, B.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return 0;
+    const size_t rb2 = qx::iq2r_row_bytes(H);
+    qx::GemmArgs ga{};
+    ga.items = B.items;
+    ga.cols = B.cols;
+    ga.expert_stride = (size_t)I * rb2;
+    ga.row_bytes = (uint32_t)rb2;
+    ga.hdr = (int)(rb2 - (size_t)(H / 256) * 144);
+    ga.nblk = H / 256;
+    ga.fmt = qx::kGemmIq2r;
+    ga.fexp = -3;
+    ga.bq = B.bqx;
+    ga.sexp = B.sx;
+    ga.b_by_token = 1;
+    ga.out = B.gu;
+    ga.out_stride = (size_t)2 * I;
+    ga.err = E->dev.err;
+    ga.weights = w.gate_r;
+    ga.out_off = 0;
+    qx::launch_moe_gemm(ga, (int)items.size(), E->stream);
+    ga.weights = w.up_r;
+    ga.out_off = I;
+    qx::launch_moe_gemm(ga, (int)items.size(), E->stream);
+    // SwiGLU, then the down input's limbs per slot
+    qx::launch_batch_swiglu(B.gu, I, S, B.h, E->stream);
+    qx::launch_batch_limbs(B.h, I, S, B.bqh, B.sh, E->stream);
+    // down: rows of H values of K = I, columns = slots, B = the slot's limbs
+    make_items(H);
+    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return 0; }
+    qx::GemmItem* items2 = B.items;
+    if (!h2d(E, items2, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return 0;
+    const size_t rb4 = qx::r4_bytes_per_row(I);
+    qx::GemmArgs gd = ga;
+    gd.items = items2;
+    gd.weights = w.down_r;
+    gd.expert_stride = (size_t)H * rb4;
+    gd.row_bytes = (uint32_t)rb4;
+    gd.hdr = (2 * (I / 256) + 15) / 16 * 16;
+    gd.codes = (gd.hdr + 8 * (I / 256) + 15) / 16 * 16;
+    gd.nblk = I / 256;
+    gd.fmt = qx::kGemmR4Iq3;
+    gd.fexp = -2;
+    gd.bq = B.bqh;
+    gd.sexp = B.sh;
+    gd.b_by_token = 0;
+    gd.out = B.y;
+    gd.out_stride = (size_t)H;
+    gd.out_off = 0;
+    qx::launch_moe_gemm(gd, (int)items.size(), E->stream);
+    qx::launch_batch_combine(B.x, B.y, B.wsel, H, N, B.moe, B.out, E->stream);
+    E->prof.kernel_launches += 6;
+    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    if (!d2h(E, layer_output, B.out, (size_t)N * H * 4, err, n) ||
+        !d2h(E, moe_output, B.moe, (size_t)N * H * 4, err, n) ||
+        !d2h(E, selected, B.sel, (size_t)S * 4, err, n))
+        return 0;
+    if (weights) {
+        std::vector<double> wd(S);
+        if (!d2h(E, wd.data(), B.wsel, (size_t)S * 8, err, n) || !finish(E, err, n)) return 0;
+        for (int s = 0; s < S; ++s) weights[s] = (float)wd[s];
+        return 1;
+    }
     return finish(E, err, n) ? 1 : 0;
 }
 

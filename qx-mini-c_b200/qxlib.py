@@ -126,6 +126,7 @@ ENGINE_SYMBOLS = [
     "qx_cuda_moe_layer", "qx_cuda_attention_layer", "qx_cuda_embed", "qx_cuda_kv_write", "qx_cuda_kv_read",
     "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_phase_trace", "qx_cuda_stream",
     "qx_cuda_ep_handle", "qx_cuda_ep_connect", "qx_cuda_ep_partition", "qx_cuda_kv_export", "qx_cuda_kv_import",
+    "qx_cuda_moe_batch",
 ]
 
 VERIFY_CHECKSUMS = 0x1
@@ -148,6 +149,7 @@ def cuda():
             "qx_cuda_generate": [P, U32, U32, U32, P, E, U64],
             "qx_cuda_final_head": [P, P, P, P, U32, P, P, E, U64],
             "qx_cuda_moe_layer": [P, U32, P, P, P, P, P, E, U64],
+            "qx_cuda_moe_batch": [P, U32, U32, P, P, P, P, P, E, U64],
             "qx_cuda_attention_layer": [P, U32, U32, P, P, P, E, U64],
             "qx_cuda_embed": [P, U32, P, E, U64],
             "qx_cuda_kv_write": [P, U32, U32, U32, P, P, P, P, E, U64],
@@ -331,6 +333,18 @@ class Engine:
         sel = np.zeros(8, np.uint32)
         w = np.zeros(8, np.float32)
         self._call("qx_cuda_moe_layer", layer, _p(x), _p(out), _p(moe), _p(sel), _p(w))
+        return out, moe, sel, w
+
+    def moe_batch(self, layer, x):
+        """x: [tokens][hidden] residuals; returns (layer_output, moe_output,
+        selected [tokens][8], weights [tokens][8]) of qx_cuda_moe_batch."""
+        x = np.ascontiguousarray(x, np.float32)
+        t = x.shape[0]
+        out = np.zeros_like(x)
+        moe = np.zeros_like(x)
+        sel = np.zeros((t, 8), np.uint32)
+        w = np.zeros((t, 8), np.float32)
+        self._call("qx_cuda_moe_batch", layer, t, _p(x), _p(out), _p(moe), _p(sel), _p(w))
         return out, moe, sel, w
 
     def attention_layer(self, layer, position, residual):
