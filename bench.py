@@ -234,59 +234,109 @@ def ncu_traffic(kernel, algorithmic_bytes):
     return None
 
 
-def run_stage(args):
-    """Configs 1-3: time one stage entry point (qx_cuda_final_head /
-    qx_cuda_moe_layer / qx_cuda_attention_layer) on the device with CUDA events
-    on the engine stream; each call streams that stage's weights from HBM
-    (config 3: attention history of 4095 positions pre-filled)."""
+def time_call(call, stream, reps, warmup=3):
+    """Median device time (us) of one host call, CUDA events on the engine
+    stream around it (the call's own input/output copies included)."""
     import torch
-    torch.cuda.set_device(0)
-    cfg = W.model_config(full=True)
-    img = qxlib.build_image(cfg)
-    H, I = cfg.hidden, cfg.moe_intermediate
-    Q, KV = cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
-    eng = qxlib.Engine(img, ctx=4096, device=0)
-    stream = torch.cuda.ExternalStream(eng.stream())
-    rng = np.random.default_rng(3)
-    if args.workload == "head":
-        x = W.head_input(H)
-        call = lambda: eng.final_head(x, 1)
-        nbytes = cfg.vocab * (H // 256) * 210 + 2 * H * 4
-        what = "config1: Q6_K head 151936x2048 + final RMSNorm + argmax"
-    elif args.workload == "moe":
-        x = W.moe_input(H)
-        call = lambda: eng.moe_layer(W.MOE_LAYER, x)
-        nbytes = cfg.experts * H * 4 + 8 * (2 * I * (H // 256) * 74 + H * (I // 256) * 98) + H * 4
-        what = "config2: one MoE layer (F32 router, top-8, IQ2_XS gate/up + SwiGLU, IQ3_XXS down)"
-    else:
-        P = 4095
-        k = rng.integers(-127, 128, (P, KV), dtype=np.int8)
-        v = rng.integers(-127, 128, (P, KV), dtype=np.int8)
-        sc = (rng.random(P, dtype=np.float32) * 0.02 + 0.01).astype(np.float32)
-        eng.kv_write(W.ATTN_LAYER, 0, k, v, sc, sc)
-        x = W.attn_input(H)
-        call = lambda: eng.attention_layer(W.ATTN_LAYER, P, x)
-        nbytes = (Q + 2 * KV) * (H // 256) * 136 + H * (Q // 256) * 136 + (P + 1) * (2 * KV + 8)
-        what = "config3: attention layer at ctx 4096 (IQ4_XS QKV/O, INT8 KV history)"
-    for _ in range(max(3, args.warmup)):
+    for _ in range(warmup):
         call()
     torch.cuda.synchronize()
-    # one event pair per call (the calls return to the host in between), median
     times = []
-    for _ in range(args.steps):
+    for _ in range(reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         call()
         e1.record(stream)
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1) * 1000.0)
-    us = float(np.median(times))
+    return float(np.median(times))
+
+
+def stage_configs(eng, cfg, stream, reps=10, which=("head", "moe", "attention", "decode4096", "batch")):
+    """BASELINE configs 1, 2, 3 (ctx 512 and 4096), 4 at ctx 4096 and 5
+    (the batched grouped-expert MoE layer at 64 and 2048 tokens) through the
+    engine's entry points, on one GPU.  Each entry streams its weights from
+    HBM; the GB/s and TFLOP/s figures count the algorithmic bytes (GGUF) and
+    the useful multiply-adds (2 per weight per token)."""
     peak, peak_kind = peaks()
-    gbs = nbytes / us / 1e3
-    print(json.dumps({"workload": args.workload, "config": what, "us_per_call": us, "algorithmic_bytes": nbytes,
-                      "GB/s": gbs, "frac_of_measured_hbm": gbs / peak, "peak_source": peak_kind,
-                      "note": "device time of the whole entry point (kernels + 8 KB input/output copies)",
-                      "steps": args.steps}))
+    bf16 = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16 = float(json.load(f)["bf16_tflops_sustained"])
+    except Exception:
+        bf16 = 1400.0
+    H, I, E = cfg.hidden, cfg.moe_intermediate, cfg.experts
+    Q, KV = cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    rng = np.random.default_rng(3)
+    out = {}
+
+    def hbm(name, us, nbytes, what):
+        gbs = nbytes / us / 1e3
+        out[name] = {"config": what, "us_per_call": round(us, 2), "algorithmic_bytes": int(nbytes),
+                     "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4)}
+
+    if "head" in which:
+        x = W.head_input(H)
+        hbm("config1_head", time_call(lambda: eng.final_head(x, 1), stream, reps),
+            cfg.vocab * (H // 256) * 210 + 2 * H * 4, "Q6_K head 151936x2048 + final RMSNorm + argmax")
+    if "moe" in which:
+        x = W.moe_input(H)
+        hbm("config2_moe", time_call(lambda: eng.moe_layer(W.MOE_LAYER, x), stream, reps),
+            E * H * 4 + 8 * (2 * I * (H // 256) * 74 + H * (I // 256) * 98) + H * 4,
+            "one MoE layer: F32 router, top-8, IQ2_XS gate/up + SwiGLU, IQ3_XXS down")
+    if "attention" in which:
+        for P in (511, 4095):
+            k = rng.integers(-127, 128, (P, KV), dtype=np.int8)
+            v = rng.integers(-127, 128, (P, KV), dtype=np.int8)
+            sc = (rng.random(P, dtype=np.float32) * 0.02 + 0.01).astype(np.float32)
+            eng.kv_write(W.ATTN_LAYER, 0, k, v, sc, sc)
+            x = W.attn_input(H)
+            hbm("config3_attention_ctx%d" % (P + 1),
+                time_call(lambda: eng.attention_layer(W.ATTN_LAYER, P, x), stream, reps),
+                (Q + 2 * KV) * (H // 256) * 136 + H * (Q // 256) * 136 + (P + 1) * (2 * KV + 8),
+                "attention layer at ctx %d (IQ4_XS QKV/O, INT8 KV history)" % (P + 1))
+    if "decode4096" in which and eng.ctx >= 4096:
+        first, steps = 3840, 256
+        for layer in range(cfg.layers):
+            k = rng.integers(-127, 128, (first, KV), dtype=np.int8)
+            v = rng.integers(-127, 128, (first, KV), dtype=np.int8)
+            sc = (rng.random(first, dtype=np.float32) * 0.02 + 0.005).astype(np.float32)
+            eng.kv_write(layer, 0, k, v, sc, sc)
+        us = time_call(lambda: eng.generate(W.START_TOKEN, first, steps), stream, 3, warmup=1)
+        tok_s = steps / (us / 1e6)
+        nbytes = W.weight_bytes_per_token(cfg) + sum(W.kv_bytes_per_token(cfg, p) for p in range(first, first + steps)) / steps
+        out["config4_ctx4096"] = {"config": "greedy decode at positions 3840..4095 over a seeded INT8 history",
+                                  "tok_s": round(tok_s, 1), "us_per_token": round(us / steps, 1),
+                                  "GB/s": round(nbytes * tok_s / 1e9, 1),
+                                  "frac_of_measured_hbm": round(nbytes * tok_s / 1e9 / peak, 4)}
+    if "batch" in which:
+        for n in (64, 2048):
+            x = np.stack([qxlib.normal_vector(1000 + t, H) for t in range(n)])
+            us = time_call(lambda: eng.moe_batch(W.MOE_LAYER, x), stream, 5)
+            macs = n * 8 * (2 * I * H + H * I) + n * E * H          # experts + router
+            _, _, sel, _ = eng.moe_batch(W.MOE_LAYER, x)
+            used = len(set(sel.ravel().tolist()))
+            nbytes = used * (2 * I * (H // 256) * 74 + H * (I // 256) * 98) + E * H * 4
+            out["config5_moe_batch_%d" % n] = {
+                "config": "batched MoE layer (grouped-expert exact-integer GEMM on tcgen05), %d tokens" % n,
+                "us_per_call": round(us, 1), "tokens_per_s": round(n / (us / 1e6), 1),
+                "useful_TFLOP/s": round(2 * macs / us / 1e6, 2),
+                "frac_of_bf16_sustained": round(2 * macs / us / 1e6 / bf16, 4),
+                "experts_touched": used, "weight_GB/s": round(nbytes / us / 1e3, 1),
+                "note": "device time of the whole call: %.1f MB in / out over PCIe included" % (2 * n * H * 4 / 1e6)}
+    out["peak_source"] = peak_kind
+    return out
+
+
+def run_stage(args):
+    """Configs 1-3 and 5 alone (--workload head|moe|attention|batch): one JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    cfg = W.model_config(full=True)
+    img = qxlib.build_image(cfg)
+    eng = qxlib.Engine(img, ctx=4096, device=0)
+    stream = torch.cuda.ExternalStream(eng.stream())
+    print(json.dumps(stage_configs(eng, cfg, stream, reps=max(3, args.steps), which=(args.workload,))))
     eng.close()
     return 0
 
@@ -313,7 +363,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling case only: the same model with fewer layers (default: all 48)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "head", "moe", "attention"],
+    ap.add_argument("--no-stage-configs", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "head", "moe", "attention", "batch"],
                     help="decode = config 4 (the bench line); head/moe/attention = configs 1-3 through the "
                          "stage entry points, one JSON line each with the stage's HBM bandwidth")
     args = ap.parse_args()
@@ -337,7 +388,7 @@ def main():
     # share of the experts and of the head, and the ranks exchange through
     # mapped peer memory inside the step kernel (handles travel over the
     # process group once, here)
-    eng = qxlib.Engine(img, ctx=W.DECODE_STEPS + 8, device=local, stream=stream.cuda_stream, ep_rank=rank,
+    eng = qxlib.Engine(img, ctx=4096, device=local, stream=stream.cuda_stream, ep_rank=rank,
                        ep_world=world)
     if world > 1:
         def gather(obj):
@@ -456,6 +507,8 @@ def main():
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": launches,
     }
+    if world == 1 and not args.no_stage_configs and not args.layers:
+        line["stage_configs"] = stage_configs(eng, cfg, stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, why = cpu_reference_sample(img, 1)
         line["cpu_baseline"] = ({"value": v, "unit": "tok/s", "cores": 1, "kind": "reference",

@@ -46,7 +46,7 @@ constexpr int kTokTile = 16;        // tokens (or expert slots) per tile: N = 12
 constexpr int kRowTile = 128;       // weight rows per tile: M = 128
 constexpr int kSlab = 4096;         // bytes of one 32-value K step of a 128-row operand
 constexpr int kTmemCols = 256;      // hi accumulator in columns [0, 128), lo in [128, 256)
-constexpr uint32_t kSmemGemm = 3 * 8 * kSlab + 1024;   // A hi, A lo, B (8 K steps each) + barrier
+constexpr uint32_t kSmemGemm = 3 * 8 * kSlab + 128;    // A hi, A lo, B (8 K steps each) + alignment
 
 // ---- tcgen05 primitives (PTX ISA 8.7, sm_100a) ------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -121,12 +121,28 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 // u16 of four 3-bit codes: magnitude index 1..3 for {8, 25, 43} plus 4 when
 // negative, of values 16 gq + 4 tt + j): the 256 integers (1 + 2s) * g of one
 // row as hi/lo digits into the operand slabs.
-__device__ __forceinline__ void decode_iq2r_row(const uint8_t* blk, int r, uint8_t* ahi, uint8_t* alo) {
-    const uint4 sv = *reinterpret_cast<const uint4*>(blk);
-    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+// One row's source bytes of one block: the group scales and the 128 code
+// bytes, loaded a block ahead so the global latency hides behind the MMAs.
+struct RowSrc {
+    uint4 sv;
     uint4 cw[8];
+};
+
+__device__ __forceinline__ void load_src(const uint8_t* scales, const uint8_t* codes, bool scales16, RowSrc& s) {
+    if (scales16) {
+        s.sv = *reinterpret_cast<const uint4*>(scales);
+    } else {
+        const uint2 v = *reinterpret_cast<const uint2*>(scales);
+        s.sv = make_uint4(v.x, v.y, 0u, 0u);
+    }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) cw[i] = *reinterpret_cast<const uint4*>(blk + 16 + 16 * i);
+    for (int i = 0; i < 8; ++i) s.cw[i] = *reinterpret_cast<const uint4*>(codes + 16 * i);
+}
+
+__device__ __forceinline__ void decode_iq2r_row(const RowSrc& src, int r, uint8_t* ahi, uint8_t* alo) {
+    const uint4 sv = src.sv;
+    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+    const uint4 (&cw)[8] = src.cw;
     // u16 (tt, gq) at halfword 16 tt + gq
 #pragma unroll
     for (int gq = 0; gq < 16; ++gq) {
@@ -158,12 +174,9 @@ __device__ __forceinline__ void lut16(uint32_t q, const uint32_t T[4], uint32_t&
     hi = __byte_perm(__byte_perm(T[0], T[1], q2), __byte_perm(T[2], T[3], q2), pick >> 16);
 }
 
-__device__ __forceinline__ void decode_r4iq3_row(const uint8_t* scales, const uint8_t* codes, int r, uint8_t* ahi,
-                                                 uint8_t* alo) {
-    const uint2 sv = *reinterpret_cast<const uint2*>(scales);
-    uint4 cw[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) cw[i] = *reinterpret_cast<const uint4*>(codes + 16 * i);
+__device__ __forceinline__ void decode_r4iq3_row(const RowSrc& src, int r, uint8_t* ahi, uint8_t* alo) {
+    const uint4 sv = src.sv;
+    const uint4 (&cw)[8] = src.cw;
     // u32 (tt, ib) at word 8 tt + ib
     constexpr int kMag[8] = {4, 12, 20, 28, 36, 44, 52, 62};
 #pragma unroll
@@ -203,7 +216,7 @@ __device__ __forceinline__ void decode_r4iq3_row(const uint8_t* scales, const ui
 // product as a float (non-finite -> 0, src/qx_format.c:4783).
 __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~(uintptr_t)1023);
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 127) & ~(uintptr_t)127);
     uint8_t* ahi = base;
     uint8_t* alo = base + 8 * kSlab;
     uint8_t* bop = base + 16 * kSlab;
@@ -245,9 +258,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     for (int j = 0; j < kTokTile; ++j) acc[j] = 0.0;
     unsigned phase = 0;
     bool ok = true;
-    for (int b = 0; b < a.nblk && ok; ++b) {
-        // B: each column's 2 KB of block b (8 slabs x 256 B: limbs 0-6 and the
-        // ones column of 32 values) to slab s, 8-row group j
+    const bool iq2 = a.fmt == kGemmIq2r;
+    auto src_at = [&](int b, RowSrc& s) {
+        if (iq2) load_src(mat + a.hdr + (size_t)b * 144, mat + a.hdr + (size_t)b * 144 + 16, true, s);
+        else load_src(mat + a.hdr + 8 * b, mat + a.codes + 128 * b, false, s);
+    };
+    RowSrc src;
+    src_at(0, src);
+    // B: each column's 2 KB of a block (8 slabs x 256 B: limbs 0-6 and the
+    // ones column of 32 values) to slab s, 8-row group j
+    auto stage_b = [&](int b) {
         for (int i = r; i < kTokTile * 128; i += kGemmThreads) {
             const int j = i >> 7, c16 = i & 127;
             if (bidx_s[j] < 0) continue;
@@ -256,12 +276,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
                        a.bq + ((size_t)bidx_s[j] * a.nblk + b) * 2048 + s * 256 + w * 16);
         }
         cp_async_commit();
-        // A: this thread's row of block b
-        if (a.fmt == kGemmIq2r) {
-            decode_iq2r_row(mat + a.hdr + (size_t)b * 144, r, ahi, alo);
-        } else {
-            decode_r4iq3_row(mat + a.hdr + 8 * b, mat + a.codes + 128 * b, r, ahi, alo);
-        }
+    };
+    stage_b(0);
+    for (int b = 0; b < a.nblk && ok; ++b) {
+        // A: this thread's row of block b (source loaded during the previous block)
+        if (iq2) decode_iq2r_row(src, r, ahi, alo);
+        else decode_r4iq3_row(src, r, ahi, alo);
         cp_async_wait<0>();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core
         __syncthreads();
@@ -276,6 +296,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
             }
             mma_commit(&mbar);
         }
+        if (b + 1 < a.nblk) src_at(b + 1, src);   // in flight during the MMAs and the fold
         // bounded wait for the MMAs (2 s; a healthy block takes microseconds);
         // every thread agrees on the outcome before it touches TMEM
         {
@@ -294,6 +315,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
             phase ^= 1u;
         }
         tc_fence_after();
+        if (ok && b + 1 < a.nblk) stage_b(b + 1);   // the MMAs have read B: refill it during the fold
         if (ok) {
             // fold: column j's exact block integer X = sum_n c_n 2^(8n) (limb 6
             // minus 128 x the ones column removes the 2^55 offset) times
@@ -391,48 +413,85 @@ __global__ void __launch_bounds__(256) k_batch_limbs(const float* x, int K, int 
 
 // F32 router in double, softmax in double, top-8 by repeated strict-> scans
 // (lowest index on ties) and renormalisation, per token
-// (src/qx_format.c:5253-5287): one CTA per token, one warp per expert row.
-__global__ void __launch_bounds__(256) k_batch_router(const float* xn, const float* router, int H, int E, int* sel,
-                                                      double* wsel, int* err) {
-    __shared__ double logit[256];
-    __shared__ double prob[256];
-    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float* x = xn + (size_t)t * H;
-    for (int e = warp; e < E; e += blockDim.x >> 5) {
-        const float* row = router + (size_t)e * H;
-        double acc = 0.0;
-        for (int i = lane; i < H; i += 32) acc = fma((double)row[i], (double)x[i], acc);
-        acc = warp_sum_d(acc);
-        if (lane == 0) logit[e] = acc;
+// (src/qx_format.c:5253-5287).  A CTA takes kRouterTok tokens (widened to
+// double in shared memory, so each router row read from L2 serves all of
+// them); warp w forms the logits of experts w, w + 8, ... (lane-strided
+// partial dots, then a butterfly), then warp j ranks token j's experts.
+constexpr int kRouterTok = 8;
+
+__global__ void __launch_bounds__(256) k_batch_router(const float* xn, const float* router, int H, int E, int ntok,
+                                                      int* sel, double* wsel, int* err) {
+    extern __shared__ __align__(16) uint8_t rsm[];
+    double* xd = reinterpret_cast<double*>(rsm);                    // [kRouterTok][H]
+    double* logit = xd + (size_t)kRouterTok * H;                    // [kRouterTok][E]
+    double* prob = logit + (size_t)kRouterTok * E;
+    const int t0 = blockIdx.x * kRouterTok, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nt = min(kRouterTok, ntok - t0);
+    for (int i = threadIdx.x; i < kRouterTok * H; i += blockDim.x) {
+        const int j = i / H;
+        xd[i] = j < nt ? (double)xn[(size_t)(t0 + j) * H + i % H] : 0.0;
     }
     __syncthreads();
-    if (warp != 0) return;
+    // warp w: experts 4 w' .. 4 w' + 3 for w' = w, w + 8, ...; each x value
+    // read from shared memory feeds four FMAs
+    for (int e0 = 4 * warp; e0 < E; e0 += 4 * (blockDim.x >> 5)) {
+        double acc[4][kRouterTok];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int j = 0; j < kRouterTok; ++j) acc[q][j] = 0.0;
+#pragma unroll 4
+        for (int i = lane; i < H; i += 32) {
+            double wv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) wv[q] = e0 + q < E ? (double)router[(size_t)(e0 + q) * H + i] : 0.0;
+#pragma unroll
+            for (int j = 0; j < kRouterTok; ++j) {
+                const double xv = xd[j * H + i];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[q][j] = fma(wv[q], xv, acc[q][j]);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int j = 0; j < kRouterTok; ++j) {
+                const double v = warp_sum_d(acc[q][j]);
+                if (lane == 0 && e0 + q < E) logit[j * E + e0 + q] = v;
+            }
+    }
+    __syncthreads();
+    if (warp >= nt) return;
+    const int t = t0 + warp;
+    const double* lg = logit + warp * E;
+    double* pr = prob + warp * E;
     double m = -1.0e300;
-    for (int e = lane; e < E; e += 32) m = fmax(m, logit[e]);
+    for (int e = lane; e < E; e += 32) m = fmax(m, lg[e]);
     for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
     double s = 0.0;
     for (int e = lane; e < E; e += 32) {
-        const double p = exp(logit[e] - m);
-        prob[e] = p;
+        const double p = exp(lg[e] - m);
+        pr[e] = p;
         s += p;
     }
     s = warp_sum_d(s);
-    for (int e = lane; e < E; e += 32) prob[e] /= s;
+    for (int e = lane; e < E; e += 32) pr[e] /= s;
     __syncwarp();
     double ws[8];
-    int picked = 0;   // bit per lane-held expert e = lane + 32 k (k < 8)
+    int picked = 0;   // bit q: expert lane + 32 q is taken
+#pragma unroll
     double sum = 0.0;
     for (int k = 0; k < 8; ++k) {
         double bv = -1.0;
         int bi = 0x7fffffff;
         for (int e = lane, q = 0; e < E; e += 32, ++q)
-            if (!((picked >> q) & 1) && (prob[e] > bv || (prob[e] == bv && e < bi))) { bv = prob[e]; bi = e; }
+            if (!((picked >> q) & 1) && (pr[e] > bv || (pr[e] == bv && e < bi))) { bv = pr[e]; bi = e; }
         for (int o = 16; o; o >>= 1) {
             const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
-        if ((bi & 31) == lane) picked |= 1 << (bi >> 5);
+        if (bi != 0x7fffffff && (bi & 31) == lane) picked |= 1 << (bi >> 5);
         ws[k] = bv;
         sum += bv;
         if (lane == 0) sel[t * 8 + k] = bi;
@@ -470,9 +529,15 @@ __global__ void k_batch_combine(const float* x, const float* y, const double* ws
 }  // namespace
 
 uint32_t moe_gemm_smem_bytes() { return kSmemGemm; }
+size_t batch_router_smem_bytes(int H, int E) { return (size_t)kRouterTok * (H + 2 * E) * 8; }
 
 cudaError_t moe_batch_configure() {
-    return cudaFuncSetAttribute(k_moe_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemGemm);
+    cudaError_t e = cudaFuncSetAttribute(k_moe_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemGemm);
+    int dev = 0, optin = 0;
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_batch_router, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    return e;
 }
 
 void launch_batch_norm(const float* x, const float* w, float* xn, int H, int ntok, cudaStream_t st) {
@@ -486,7 +551,8 @@ void launch_batch_limbs(const float* x, int K, int nrows, uint8_t* bq, int* sexp
 
 void launch_batch_router(const float* xn, const float* router, int H, int E, int ntok, int* sel, double* wsel, int* err,
                          cudaStream_t st) {
-    k_batch_router<<<ntok, 256, 0, st>>>(xn, router, H, E, sel, wsel, err);
+    const size_t smem = (size_t)kRouterTok * (H + 2 * E) * 8;
+    k_batch_router<<<(ntok + kRouterTok - 1) / kRouterTok, 256, smem, st>>>(xn, router, H, E, ntok, sel, wsel, err);
 }
 
 void launch_moe_gemm(const GemmArgs& a, int nitems, cudaStream_t st) {

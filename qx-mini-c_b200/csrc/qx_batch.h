@@ -35,6 +35,7 @@ struct GemmArgs {
 };
 
 uint32_t moe_gemm_smem_bytes();
+size_t batch_router_smem_bytes(int H, int E);
 cudaError_t moe_batch_configure();
 void launch_batch_norm(const float* x, const float* w, float* xn, int H, int ntok, cudaStream_t st);
 void launch_batch_limbs(const float* x, int K, int nrows, uint8_t* bq, int* sexp, cudaStream_t st);

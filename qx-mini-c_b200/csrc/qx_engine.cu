@@ -856,7 +856,8 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
     }
     const LayerW& w = E->layers[layer];
     const int H = E->dm.hidden, I = E->dm.moe_inter, EX = E->dm.experts;
-    if (!w.gate_r || !w.up_r || !w.down_r || w.tgate != 17 || w.tup != 17 || w.tdown != 18 || H % 128 || I % 128) {
+    if (!w.gate_r || !w.up_r || !w.down_r || w.tgate != 17 || w.tup != 17 || w.tdown != 18 || H % 128 || I % 128 ||
+        EX > 256 || qx::batch_router_smem_bytes(H, EX) > 200 * 1024) {
         set_err(err, n, "batched experts need the IQ2_XS/IQ3_XXS mix in the one-launch step kernel's layouts");
         return 0;
     }
@@ -878,7 +879,11 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
     E->prof.device_to_host_bytes += (uint64_t)S * 4;
     std::vector<int> count(EX, 0), start(EX + 1, 0), cols(S);
     for (int s = 0; s < S; ++s) {
-        if (sel[s] < 0 || sel[s] >= EX) { set_err(err, n, "invalid selected router weights"); return 0; }
+        if (sel[s] < 0 || sel[s] >= EX) {   // a non-finite router softmax: fail the call, clear the device flag
+            finish(E, err, n);
+            set_err(err, n, "invalid selected router weights");
+            return 0;
+        }
         count[sel[s]]++;
     }
     for (int e = 0; e < EX; ++e) start[e + 1] = start[e] + count[e];

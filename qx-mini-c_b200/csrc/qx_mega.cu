@@ -770,7 +770,6 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
     }
     __syncthreads();
     if (!active) return;
-    mark(d, epoch, 0);
     cp_async_wait<0>();
     __syncthreads();
     mark(d, epoch, 1);
@@ -797,7 +796,6 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
         }
     }
     __syncthreads();
-    mark(d, epoch, 2);
     float ka = 0.f, va = 0.f;
     for (int k = 0; k < KVH; ++k) {
         ka = fmaxf(ka, S.sf[k]);
@@ -839,7 +837,6 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
     double den = fixed_order_sum(f.w_s, T, S.sd);
     if (!isfinite(den) || den <= 0.0) den = 1.0;
     for (int t = i; t < T; t += kMT) f.w_s[t] = f.w_s[t] / den;
-    mark(d, epoch, 5);
     __syncthreads();
     const float acc = context_chain(T, f.w_s, prod, [&](int t, int dd) {
         return t == pos ? i8_to_f32(S.v8[g * D + sl * SW + dd]) * vsc : i8_to_f32(f.vrows[t * SW + dd]) * f.vscl[t];
@@ -1047,7 +1044,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         // ---------------- QKV (weights in buf[qb]) ----------------
         {
             group_wait(G, kGQkv, d);             // this phase's tiles and norm vector
-            mark(d, epoch, 0);
             if (layer > 0 && ep) {
                 ep_wait_layer(d, seqb, layer - 1);
                 ep_combine(d, layer - 1, xs);
@@ -1056,7 +1052,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             } else {
                 __syncthreads();
             }
-            mark(d, epoch, 1);
             // attention RMSNorm of xs in place
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
             double ss = 0.0;
@@ -1080,7 +1075,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             for (int r = threadIdx.x; r < mine * kTileRows; r += kMT)
                 d.qkv[item_id(r / kTileRows) * kTileRows + r % kTileRows] =
                     finite_or_zero_d(tile_row(part, r / kTileRows, nblk, r % kTileRows));
-            mark(d, epoch, 5);
             grid_arrive(bar, epoch, nsync, d);
             if (fused) issue_attn_fused(d, w, layer, pos, fz);   // the activation region is free again
             cp_async_commit();
@@ -1102,12 +1096,10 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         // ---------------- O projection (weights in buf[1-qb]) ----------------
         {
             copy_to_smem(d.ctxv, xs, Q);
-            mark(d, epoch, 0);
             build_xq(xs, Q, xb, sb);
             __syncthreads();
             mark(d, epoch, 1);
             group_wait(G, kGOproj, d);
-            mark(d, epoch, 2);
             const uint32_t rb = (uint32_t)r4_row_bytes(Q), tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(H / kTileRows), nblk = Q / 256;
             run_tasks<QXH_R4_IQ4_F>(buf[1 - qb], tb, rb, mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part);
@@ -1126,16 +1118,13 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 xown = xr + o;
                 d.x[row] = xown;
             }
-            mark(d, epoch, 4);
             grid_sync(bar, epoch, nsync, d);
         }
         // ---------------- router (weights in buf[qb]) ----------------
         {
             group_wait(G, kGRouter, d);          // router rows and norm vector
-            mark(d, epoch, 0);
             copy_to_smem(d.x, xs, H);
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
-            mark(d, epoch, 1);
             double ss = 0.0;
             for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
             ss = block_sum_d(ss, scratch);
@@ -1180,10 +1169,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             }
             __syncthreads();
             const int n_own = n_own_s;
-            mark(d, epoch, 1);
             issue_gateup(d, w, sel, own, n_own, smem + L.buf0, L.iq2r_rb, G);   // both buffers: free now
             top8_weights(d, layer, sel, wsel);  // read in the down phase, after several block syncs
-            mark(d, epoch, 2);
             const uint32_t rb = L.iq2r_rb, tb = (uint32_t)kTileRows * rb;
             const int mine = my_items(n_own * (I / kTileRows)), nblk = H / 256;
             run_tasks<QXH_IQ2R_F>(smem + L.buf0, tb, rb, 2 * mine, nblk, SameXQ{XQ{xb, sb}}, K4, T, part,
@@ -1198,7 +1185,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                 const double gd = (double)gv;
                 d.hbuf[(it / tpe) * I + (it % tpe) * kTileRows + rr] = (float)(gd / (1.0 + exp(-gd)) * (double)uv);
             }
-            mark(d, epoch, 4);
             grid_arrive(bar, epoch, nsync, d);
             issue_down(d, w, sel, own, n_own, buf[qb], G);
             grid_wait(bar, epoch, nsync, d);
@@ -1207,10 +1193,8 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         {
             const int n_own = n_own_s;
             copy_to_smem(d.hbuf, xs, n_own * I);
-            mark(d, epoch, 0);
             // into the free gate/up buffer: next layer's QKV tiles (or the first head group)
             if (layer + 1 < m.layers) issue_qkv(d, layers[layer + 1], buf[1 - qb], L.norm, G);
-            mark(d, epoch, 1);
             build_xq(xs, n_own * I, xb, sb);   // slot j's groups start at j * I / 16 (I % 256 == 0)
             __syncthreads();
             mark(d, epoch, 2);
@@ -1237,7 +1221,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                     for (int p = 0; p < d.ep_world; ++p) ep_terms(d.ep_peers[p], layer & 1, own[j], H)[row] = term;
                 }
             }
-            mark(d, epoch, 4);
             if (!ep) {
                 __syncthreads();
                 for (int r = threadIdx.x; r < mine * kTileRows; r += kMT) {
@@ -1251,7 +1234,6 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             } else {
                 __threadfence_system();
             }
-            mark(d, epoch, 5);
             grid_sync(bar, epoch, nsync, d);
             if (ep && blockIdx.x == 0 && threadIdx.x == 0) {   // every CTA's stores are ordered before the barrier
                 __threadfence_system();
