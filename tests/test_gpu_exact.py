@@ -236,3 +236,22 @@ def test_smaller_engine_created_later_does_not_break_the_first(full, mini_image)
         assert full.decode_step(g[0]["input"], 0)["token"] == g[0]["token"]
     finally:
         small.close()
+
+
+def test_device_exp_against_host_libm():
+    """The softmaxes and SiLU call CUDA's double exp; the reference calls the
+    C library's (src/qx_format.c:2511-2513, :5131-5167, :5257-5285).  Both are
+    within an ulp of e^x but need not round alike.  Count how often they
+    differ on the ranges the engine feeds them: softmax arguments (score -
+    max, logit - max) in [-40, 0] and SiLU arguments in [-20, 20]."""
+    import math
+    import torch
+    rng = np.random.default_rng(9)
+    for lo, hi in ((-40.0, 0.0), (-20.0, 20.0)):
+        x = rng.uniform(lo, hi, 200000)
+        dev = torch.exp(torch.from_numpy(x).cuda()).cpu().numpy()
+        host = np.array([math.exp(v) for v in x])
+        diff = int(np.count_nonzero(dev != host))
+        ulps = np.abs(dev.view(np.int64) - host.view(np.int64))
+        print("exp on [%g, %g]: %d of %d differ (max %d ulp)" % (lo, hi, diff, x.size, int(ulps.max())))
+        assert ulps.max() <= 1        # both faithful; how often they differ is reported, not bounded
