@@ -154,6 +154,22 @@ int qx_cuda_moe_batch(qx_cuda_engine *engine, uint32_t layer, uint32_t tokens, c
                       float *layer_output, float *moe_output, uint32_t *selected, float *weights, char *err,
                       uint64_t err_len);
 
+/* Prompt prefill: `tokens` prompt tokens at positions position ..
+ * position + tokens - 1 through every layer at once, layer by layer, and the
+ * greedy token after the last one.  The reference's prompt loop
+ * (qx_dump_prompt_state_loop_probe_summary, src/qx_format.c:5970; its layer
+ * loop :6250-6547) runs the prompt one token at a time and skips the head for
+ * all but the last prompt position (:6533-6547); here the projections of all
+ * tokens run as GEMMs on the tcgen05 tensor cores (exact integer
+ * contraction), the per-token attention reads the cache the batch has just
+ * appended, and the MoE is qx_cuda_moe_batch's.  The INT8 KV cache holds the
+ * prompt afterwards, so qx_cuda_generate / qx_cuda_decode_step continue at
+ * position + tokens.  final_residual[hidden] (may be NULL) is the last
+ * token's.  tokens <= QX_CUDA_MAX_BATCH; same quant-mix requirement as
+ * qx_cuda_moe_batch plus IQ4_XS attention. */
+int qx_cuda_prefill(qx_cuda_engine *engine, const uint32_t *tokens, uint32_t tokens_count, uint32_t position,
+                    uint32_t *next_token, float *final_residual, char *err, uint64_t err_len);
+
 /* The attention half of one layer at `position`, state-loop order
  * (src/qx_format.c:6283-6423 with qx_rope_gqa_attention_partial, :5051-5196):
  * attn RMSNorm, K/V projection, K head norm + RoPE, INT8 append at

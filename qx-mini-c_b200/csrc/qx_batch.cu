@@ -46,6 +46,7 @@ constexpr int kTokTile = 16;        // tokens (or expert slots) per tile: N = 12
 constexpr int kRowTile = 128;       // weight rows per tile: M = 128
 constexpr int kSlab = 4096;         // bytes of one 32-value K step of a 128-row operand
 constexpr int kTmemCols = 256;      // hi accumulator in columns [0, 128), lo in [128, 256)
+constexpr int kMaxBlk = 16;         // 256-value blocks per row (K <= 4096)
 constexpr uint32_t kSmemGemm = 3 * 8 * kSlab + 128;    // A hi, A lo, B (8 K steps each) + alignment
 
 // ---- tcgen05 primitives (PTX ISA 8.7, sm_100a) ------------------------------
@@ -174,25 +175,31 @@ __device__ __forceinline__ void lut16(uint32_t q, const uint32_t T[4], uint32_t&
     hi = __byte_perm(__byte_perm(T[0], T[1], q2), __byte_perm(T[2], T[3], q2), pick >> 16);
 }
 
-__device__ __forceinline__ void decode_r4iq3_row(const RowSrc& src, int r, uint8_t* ahi, uint8_t* alo) {
+// IQ4 (R4 of IQ4_XS origin): the code is an index into the IQ4_NL values
+// (src/qx_format.c:2032), the scale byte is ls - 32 (signed).
+__device__ constexpr int kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+template <bool IQ4>
+__device__ __forceinline__ void decode_r4_row(const RowSrc& src, int r, uint8_t* ahi, uint8_t* alo) {
     const uint4 sv = src.sv;
     const uint4 (&cw)[8] = src.cw;
     // u32 (tt, ib) at word 8 tt + ib
     constexpr int kMag[8] = {4, 12, 20, 28, 36, 44, 52, 62};
 #pragma unroll
     for (int ib = 0; ib < 8; ++ib) {
-        const int s = (int)(((ib < 4 ? sv.x : sv.y) >> (8 * (ib & 3))) & 255u);
-        int v[8];
+        const uint32_t sb = ((ib < 4 ? sv.x : sv.y) >> (8 * (ib & 3))) & 255u;
+        const int s = IQ4 ? (int)(int8_t)sb : (int)sb;
+        int v[16];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) v[c] = s * kMag[c];
+        for (int c = 0; c < 16; ++c) v[c] = IQ4 ? s * kIq4nl[c] : (c < 8 ? s * kMag[c] : -(s * kMag[c - 8]));
         const uint32_t Th[4] = {pack4(v[0] >> 6, v[1] >> 6, v[2] >> 6, v[3] >> 6),
                                 pack4(v[4] >> 6, v[5] >> 6, v[6] >> 6, v[7] >> 6),
-                                pack4((-v[0]) >> 6, (-v[1]) >> 6, (-v[2]) >> 6, (-v[3]) >> 6),
-                                pack4((-v[4]) >> 6, (-v[5]) >> 6, (-v[6]) >> 6, (-v[7]) >> 6)};
+                                pack4(v[8] >> 6, v[9] >> 6, v[10] >> 6, v[11] >> 6),
+                                pack4(v[12] >> 6, v[13] >> 6, v[14] >> 6, v[15] >> 6)};
         const uint32_t Tl[4] = {pack4(v[0] & 63, v[1] & 63, v[2] & 63, v[3] & 63),
                                 pack4(v[4] & 63, v[5] & 63, v[6] & 63, v[7] & 63),
-                                pack4((-v[0]) & 63, (-v[1]) & 63, (-v[2]) & 63, (-v[3]) & 63),
-                                pack4((-v[4]) & 63, (-v[5]) & 63, (-v[6]) & 63, (-v[7]) & 63)};
+                                pack4(v[8] & 63, v[9] & 63, v[10] & 63, v[11] & 63),
+                                pack4(v[12] & 63, v[13] & 63, v[14] & 63, v[15] & 63)};
         uint32_t h0[4], h1[4], l0[4], l1[4];
 #pragma unroll
         for (int tt = 0; tt < 4; ++tt) {
@@ -223,7 +230,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     __shared__ __align__(8) uint64_t mbar;
     __shared__ uint32_t tmem_base_s;
     __shared__ int cols_s[kTokTile], bidx_s[kTokTile];
-    __shared__ int sexp_s[kTokTile][8];
+    __shared__ int sexp_s[kTokTile][kMaxBlk];
     const GemmItem it = a.items[blockIdx.x];
     const int r = threadIdx.x, warp = r >> 5, ncol = it.ncols;
     if (r < kTokTile) {
@@ -281,7 +288,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     for (int b = 0; b < a.nblk && ok; ++b) {
         // A: this thread's row of block b (source loaded during the previous block)
         if (iq2) decode_iq2r_row(src, r, ahi, alo);
-        else decode_r4iq3_row(src, r, ahi, alo);
+        else if (a.fmt == kGemmR4Iq4) decode_r4_row<true>(src, r, ahi, alo);
+        else decode_r4_row<false>(src, r, ahi, alo);
         cp_async_wait<0>();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core
         __syncthreads();
@@ -526,7 +534,146 @@ __global__ void k_batch_combine(const float* x, const float* y, const double* ws
     out[i] = x[i] + m;
 }
 
+// ---- prompt prefill: the attention half for many tokens ----------------------
+// Embedding rows (Q4_K, d * sc * q - dmin * m with each product rounded to
+// float, src/qx_format.c:2089-2110, :3759-3819), one CTA per token.
+__global__ void __launch_bounds__(256) k_batch_embed(const uint32_t* tokens, const uint8_t* emb, int H, int V,
+                                                     float* x, int* err) {
+    const uint32_t tok = tokens[blockIdx.x];
+    if (tok >= (uint32_t)V) {
+        if (threadIdx.x == 0) atomicOr(err, kErrToken);
+        return;
+    }
+    const int nblk = H / 256;
+    const uint8_t* row = emb + (size_t)tok * (size_t)(nblk * 144);
+    float* xt = x + (size_t)blockIdx.x * H;
+    const int t = threadIdx.x, c = t >> 6, l = t & 63;
+    for (int b = 0; b < nblk; ++b) {
+        const uint8_t* blk = row + b * 144;
+        const float dd = h2f(ld16(blk)), dmin = h2f(ld16(blk + 2));
+        const uint8_t* sc = blk + 4;
+        const int j = 2 * c + (l >= 32);
+        uint32_t scv, mn;
+        if (j < 4) { scv = sc[j] & 63u; mn = sc[j + 4] & 63u; }
+        else { scv = (sc[j + 4] & 15u) | ((sc[j - 4] >> 6) << 4); mn = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4); }
+        const uint8_t qb = blk[16 + 32 * c + (l & 31)];
+        const uint32_t q = l < 32 ? (qb & 15u) : (qb >> 4);
+        xt[b * 256 + t] = __fsub_rn(__fmul_rn(__fmul_rn(dd, (float)scv), (float)q), __fmul_rn(dmin, (float)mn));
+    }
+}
+
+// Per token (CTA): per-head Q/K RMSNorm + split-half RoPE at the token's
+// position (src/qx_format.c:3740-3757, :4625-4641), the normed Q to qn, and
+// the INT8 K/V row (one scale per token over all KV values, :4449-4463)
+// appended to the cache at (layer, p0 + t) (:6343-6400).
+__global__ void __launch_bounds__(256) k_batch_qkv_post(const float* qkv, const float* q_norm, const float* k_norm,
+                                                        const double* rope, int layer, int p0, int QH, int KVH,
+                                                        int ctx, float* qn, int8_t* kcache, int8_t* vcache,
+                                                        float* kscale, float* vscale) {
+    constexpr int D = 128;
+    __shared__ float v[4096 + 2 * 1024];
+    __shared__ float scratch_f[8];
+    const int Q = QH * D, KV = KVH * D, t = blockIdx.x, pos = p0 + t;
+    const float* src = qkv + (size_t)t * (Q + 2 * KV);
+    for (int j = threadIdx.x; j < Q + 2 * KV; j += blockDim.x) v[j] = src[j];
+    __syncthreads();
+    const double* rp = rope + (size_t)pos * 128;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int hh = warp; hh < QH + KVH; hh += blockDim.x >> 5) {
+        if (hh < QH) warp_norm_rope(v + hh * D, q_norm, rp, lane);
+        else warp_norm_rope(v + Q + (hh - QH) * D, k_norm, rp, lane);
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < Q; j += blockDim.x) qn[(size_t)t * Q + j] = v[j];
+    const float* kc = v + Q;
+    const float* vc = v + Q + KV;
+    float ka = 0.f, va = 0.f;
+    for (int j = threadIdx.x; j < KV; j += blockDim.x) {
+        ka = fmaxf(ka, isfinite(kc[j]) ? fabsf(kc[j]) : 0.f);
+        va = fmaxf(va, isfinite(vc[j]) ? fabsf(vc[j]) : 0.f);
+    }
+    ka = block_max_f(ka, scratch_f);
+    va = block_max_f(va, scratch_f);
+    const float ksc = ka > 0.f ? ka / 127.0f : 1.0f, vsc = va > 0.f ? va / 127.0f : 1.0f;
+    const size_t slot = (size_t)layer * ctx + pos;
+    for (int j = threadIdx.x; j < KV; j += blockDim.x) {
+        const int qk = isfinite(kc[j]) ? (int)lrintf(kc[j] / ksc) : 0;
+        const int qq = isfinite(vc[j]) ? (int)lrintf(vc[j] / vsc) : 0;
+        kcache[slot * KV + j] = (int8_t)max(-127, min(127, qk));
+        vcache[slot * KV + j] = (int8_t)max(-127, min(127, qq));
+    }
+    if (threadIdx.x == 0) { kscale[slot] = ksc; vscale[slot] = vsc; }
+}
+
+// Causal GQA attention of token t (grid.x) and query head h (grid.y) over
+// positions 0..p0 + t of the cache: scores in double in dimension order,
+// softmax with the max subtracted and a fixed-order sum, context accumulated
+// in float over positions in order (src/qx_format.c:5127-5172) - the same
+// arithmetic as the decode step's attention.  128 threads; dynamic shared
+// memory: (p0 + t + 1) doubles.
+__global__ void __launch_bounds__(128) k_batch_attn(const float* qn, const int8_t* kcache, const int8_t* vcache,
+                                                    const float* kscale, const float* vscale, int layer, int p0,
+                                                    int QH, int KVH, int ctx, float* ctx_out) {
+    constexpr int D = 128;
+    extern __shared__ __align__(16) double w_s[];
+    __shared__ double qd[D];
+    __shared__ double scratch_d[4];
+    const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x, g = h / (QH / KVH);
+    const int Q = QH * D, KV = KVH * D, T = p0 + t + 1;
+    qd[i] = (double)qn[(size_t)t * Q + h * D + i];
+    __syncthreads();
+    const double sqrt_d = sqrt((double)D);
+    double mloc = -1.0e300;
+    for (int p = i; p < T; p += D) {
+        const size_t st = (size_t)layer * ctx + p;
+        const double sc = score_row(qd, kcache + st * KV + g * D, kscale[st], sqrt_d);
+        w_s[p] = sc;
+        mloc = fmax(mloc, sc);
+    }
+    const double mx = block_max_d(mloc, scratch_d);
+    for (int p = i; p < T; p += D) w_s[p] = exp(w_s[p] - mx);
+    double den = fixed_order_sum(w_s, T, scratch_d);
+    if (!isfinite(den) || den <= 0.0) den = 1.0;
+    for (int p = i; p < T; p += D) w_s[p] = w_s[p] / den;
+    __syncthreads();
+    const int8_t* vb = vcache + (size_t)layer * ctx * KV + g * D + i;
+    const float* vs = vscale + (size_t)layer * ctx;
+    float acc = 0.0f;
+    for (int p = 0; p < T; ++p) acc += (float)(w_s[p] * (double)(i8_to_f32(vb[(size_t)p * KV]) * vs[p]));
+    ctx_out[(size_t)t * Q + h * D + i] = acc;
+}
+
+// x[i] += y[i] (the residual adds, float, src/qx_format.c:6420-6423).
+__global__ void k_batch_add(float* x, const float* y, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = x[i] + y[i];
+}
+
 }  // namespace
+
+void launch_batch_embed(const uint32_t* tokens, const uint8_t* emb, int H, int V, int ntok, float* x, int* err,
+                        cudaStream_t st) {
+    k_batch_embed<<<ntok, 256, 0, st>>>(tokens, emb, H, V, x, err);
+}
+
+void launch_batch_qkv_post(const float* qkv, const float* q_norm, const float* k_norm, const double* rope, int layer,
+                           int p0, int ntok, int QH, int KVH, int ctx, float* qn, int8_t* kcache, int8_t* vcache,
+                           float* kscale, float* vscale, cudaStream_t st) {
+    k_batch_qkv_post<<<ntok, 256, 0, st>>>(qkv, q_norm, k_norm, rope, layer, p0, QH, KVH, ctx, qn, kcache, vcache,
+                                          kscale, vscale);
+}
+
+void launch_batch_attn(const float* qn, const int8_t* kcache, const int8_t* vcache, const float* kscale,
+                       const float* vscale, int layer, int p0, int ntok, int QH, int KVH, int ctx, float* ctx_out,
+                       cudaStream_t st) {
+    const size_t smem = (size_t)(p0 + ntok) * 8;
+    k_batch_attn<<<dim3(ntok, QH), 128, smem, st>>>(qn, kcache, vcache, kscale, vscale, layer, p0, QH, KVH, ctx,
+                                                    ctx_out);
+}
+
+void launch_batch_add(float* x, const float* y, size_t n, cudaStream_t st) {
+    k_batch_add<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, n);
+}
 
 uint32_t moe_gemm_smem_bytes() { return kSmemGemm; }
 size_t batch_router_smem_bytes(int H, int E) { return (size_t)kRouterTok * (H + 2 * E) * 8; }
@@ -537,6 +684,7 @@ cudaError_t moe_batch_configure() {
     if (e == cudaSuccess) e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k_batch_router, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_batch_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 2048);
     return e;
 }
 

@@ -81,9 +81,10 @@ struct qx_cuda_engine {
     struct Batch {
         size_t cap = 0;
         void* mem = nullptr;
-        float *x, *xn, *gu, *h, *y, *out, *moe;
+        float *x, *xn, *gu, *h, *y, *out, *moe, *qkv, *qn, *ctxo, *ao;
         uint8_t *bqx, *bqh;
-        int *sx, *sh, *sel, *cols;
+        int *sx, *sh, *sel, *cols, *tcols;
+        uint32_t* tok;
         double* wsel;
         qx::GemmItem* items;
         size_t item_cap;
@@ -826,14 +827,18 @@ bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
     if (B.cap >= ntok) return true;
     if (B.mem) { cudaFree(B.mem); B.mem = nullptr; B.cap = 0; }
     const size_t H = E->dm.hidden, I = E->dm.moe_inter, S = ntok * 8;
-    const size_t items = (S / 16 + (size_t)E->dm.experts) * std::max(2 * I / 128, H / 128);
+    const size_t Q = E->dm.q_dim(), KV = E->dm.kv_dim(), K = std::max(H, Q);
+    const size_t items = std::max((S / 16 + (size_t)E->dm.experts) * std::max(2 * I / 128, H / 128),
+                                  (ntok / 16 + 1) * std::max(Q / 128, H / 128));
     size_t off = 0;
     std::vector<std::pair<void**, size_t>> parts = {
         {(void**)&B.x, ntok * H * 4}, {(void**)&B.xn, ntok * H * 4}, {(void**)&B.out, ntok * H * 4},
         {(void**)&B.moe, ntok * H * 4}, {(void**)&B.gu, S * 2 * I * 4}, {(void**)&B.h, S * I * 4},
-        {(void**)&B.y, S * H * 4}, {(void**)&B.bqx, ntok * (H / 256) * 2048}, {(void**)&B.bqh, S * (I / 256) * 2048},
-        {(void**)&B.sx, ntok * (H / 256) * 4}, {(void**)&B.sh, S * (I / 256) * 4}, {(void**)&B.sel, S * 4},
-        {(void**)&B.cols, S * 4}, {(void**)&B.wsel, S * 8}, {(void**)&B.items, items * sizeof(qx::GemmItem)}};
+        {(void**)&B.y, S * H * 4}, {(void**)&B.bqx, ntok * (K / 256) * 2048}, {(void**)&B.bqh, S * (I / 256) * 2048},
+        {(void**)&B.sx, ntok * (K / 256) * 4}, {(void**)&B.sh, S * (I / 256) * 4}, {(void**)&B.sel, S * 4},
+        {(void**)&B.cols, S * 4}, {(void**)&B.wsel, S * 8}, {(void**)&B.items, items * sizeof(qx::GemmItem)},
+        {(void**)&B.qkv, ntok * (Q + 2 * KV) * 4}, {(void**)&B.qn, ntok * Q * 4}, {(void**)&B.ctxo, ntok * Q * 4},
+        {(void**)&B.ao, ntok * H * 4}, {(void**)&B.tcols, ntok * 4}, {(void**)&B.tok, ntok * 4}};
     for (auto& p : parts) off = align_up(off + p.second, 256);
     if (!cuda_ok(cudaMalloc(&B.mem, off), "cudaMalloc(batch)", err, n)) return false;
     off = 0;
@@ -848,24 +853,62 @@ bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
 
 }  // namespace
 
-QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, const float* x, float* layer_output,
-                             float* moe_output, uint32_t* selected, float* weights, char* err, uint64_t n) {
-    if (!E || !x || !layer_output || layer >= (uint32_t)E->dm.layers || ntok == 0 || ntok > QX_CUDA_MAX_BATCH) {
-        set_err(err, n, "invalid batched expert argument");
-        return 0;
-    }
-    const LayerW& w = E->layers[layer];
+namespace {
+
+bool batch_supported(const qx_cuda_engine* E, const LayerW& w, bool attention, char* err, uint64_t n) {
     const int H = E->dm.hidden, I = E->dm.moe_inter, EX = E->dm.experts;
-    if (!w.gate_r || !w.up_r || !w.down_r || w.tgate != 17 || w.tup != 17 || w.tdown != 18 || H % 128 || I % 128 ||
-        EX > 256 || qx::batch_router_smem_bytes(H, EX) > 200 * 1024) {
-        set_err(err, n, "batched experts need the IQ2_XS/IQ3_XXS mix in the one-launch step kernel's layouts");
-        return 0;
-    }
-    DeviceGuard g(E->device);
-    if (!batch_reserve(E, ntok, err, n)) return 0;
+    bool ok = w.gate_r && w.up_r && w.down_r && w.tgate == 17 && w.tup == 17 && w.tdown == 18 && H % 128 == 0 &&
+              I % 128 == 0 && EX <= 256 && qx::batch_router_smem_bytes(H, EX) <= 200 * 1024;
+    if (attention)
+        ok = ok && w.wq_r && w.wk_r && w.wv_r && w.wo_r && w.tq == 23 && w.tk == 23 && w.tv == 23 && w.to == 23 &&
+             E->dm.head_dim == 128 && E->dm.q_dim() <= 4096 && E->dm.kv_dim() <= 1024 && E->dm.q_dim() % 128 == 0 &&
+             E->dm.kv_dim() % 128 == 0;
+    if (!ok) set_err(err, n, "batched path needs the benchmark quant mix in the one-launch step kernel's layouts");
+    return ok;
+}
+
+// GEMM arguments for an R4-laid IQ4_XS matrix of `rows` x K (one "expert"),
+// columns = tokens 0..N-1 (ids in B.tcols), B rows = tokens.
+qx::GemmArgs proj_args(qx_cuda_engine* E, const uint8_t* weights, int K, float* out, size_t out_stride, int out_off) {
     auto& B = E->batch;
-    const int N = (int)ntok, S = N * 8;
-    if (!h2d(E, B.x, x, (size_t)N * H * 4, err, n)) return 0;
+    const size_t rb = qx::r4_bytes_per_row(K);
+    qx::GemmArgs a{};
+    a.items = B.items;
+    a.cols = B.tcols;
+    a.weights = weights;
+    a.expert_stride = 0;
+    a.row_bytes = (uint32_t)rb;
+    a.hdr = (2 * (K / 256) + 15) / 16 * 16;
+    a.codes = (a.hdr + 8 * (K / 256) + 15) / 16 * 16;
+    a.nblk = K / 256;
+    a.fmt = qx::kGemmR4Iq4;
+    a.fexp = 0;
+    a.bq = B.bqx;
+    a.sexp = B.sx;
+    a.b_by_token = 0;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.out_off = out_off;
+    a.err = E->dev.err;
+    return a;
+}
+
+// Work items of a projection over N tokens: 16-token tiles x 128-row tiles.
+bool proj_items(qx_cuda_engine* E, int N, int rows, int* count, char* err, uint64_t n) {
+    std::vector<qx::GemmItem> items;
+    for (int c0 = 0; c0 < N; c0 += 16)
+        for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({0, c0, std::min(16, N - c0), r0});
+    if (items.size() > E->batch.item_cap) { set_err(err, n, "batched work list too long"); return false; }
+    *count = (int)items.size();
+    return h2d(E, E->batch.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n);
+}
+
+// One MoE layer for the N residuals in B.x: B.out = B.x + moe (B.moe), the
+// selections in B.sel / B.wsel.  Leaves the stream running.
+bool moe_batch_run(qx_cuda_engine* E, uint32_t layer, int N, char* err, uint64_t n) {
+    auto& B = E->batch;
+    const LayerW& w = E->layers[layer];
+    const int H = E->dm.hidden, I = E->dm.moe_inter, EX = E->dm.experts, S = N * 8;
     // norm, activation limbs, router + top-8 (every token)
     qx::launch_batch_norm(B.x, w.ffn_norm, B.xn, H, N, E->stream);
     qx::launch_batch_limbs(B.xn, H, N, B.bqx, B.sx, E->stream);
@@ -875,14 +918,14 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
     std::vector<int> sel(S);
     if (!cuda_ok(cudaMemcpyAsync(sel.data(), B.sel, (size_t)S * 4, cudaMemcpyDeviceToHost, E->stream), "d2h", err, n) ||
         !cuda_ok(cudaStreamSynchronize(E->stream), "router", err, n))
-        return 0;
+        return false;
     E->prof.device_to_host_bytes += (uint64_t)S * 4;
     std::vector<int> count(EX, 0), start(EX + 1, 0), cols(S);
     for (int s = 0; s < S; ++s) {
         if (sel[s] < 0 || sel[s] >= EX) {   // a non-finite router softmax: fail the call, clear the device flag
             finish(E, err, n);
             set_err(err, n, "invalid selected router weights");
-            return 0;
+            return false;
         }
         count[sel[s]]++;
     }
@@ -898,11 +941,11 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
             for (int c0 = start[e]; c0 < start[e + 1]; c0 += 16)
                 for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({e, c0, std::min(16, start[e + 1] - c0), r0});
     };
-    if (!h2d(E, B.cols, cols.data(), (size_t)S * 4, err, n)) return 0;
+    if (!h2d(E, B.cols, cols.data(), (size_t)S * 4, err, n)) return false;
     // gate and up: rows of I values of K = H, columns = slots, B = the token's limbs
     make_items(I);
-    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return 0; }
-    if (!h2d(E, B.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return 0;
+    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return false; }
+    if (!h2d(E, B.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return false;
     const size_t rb2 = qx::iq2r_row_bytes(H);
     qx::GemmArgs ga{};
     ga.items = B.items;
@@ -930,12 +973,10 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
     qx::launch_batch_limbs(B.h, I, S, B.bqh, B.sh, E->stream);
     // down: rows of H values of K = I, columns = slots, B = the slot's limbs
     make_items(H);
-    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return 0; }
-    qx::GemmItem* items2 = B.items;
-    if (!h2d(E, items2, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return 0;
+    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return false; }
+    if (!h2d(E, B.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return false;
     const size_t rb4 = qx::r4_bytes_per_row(I);
     qx::GemmArgs gd = ga;
-    gd.items = items2;
     gd.weights = w.down_r;
     gd.expert_stride = (size_t)H * rb4;
     gd.row_bytes = (uint32_t)rb4;
@@ -953,7 +994,24 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
     qx::launch_moe_gemm(gd, (int)items.size(), E->stream);
     qx::launch_batch_combine(B.x, B.y, B.wsel, H, N, B.moe, B.out, E->stream);
     E->prof.kernel_launches += 6;
-    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    return cuda_ok(cudaGetLastError(), "kernel launch", err, n);
+}
+
+}  // namespace
+
+QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, const float* x, float* layer_output,
+                             float* moe_output, uint32_t* selected, float* weights, char* err, uint64_t n) {
+    if (!E || !x || !layer_output || layer >= (uint32_t)E->dm.layers || ntok == 0 || ntok > QX_CUDA_MAX_BATCH) {
+        set_err(err, n, "invalid batched expert argument");
+        return 0;
+    }
+    if (!batch_supported(E, E->layers[layer], false, err, n)) return 0;
+    DeviceGuard g(E->device);
+    if (!batch_reserve(E, ntok, err, n)) return 0;
+    auto& B = E->batch;
+    const int N = (int)ntok, S = N * 8, H = E->dm.hidden;
+    if (!h2d(E, B.x, x, (size_t)N * H * 4, err, n)) return 0;
+    if (!moe_batch_run(E, layer, N, err, n)) return 0;
     if (!d2h(E, layer_output, B.out, (size_t)N * H * 4, err, n) ||
         !d2h(E, moe_output, B.moe, (size_t)N * H * 4, err, n) ||
         !d2h(E, selected, B.sel, (size_t)S * 4, err, n))
@@ -965,6 +1023,76 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
         return 1;
     }
     return finish(E, err, n) ? 1 : 0;
+}
+
+QX_API int qx_cuda_prefill(qx_cuda_engine* E, const uint32_t* tokens, uint32_t ntok, uint32_t position,
+                           uint32_t* next_token, float* final_residual, char* err, uint64_t n) {
+    if (!E || !tokens || !next_token || ntok == 0 || ntok > QX_CUDA_MAX_BATCH) {
+        set_err(err, n, "invalid prefill argument");
+        return 0;
+    }
+    if ((uint64_t)position + ntok > (uint64_t)E->dm.ctx) { set_err(err, n, "steps exceed ctx"); return 0; }
+    for (uint32_t t = 0; t < ntok; ++t)
+        if (tokens[t] >= (uint32_t)E->dm.vocab) { set_err(err, n, "prompt token out of range"); return 0; }
+    for (const auto& w : E->layers)
+        if (!batch_supported(E, w, true, err, n)) return 0;
+    DeviceGuard g(E->device);
+    if (!batch_reserve(E, ntok, err, n)) return 0;
+    auto& B = E->batch;
+    const int N = (int)ntok, H = E->dm.hidden, Q = E->dm.q_dim(), KV = E->dm.kv_dim();
+    const int QH = E->dm.q_heads, KVH = E->dm.kv_heads, C = E->dm.ctx;
+    Dev& d = E->dev;
+    {
+        std::vector<int> ids(N);
+        for (int t = 0; t < N; ++t) ids[t] = t;
+        if (!h2d(E, B.tcols, ids.data(), (size_t)N * 4, err, n) || !h2d(E, B.tok, tokens, (size_t)N * 4, err, n))
+            return 0;
+    }
+    qx::launch_batch_embed(B.tok, d.tok_embd, H, E->dm.vocab, N, B.x, d.err, E->stream);
+    E->prof.kernel_launches++;
+    for (int layer = 0; layer < E->dm.layers; ++layer) {
+        const LayerW& w = E->layers[layer];
+        int cnt = 0;
+        // attention RMSNorm, limbs, Q/K/V on the tensor cores
+        qx::launch_batch_norm(B.x, w.attn_norm, B.xn, H, N, E->stream);
+        qx::launch_batch_limbs(B.xn, H, N, B.bqx, B.sx, E->stream);
+        if (!proj_items(E, N, Q, &cnt, err, n)) return 0;
+        qx::launch_moe_gemm(proj_args(E, w.wq_r, H, B.qkv, (size_t)(Q + 2 * KV), 0), cnt, E->stream);
+        if (!proj_items(E, N, KV, &cnt, err, n)) return 0;
+        qx::launch_moe_gemm(proj_args(E, w.wk_r, H, B.qkv, (size_t)(Q + 2 * KV), Q), cnt, E->stream);
+        qx::launch_moe_gemm(proj_args(E, w.wv_r, H, B.qkv, (size_t)(Q + 2 * KV), Q + KV), cnt, E->stream);
+        // head norms, RoPE, the K/V rows of every token into the cache, causal attention
+        qx::launch_batch_qkv_post(B.qkv, w.q_norm, w.k_norm, d.rope, layer, (int)position, N, QH, KVH, C, B.qn,
+                                  d.kcache, d.vcache, d.kscale, d.vscale, E->stream);
+        qx::launch_batch_attn(B.qn, d.kcache, d.vcache, d.kscale, d.vscale, layer, (int)position, N, QH, KVH, C,
+                              B.ctxo, E->stream);
+        // O projection + residual
+        qx::launch_batch_limbs(B.ctxo, Q, N, B.bqx, B.sx, E->stream);
+        if (!proj_items(E, N, H, &cnt, err, n)) return 0;
+        qx::launch_moe_gemm(proj_args(E, w.wo_r, Q, B.ao, (size_t)H, 0), cnt, E->stream);
+        qx::launch_batch_add(B.x, B.ao, (size_t)N * H, E->stream);
+        E->prof.kernel_launches += 10;
+        // the MoE FFN, then its output is the next layer's residual
+        if (!moe_batch_run(E, (uint32_t)layer, N, err, n)) return 0;
+        std::swap(B.x, B.out);
+    }
+    // the head for the last prompt token only (the reference skips it for the
+    // others, src/qx_format.c:6533-6547): greedy next token at position p0 + N - 1
+    E->h_io[1] = (int)(position + ntok - 1);
+    if (!cuda_ok(cudaMemcpyAsync(d.x, B.x + (size_t)(N - 1) * H, (size_t)H * 4, cudaMemcpyDeviceToDevice, E->stream),
+                 "d2d", err, n) ||
+        !cuda_ok(cudaMemcpyAsync(d.pos, E->h_io + 1, 4, cudaMemcpyHostToDevice, E->stream), "h2d", err, n))
+        return 0;
+    Dev dh = d;
+    dh.logits_d = nullptr;
+    qx::launch_head(dh, E->stream);
+    E->prof.kernel_launches++;
+    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    if (!d2h(E, E->h_io + 2, d.token, 4, err, n) || !d2h(E, final_residual, d.x, (size_t)H * 4, err, n)) return 0;
+    if (!finish(E, err, n)) return 0;
+    *next_token = (uint32_t)E->h_io[2];
+    E->prof.decode_steps += ntok;
+    return 1;
 }
 
 QX_API int qx_cuda_attention_layer(qx_cuda_engine* E, uint32_t layer, uint32_t position, float* residual,

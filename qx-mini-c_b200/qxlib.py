@@ -126,7 +126,7 @@ ENGINE_SYMBOLS = [
     "qx_cuda_moe_layer", "qx_cuda_attention_layer", "qx_cuda_embed", "qx_cuda_kv_write", "qx_cuda_kv_read",
     "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_phase_trace", "qx_cuda_stream",
     "qx_cuda_ep_handle", "qx_cuda_ep_connect", "qx_cuda_ep_partition", "qx_cuda_kv_export", "qx_cuda_kv_import",
-    "qx_cuda_moe_batch",
+    "qx_cuda_moe_batch", "qx_cuda_prefill",
 ]
 
 VERIFY_CHECKSUMS = 0x1
@@ -150,6 +150,7 @@ def cuda():
             "qx_cuda_final_head": [P, P, P, P, U32, P, P, E, U64],
             "qx_cuda_moe_layer": [P, U32, P, P, P, P, P, E, U64],
             "qx_cuda_moe_batch": [P, U32, U32, P, P, P, P, P, E, U64],
+            "qx_cuda_prefill": [P, P, U32, U32, P, P, E, U64],
             "qx_cuda_attention_layer": [P, U32, U32, P, P, P, E, U64],
             "qx_cuda_embed": [P, U32, P, E, U64],
             "qx_cuda_kv_write": [P, U32, U32, U32, P, P, P, P, E, U64],
@@ -346,6 +347,15 @@ class Engine:
         w = np.zeros((t, 8), np.float32)
         self._call("qx_cuda_moe_batch", layer, t, _p(x), _p(out), _p(moe), _p(sel), _p(w))
         return out, moe, sel, w
+
+    def prefill(self, tokens, position=0, want_residual=False):
+        """Prompt prefill (qx_cuda_prefill): returns the greedy next token (and
+        the last prompt token's final residual)."""
+        tokens = np.ascontiguousarray(tokens, np.uint32)
+        nxt = np.zeros(1, np.uint32)
+        res = np.zeros(self.hidden, np.float32) if want_residual else None
+        self._call("qx_cuda_prefill", _p(tokens), tokens.size, position, _p(nxt), _p(res))
+        return (int(nxt[0]), res) if want_residual else int(nxt[0])
 
     def attention_layer(self, layer, position, residual):
         res = np.array(residual, np.float32, copy=True)
