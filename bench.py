@@ -252,7 +252,7 @@ def time_call(call, stream, reps, warmup=3):
     return float(np.median(times))
 
 
-def stage_configs(eng, cfg, stream, reps=10, which=("head", "moe", "attention", "decode4096", "batch")):
+def stage_configs(eng, cfg, stream, reps=10, which=("head", "moe", "attention", "decode4096", "batch", "prefill")):
     """BASELINE configs 1, 2, 3 (ctx 512 and 4096), 4 at ctx 4096 and 5
     (the batched grouped-expert MoE layer at 64 and 2048 tokens) through the
     engine's entry points, on one GPU.  Each entry streams its weights from
@@ -324,6 +324,19 @@ def stage_configs(eng, cfg, stream, reps=10, which=("head", "moe", "attention", 
                 "frac_of_bf16_sustained": round(2 * macs / us / 1e6 / bf16, 4),
                 "experts_touched": used, "weight_GB/s": round(nbytes / us / 1e3, 1),
                 "note": "device time of the whole call: %.1f MB in / out over PCIe included" % (2 * n * H * 4 / 1e6)}
+    if "prefill" in which and eng.ctx >= 2048:
+        n = 2048
+        prompt = np.random.default_rng(5).integers(0, cfg.vocab, n).astype(np.uint32)
+        us = time_call(lambda: eng.prefill(prompt, 0), stream, 3, warmup=1)
+        per_tok = (Q + 2 * KV) * H + H * Q + E * H + 8 * 3 * I * H          # weight multiply-adds per token and layer
+        macs = n * cfg.layers * per_tok + cfg.vocab * H                    # + the head for the last token
+        out["config5_prefill_2048"] = {
+            "config": "2048-token prompt prefill, 48 layers, tcgen05 projection and expert GEMMs, batched causal attention",
+            "us_per_call": round(us, 1), "tokens_per_s": round(n / (us / 1e6), 1),
+            "useful_TFLOP/s": round(2 * macs / us / 1e6, 2),
+            "frac_of_bf16_sustained": round(2 * macs / us / 1e6 / bf16, 4),
+            "note": "the reference runs a prompt one token at a time (src/qx_format.c:6250-6547); the result is "
+                    "bit-identical to this engine's per-token step (tests/test_gpu_batch.py)"}
     out["peak_source"] = peak_kind
     return out
 
@@ -364,7 +377,7 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling case only: the same model with fewer layers (default: all 48)")
     ap.add_argument("--no-stage-configs", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "head", "moe", "attention", "batch"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "head", "moe", "attention", "batch", "prefill"],
                     help="decode = config 4 (the bench line); head/moe/attention = configs 1-3 through the "
                          "stage entry points, one JSON line each with the stage's HBM bandwidth")
     args = ap.parse_args()

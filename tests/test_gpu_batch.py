@@ -93,3 +93,80 @@ def test_moe_batch_arguments(mini_image):
         check_against_per_token(eng, 0, x, range(3))
     finally:
         eng.close()
+
+
+def stepwise(eng, prompt, position=0):
+    r = None
+    for p, t in enumerate(prompt):
+        r = eng.decode_step(int(t), position + p, want_residual=True)
+    return r
+
+
+@pytest.mark.parametrize("geometry,n", [("mini", 1), ("mini", 77), ("full4", 300)])
+def test_prefill_equals_the_per_token_prompt_loop(geometry, n):
+    """qx_cuda_prefill against the prompt run one token at a time through the
+    decode step (the reference's prompt loop, src/qx_format.c:6250-6547):
+    the next token, the last token's final residual and every INT8 K/V row
+    and scale of every layer must be identical."""
+    cfg = qxlib.mini_config(7) if geometry == "mini" else qxlib.synth_config(7, layers=4)
+    eng = qxlib.Engine(qxlib.build_image(cfg), ctx=n + 24)
+    try:
+        prompt = np.random.default_rng(n).integers(0, eng.vocab, n).astype(np.uint32)
+        eng.reset()
+        nxt, res = eng.prefill(prompt, 0, want_residual=True)
+        kv_pre = [eng.kv_read(layer, 0, n) for layer in range(eng.layers)]
+        cont = eng.generate(nxt, n, 8)            # decoding continues from the prefilled cache
+        eng.reset()
+        r = stepwise(eng, prompt)
+        assert nxt == r["token"]
+        np.testing.assert_array_equal(res.view(np.uint32), r["residual"].view(np.uint32))
+        for layer in range(eng.layers):
+            k, v, ks, vs = eng.kv_read(layer, 0, n)
+            np.testing.assert_array_equal(kv_pre[layer][0], k)
+            np.testing.assert_array_equal(kv_pre[layer][1], v)
+            np.testing.assert_array_equal(kv_pre[layer][2].view(np.uint32), ks.view(np.uint32))
+            np.testing.assert_array_equal(kv_pre[layer][3].view(np.uint32), vs.view(np.uint32))
+        assert list(eng.generate(nxt, n, 8)) == list(cont)
+    finally:
+        eng.close()
+
+
+def test_prefill_mini_matches_the_reference(ref, mini_image):
+    """The reference's own C path (the shim's decode step, pinned to its
+    unmodified state loop) decodes 5 tokens and then a 24-token prompt one
+    token at a time; the engine decodes the same 5 tokens and prefills the
+    prompt at position 5.  The next token and the whole INT8 K/V cache must
+    agree."""
+    eng = qxlib.Engine(mini_image, ctx=64)
+    try:
+        R = ref.open_image(mini_image)
+        kv = R.new_kv(64)
+        prompt = np.random.default_rng(3).integers(0, eng.vocab, 24).astype(np.uint32)
+        lead = [42]
+        for p in range(5):
+            lead.append(R.decode_step(lead[-1], p, kv)["token"])
+        rt = None
+        for p, t in enumerate(prompt):
+            rt = R.decode_step(int(t), 5 + p, kv)
+        eng.reset()
+        for p in range(5):
+            eng.decode_step(lead[p], p)
+        assert eng.prefill(prompt, 5) == rt["token"]
+        for layer in range(eng.layers):
+            k, v, ks, vs = eng.kv_read(layer, 0, 29)
+            np.testing.assert_array_equal(k, kv["k"][layer, :29])
+            np.testing.assert_array_equal(v, kv["v"][layer, :29])
+            np.testing.assert_array_equal(ks, kv["ks"][layer, :29])
+    finally:
+        eng.close()
+
+
+def test_prefill_arguments(mini_image):
+    eng = qxlib.Engine(mini_image, ctx=32)
+    try:
+        with pytest.raises(RuntimeError, match="steps exceed ctx"):
+            eng.prefill(np.zeros(40, np.uint32), 0)
+        with pytest.raises(RuntimeError, match="prompt token out of range"):
+            eng.prefill(np.array([1, eng.vocab], np.uint32), 0)
+    finally:
+        eng.close()
