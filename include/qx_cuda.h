@@ -170,6 +170,20 @@ int qx_cuda_moe_batch(qx_cuda_engine *engine, uint32_t layer, uint32_t tokens, c
 int qx_cuda_prefill(qx_cuda_engine *engine, const uint32_t *tokens, uint32_t tokens_count, uint32_t position,
                     uint32_t *next_token, float *final_residual, char *err, uint64_t err_len);
 
+/* One greedy decode step for `count` independent sequences at once (batched
+ * decode).  Sequence i occupies KV slot slots[i] (< QX_CUDA_MAX_SLOTS, each
+ * slot its own INT8 cache of ctx_tokens positions, allocated on the first
+ * call: slots x layers x ctx x (2 x kv + 8) bytes), feeds tokens[i] at
+ * positions[i] and gets next_tokens[i].  Per sequence this is the reference's
+ * state-loop step (src/qx_format.c:6250-6627), which has no batched form; the
+ * projections, experts and head run as GEMMs over the batch on the tcgen05
+ * tensor cores.  A slot's positions must be fed in order from 0 (positions
+ * beyond the current one are never read).  Slots are separate from the
+ * engine's single-sequence cache. */
+#define QX_CUDA_MAX_SLOTS 64u
+int qx_cuda_decode_batch(qx_cuda_engine *engine, uint32_t count, const uint32_t *slots, const uint32_t *tokens,
+                         const uint32_t *positions, uint32_t *next_tokens, char *err, uint64_t err_len);
+
 /* The attention half of one layer at `position`, state-loop order
  * (src/qx_format.c:6283-6423 with qx_rope_gqa_attention_partial, :5051-5196):
  * attn RMSNorm, K/V projection, K head norm + RoPE, INT8 append at

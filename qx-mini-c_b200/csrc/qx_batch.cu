@@ -124,12 +124,15 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 // row as hi/lo digits into the operand slabs.
 // One row's source bytes of one block: the group scales and the 128 code
 // bytes, loaded a block ahead so the global latency hides behind the MMAs.
-struct RowSrc {
+template <int NW>
+struct RowSrcN {
     uint4 sv;
-    uint4 cw[8];
+    uint4 cw[NW];
 };
+using RowSrc = RowSrcN<8>;
 
-__device__ __forceinline__ void load_src(const uint8_t* scales, const uint8_t* codes, bool scales16, RowSrc& s) {
+template <int NW>
+__device__ __forceinline__ void load_src(const uint8_t* scales, const uint8_t* codes, bool scales16, RowSrcN<NW>& s) {
     if (scales16) {
         s.sv = *reinterpret_cast<const uint4*>(scales);
     } else {
@@ -137,7 +140,31 @@ __device__ __forceinline__ void load_src(const uint8_t* scales, const uint8_t* c
         s.sv = make_uint4(v.x, v.y, 0u, 0u);
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s.cw[i] = *reinterpret_cast<const uint4*>(codes + 16 * i);
+    for (int i = 0; i < NW; ++i) s.cw[i] = *reinterpret_cast<const uint4*>(codes + 16 * i);
+}
+
+// R8 block (the re-laid Q6_K head: 16 int8 group scales, then 16 units of 16
+// bytes; unit 4 (gq >> 2) + t holds the int8 weights q - 32 of values
+// 16 gq + 4 t .. + 3 at byte 4 (gq & 3)): A = scale * (q - 32) per value,
+// |A| <= 4096, as hi/lo digits.
+__device__ __forceinline__ void decode_r8_row(const RowSrcN<16>& src, int r, uint8_t* ahi, uint8_t* alo) {
+    const uint32_t sw[4] = {src.sv.x, src.sv.y, src.sv.z, src.sv.w};
+#pragma unroll
+    for (int gq = 0; gq < 16; ++gq) {
+        const int sc = (int)(int8_t)(uint8_t)(sw[gq >> 2] >> (8 * (gq & 3)));
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t W = word_of(src.cw, 16 * (gq >> 2) + 4 * t + (gq & 3));
+            const int a0 = sc * (int)(int8_t)(uint8_t)W, a1 = sc * (int)(int8_t)(uint8_t)(W >> 8);
+            const int a2 = sc * (int)(int8_t)(uint8_t)(W >> 16), a3 = sc * (int)(int8_t)(uint8_t)(W >> 24);
+            hw[t] = pack4(a0 >> 6, a1 >> 6, a2 >> 6, a3 >> 6);
+            lw[t] = pack4(a0 & 63, a1 & 63, a2 & 63, a3 & 63);
+        }
+        const uint32_t o = op_off(r, 16 * gq);
+        *reinterpret_cast<uint4*>(ahi + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(alo + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
 }
 
 __device__ __forceinline__ void decode_iq2r_row(const RowSrc& src, int r, uint8_t* ahi, uint8_t* alo) {
@@ -221,6 +248,7 @@ __device__ __forceinline__ void decode_r4_row(const RowSrc& src, int r, uint8_t*
 // block: decode A (hi/lo), stage B, 16 MMAs (8 K steps x 2 digits), commit,
 // fold the accumulators.  Output out[col * out_stride + row] = the dot
 // product as a float (non-finite -> 0, src/qx_format.c:4783).
+template <int FMT>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 127) & ~(uintptr_t)127);
@@ -265,12 +293,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     for (int j = 0; j < kTokTile; ++j) acc[j] = 0.0;
     unsigned phase = 0;
     bool ok = true;
-    const bool iq2 = a.fmt == kGemmIq2r;
-    auto src_at = [&](int b, RowSrc& s) {
-        if (iq2) load_src(mat + a.hdr + (size_t)b * 144, mat + a.hdr + (size_t)b * 144 + 16, true, s);
+    using Src = RowSrcN<FMT == kGemmR8 ? 16 : 8>;
+    auto src_at = [&](int b, Src& s) {
+        if (FMT == kGemmIq2r) load_src(mat + a.hdr + (size_t)b * 144, mat + a.hdr + (size_t)b * 144 + 16, true, s);
+        else if (FMT == kGemmR8) load_src(mat + a.hdr + (size_t)b * 272, mat + a.hdr + (size_t)b * 272 + 16, true, s);
         else load_src(mat + a.hdr + 8 * b, mat + a.codes + 128 * b, false, s);
     };
-    RowSrc src;
+    Src src;
     src_at(0, src);
     // B: each column's 2 KB of a block (8 slabs x 256 B: limbs 0-6 and the
     // ones column of 32 values) to slab s, 8-row group j
@@ -287,8 +316,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     stage_b(0);
     for (int b = 0; b < a.nblk && ok; ++b) {
         // A: this thread's row of block b (source loaded during the previous block)
-        if (iq2) decode_iq2r_row(src, r, ahi, alo);
-        else if (a.fmt == kGemmR4Iq4) decode_r4_row<true>(src, r, ahi, alo);
+        if constexpr (FMT == kGemmIq2r) decode_iq2r_row(src, r, ahi, alo);
+        else if constexpr (FMT == kGemmR4Iq4) decode_r4_row<true>(src, r, ahi, alo);
+        else if constexpr (FMT == kGemmR8) decode_r8_row(src, r, ahi, alo);
         else decode_r4_row<false>(src, r, ahi, alo);
         cp_async_wait<0>();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core
@@ -359,7 +389,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
 #pragma unroll
         for (int j = 0; j < kTokTile; ++j) {
             const double v = acc[j];
-            if (j < ncol) a.out[(size_t)cols_s[j] * a.out_stride + a.out_off + it.row0 + r] = isfinite(v) ? (float)v : 0.0f;
+            if (j < ncol) {
+                const size_t o = (size_t)cols_s[j] * a.out_stride + a.out_off + it.row0 + r;
+                if (a.out_d) a.out_d[o] = v;                       // the head: double logits
+                else a.out[o] = isfinite(v) ? (float)v : 0.0f;
+            }
         }
     }
     tc_fence_after();
@@ -567,13 +601,16 @@ __global__ void __launch_bounds__(256) k_batch_embed(const uint32_t* tokens, con
 // the INT8 K/V row (one scale per token over all KV values, :4449-4463)
 // appended to the cache at (layer, p0 + t) (:6343-6400).
 __global__ void __launch_bounds__(256) k_batch_qkv_post(const float* qkv, const float* q_norm, const float* k_norm,
-                                                        const double* rope, int layer, int p0, int QH, int KVH,
-                                                        int ctx, float* qn, int8_t* kcache, int8_t* vcache,
-                                                        float* kscale, float* vscale) {
+                                                        const double* rope, int layer, const int* tpos,
+                                                        const int* tslot, KvView kv, int QH, int KVH, float* qn) {
     constexpr int D = 128;
     __shared__ float v[4096 + 2 * 1024];
     __shared__ float scratch_f[8];
-    const int Q = QH * D, KV = KVH * D, t = blockIdx.x, pos = p0 + t;
+    const int Q = QH * D, KV = KVH * D, t = blockIdx.x, pos = tpos[t], ctx = kv.ctx;
+    int8_t* kcache = kv.k + (size_t)tslot[t] * kv.slot_rows * KV;
+    int8_t* vcache = kv.v + (size_t)tslot[t] * kv.slot_rows * KV;
+    float* kscale = kv.ks + (size_t)tslot[t] * kv.slot_rows;
+    float* vscale = kv.vs + (size_t)tslot[t] * kv.slot_rows;
     const float* src = qkv + (size_t)t * (Q + 2 * KV);
     for (int j = threadIdx.x; j < Q + 2 * KV; j += blockDim.x) v[j] = src[j];
     __syncthreads();
@@ -611,15 +648,18 @@ __global__ void __launch_bounds__(256) k_batch_qkv_post(const float* qkv, const 
 // in float over positions in order (src/qx_format.c:5127-5172) - the same
 // arithmetic as the decode step's attention.  128 threads; dynamic shared
 // memory: (p0 + t + 1) doubles.
-__global__ void __launch_bounds__(128) k_batch_attn(const float* qn, const int8_t* kcache, const int8_t* vcache,
-                                                    const float* kscale, const float* vscale, int layer, int p0,
-                                                    int QH, int KVH, int ctx, float* ctx_out) {
+__global__ void __launch_bounds__(128) k_batch_attn(const float* qn, KvView kv, int layer, const int* tpos,
+                                                    const int* tslot, int QH, int KVH, float* ctx_out) {
     constexpr int D = 128;
     extern __shared__ __align__(16) double w_s[];
     __shared__ double qd[D];
     __shared__ double scratch_d[4];
     const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x, g = h / (QH / KVH);
-    const int Q = QH * D, KV = KVH * D, T = p0 + t + 1;
+    const int Q = QH * D, KV = KVH * D, T = tpos[t] + 1, ctx = kv.ctx;
+    const int8_t* kcache = kv.k + (size_t)tslot[t] * kv.slot_rows * KV;
+    const int8_t* vcache = kv.v + (size_t)tslot[t] * kv.slot_rows * KV;
+    const float* kscale = kv.ks + (size_t)tslot[t] * kv.slot_rows;
+    const float* vscale = kv.vs + (size_t)tslot[t] * kv.slot_rows;
     qd[i] = (double)qn[(size_t)t * Q + h * D + i];
     __syncthreads();
     const double sqrt_d = sqrt((double)D);
@@ -643,6 +683,36 @@ __global__ void __launch_bounds__(128) k_batch_attn(const float* qn, const int8_
     ctx_out[(size_t)t * Q + h * D + i] = acc;
 }
 
+// Greedy pick per token over double logits [ntok][V]: the largest, lowest
+// index on ties (src/qx_format.c:3723-3730); a non-finite logit is an error
+// (:3715).
+__global__ void __launch_bounds__(1024) k_batch_argmax(const double* logits, int V, uint32_t* out, int* err) {
+    __shared__ double bv_s[32];
+    __shared__ int bi_s[32];
+    const double* lg = logits + (size_t)blockIdx.x * V;
+    double bv = -1.0e300;
+    int bi = 0x7fffffff;
+    bool bad = false;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const double v = lg[i];
+        if (!isfinite(v)) bad = true;
+        if (v > bv) { bv = v; bi = i; }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (bad) atomicOr(err, kErrNonFinite);
+    if ((threadIdx.x & 31) == 0) { bv_s[threadIdx.x >> 5] = bv; bi_s[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (bv_s[w] > bv || (bv_s[w] == bv && bi_s[w] < bi)) { bv = bv_s[w]; bi = bi_s[w]; }
+        out[blockIdx.x] = (uint32_t)bi;
+    }
+}
+
 // x[i] += y[i] (the residual adds, float, src/qx_format.c:6420-6423).
 __global__ void k_batch_add(float* x, const float* y, size_t n) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -657,18 +727,19 @@ void launch_batch_embed(const uint32_t* tokens, const uint8_t* emb, int H, int V
 }
 
 void launch_batch_qkv_post(const float* qkv, const float* q_norm, const float* k_norm, const double* rope, int layer,
-                           int p0, int ntok, int QH, int KVH, int ctx, float* qn, int8_t* kcache, int8_t* vcache,
-                           float* kscale, float* vscale, cudaStream_t st) {
-    k_batch_qkv_post<<<ntok, 256, 0, st>>>(qkv, q_norm, k_norm, rope, layer, p0, QH, KVH, ctx, qn, kcache, vcache,
-                                          kscale, vscale);
+                           const int* tpos, const int* tslot, const KvView& kv, int ntok, int QH, int KVH, float* qn,
+                           cudaStream_t st) {
+    k_batch_qkv_post<<<ntok, 256, 0, st>>>(qkv, q_norm, k_norm, rope, layer, tpos, tslot, kv, QH, KVH, qn);
 }
 
-void launch_batch_attn(const float* qn, const int8_t* kcache, const int8_t* vcache, const float* kscale,
-                       const float* vscale, int layer, int p0, int ntok, int QH, int KVH, int ctx, float* ctx_out,
-                       cudaStream_t st) {
-    const size_t smem = (size_t)(p0 + ntok) * 8;
-    k_batch_attn<<<dim3(ntok, QH), 128, smem, st>>>(qn, kcache, vcache, kscale, vscale, layer, p0, QH, KVH, ctx,
-                                                    ctx_out);
+void launch_batch_attn(const float* qn, const KvView& kv, int layer, const int* tpos, const int* tslot, int max_pos,
+                       int ntok, int QH, int KVH, float* ctx_out, cudaStream_t st) {
+    const size_t smem = (size_t)(max_pos + 1) * 8;
+    k_batch_attn<<<dim3(ntok, QH), 128, smem, st>>>(qn, kv, layer, tpos, tslot, QH, KVH, ctx_out);
+}
+
+void launch_batch_argmax(const double* logits, int V, int ntok, uint32_t* out, int* err, cudaStream_t st) {
+    k_batch_argmax<<<ntok, 1024, 0, st>>>(logits, V, out, err);
 }
 
 void launch_batch_add(float* x, const float* y, size_t n, cudaStream_t st) {
@@ -679,7 +750,10 @@ uint32_t moe_gemm_smem_bytes() { return kSmemGemm; }
 size_t batch_router_smem_bytes(int H, int E) { return (size_t)kRouterTok * (H + 2 * E) * 8; }
 
 cudaError_t moe_batch_configure() {
-    cudaError_t e = cudaFuncSetAttribute(k_moe_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemGemm);
+    cudaError_t e = cudaSuccess;
+    for (const void* f : {(const void*)k_moe_gemm<kGemmIq2r>, (const void*)k_moe_gemm<kGemmR4Iq3>,
+                          (const void*)k_moe_gemm<kGemmR4Iq4>, (const void*)k_moe_gemm<kGemmR8>})
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemGemm);
     int dev = 0, optin = 0;
     if (e == cudaSuccess) e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -704,7 +778,13 @@ void launch_batch_router(const float* xn, const float* router, int H, int E, int
 }
 
 void launch_moe_gemm(const GemmArgs& a, int nitems, cudaStream_t st) {
-    if (nitems > 0) k_moe_gemm<<<nitems, kGemmThreads, kSmemGemm, st>>>(a);
+    if (nitems <= 0) return;
+    switch (a.fmt) {
+        case kGemmIq2r: k_moe_gemm<kGemmIq2r><<<nitems, kGemmThreads, kSmemGemm, st>>>(a); break;
+        case kGemmR4Iq3: k_moe_gemm<kGemmR4Iq3><<<nitems, kGemmThreads, kSmemGemm, st>>>(a); break;
+        case kGemmR4Iq4: k_moe_gemm<kGemmR4Iq4><<<nitems, kGemmThreads, kSmemGemm, st>>>(a); break;
+        default: k_moe_gemm<kGemmR8><<<nitems, kGemmThreads, kSmemGemm, st>>>(a); break;
+    }
 }
 
 void launch_batch_swiglu(const float* gu, int I, int nslots, float* h, cudaStream_t st) {

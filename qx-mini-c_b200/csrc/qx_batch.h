@@ -12,7 +12,7 @@ namespace qx {
 struct GemmItem {
     int expert, col0, ncols, row0;
 };
-enum { kGemmIq2r = 0, kGemmR4Iq3 = 1, kGemmR4Iq4 = 2 };
+enum { kGemmIq2r = 0, kGemmR4Iq3 = 1, kGemmR4Iq4 = 2, kGemmR8 = 3 };
 
 struct GemmArgs {
     const GemmItem* items;
@@ -24,14 +24,26 @@ struct GemmArgs {
     int codes;                    // R4: first code byte
     int nblk;                     // 256-value blocks per row (K / 256)
     int fmt;                      // kGemmIq2r or kGemmR4Iq3
-    int fexp;                     // block factor d * 2^(fexp - S): -3 (IQ2_XS), -2 (IQ3_XXS), 0 (IQ4_XS)
+    int fexp;                     // block factor d * 2^(fexp - S): -3 (IQ2_XS), -2 (IQ3_XXS), 0 (IQ4_XS, Q6_K)
     const uint8_t* bq;            // limbs [rows][nblk][2048 B] (k_batch_limbs)
     const int* sexp;              // block exponents [rows][nblk]
     int b_by_token;               // 1: B row = column id / 8 (the token), 0: B row = column id
-    float* out;                   // out[col * out_stride + out_off + row]
+    float* out;                   // out[col * out_stride + out_off + row] (non-finite -> 0)
+    double* out_d;                // if set: the double results there instead (the head's logits)
     size_t out_stride;
     int out_off;
     int* err;
+};
+
+// An INT8 KV cache of `slots` sequences: [slot][layer][ctx][kv] bytes and
+// [slot][layer][ctx] scales, slot_rows = layers * ctx.
+struct KvView {
+    int8_t* k;
+    int8_t* v;
+    float* ks;
+    float* vs;
+    size_t slot_rows;
+    int ctx;
 };
 
 uint32_t moe_gemm_smem_bytes();
@@ -46,11 +58,11 @@ void launch_batch_swiglu(const float* gu, int I, int nslots, float* h, cudaStrea
 void launch_batch_embed(const uint32_t* tokens, const uint8_t* emb, int H, int V, int ntok, float* x, int* err,
                         cudaStream_t st);
 void launch_batch_qkv_post(const float* qkv, const float* q_norm, const float* k_norm, const double* rope, int layer,
-                           int p0, int ntok, int QH, int KVH, int ctx, float* qn, int8_t* kcache, int8_t* vcache,
-                           float* kscale, float* vscale, cudaStream_t st);
-void launch_batch_attn(const float* qn, const int8_t* kcache, const int8_t* vcache, const float* kscale,
-                       const float* vscale, int layer, int p0, int ntok, int QH, int KVH, int ctx, float* ctx_out,
-                       cudaStream_t st);
+                           const int* tpos, const int* tslot, const KvView& kv, int ntok, int QH, int KVH, float* qn,
+                           cudaStream_t st);
+void launch_batch_attn(const float* qn, const KvView& kv, int layer, const int* tpos, const int* tslot, int max_pos,
+                       int ntok, int QH, int KVH, float* ctx_out, cudaStream_t st);
+void launch_batch_argmax(const double* logits, int V, int ntok, uint32_t* out, int* err, cudaStream_t st);
 void launch_batch_add(float* x, const float* y, size_t n, cudaStream_t st);
 void launch_batch_combine(const float* x, const float* y, const double* wsel, int H, int ntok, float* moe, float* out,
                           cudaStream_t st);

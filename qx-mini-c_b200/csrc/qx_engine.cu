@@ -83,11 +83,15 @@ struct qx_cuda_engine {
         void* mem = nullptr;
         float *x, *xn, *gu, *h, *y, *out, *moe, *qkv, *qn, *ctxo, *ao;
         uint8_t *bqx, *bqh;
-        int *sx, *sh, *sel, *cols, *tcols;
-        uint32_t* tok;
+        int *sx, *sh, *sel, *cols, *tcols, *tpos, *tslot;
+        uint32_t *tok, *next;
+        double* logits;                  // [cap][vocab] (batched decode's head)
         double* wsel;
         qx::GemmItem* items;
         size_t item_cap;
+        // sequence slots of qx_cuda_decode_batch: their own INT8 KV caches
+        void* slot_mem = nullptr;
+        qx::KvView slots{};
     } batch;
 };
 
@@ -205,6 +209,7 @@ QX_API void qx_cuda_engine_destroy(qx_cuda_engine* E) {
     if (E->layers_dev) cudaFree(E->layers_dev);
     if (E->relay) cudaFree(E->relay);
     if (E->batch.mem) cudaFree(E->batch.mem);
+    if (E->batch.slot_mem) cudaFree(E->batch.slot_mem);
     for (void* p : E->ep_opened) cudaIpcCloseMemHandle(p);
     if (E->ep_xchg) cudaFree(E->ep_xchg);
     if (E->ep_peers_dev) cudaFree(E->ep_peers_dev);
@@ -828,8 +833,11 @@ bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
     if (B.mem) { cudaFree(B.mem); B.mem = nullptr; B.cap = 0; }
     const size_t H = E->dm.hidden, I = E->dm.moe_inter, S = ntok * 8;
     const size_t Q = E->dm.q_dim(), KV = E->dm.kv_dim(), K = std::max(H, Q);
-    const size_t items = std::max((S / 16 + (size_t)E->dm.experts) * std::max(2 * I / 128, H / 128),
-                                  (ntok / 16 + 1) * std::max(Q / 128, H / 128));
+    const size_t V = E->dm.vocab;
+    const size_t nhead = std::min<size_t>(ntok, QX_CUDA_MAX_SLOTS);   // tokens the batched head serves
+    const size_t items = std::max(std::max((S / 16 + (size_t)E->dm.experts) * std::max(2 * I / 128, H / 128),
+                                           (ntok / 16 + 1) * std::max(Q / 128, H / 128)),
+                                  (nhead / 16 + 1) * (V / 128));
     size_t off = 0;
     std::vector<std::pair<void**, size_t>> parts = {
         {(void**)&B.x, ntok * H * 4}, {(void**)&B.xn, ntok * H * 4}, {(void**)&B.out, ntok * H * 4},
@@ -838,7 +846,9 @@ bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
         {(void**)&B.sx, ntok * (K / 256) * 4}, {(void**)&B.sh, S * (I / 256) * 4}, {(void**)&B.sel, S * 4},
         {(void**)&B.cols, S * 4}, {(void**)&B.wsel, S * 8}, {(void**)&B.items, items * sizeof(qx::GemmItem)},
         {(void**)&B.qkv, ntok * (Q + 2 * KV) * 4}, {(void**)&B.qn, ntok * Q * 4}, {(void**)&B.ctxo, ntok * Q * 4},
-        {(void**)&B.ao, ntok * H * 4}, {(void**)&B.tcols, ntok * 4}, {(void**)&B.tok, ntok * 4}};
+        {(void**)&B.ao, ntok * H * 4}, {(void**)&B.tcols, ntok * 4}, {(void**)&B.tok, ntok * 4},
+        {(void**)&B.tpos, ntok * 4}, {(void**)&B.tslot, ntok * 4}, {(void**)&B.next, ntok * 4},
+        {(void**)&B.logits, nhead * V * 8}};
     for (auto& p : parts) off = align_up(off + p.second, 256);
     if (!cuda_ok(cudaMalloc(&B.mem, off), "cudaMalloc(batch)", err, n)) return false;
     off = 0;
@@ -1025,6 +1035,37 @@ QX_API int qx_cuda_moe_batch(qx_cuda_engine* E, uint32_t layer, uint32_t ntok, c
     return finish(E, err, n) ? 1 : 0;
 }
 
+namespace {
+
+// The attention half of one layer for the N tokens in B.x (positions B.tpos,
+// KV slots B.tslot of `kv`): attention RMSNorm, Q/K/V on the tensor cores,
+// head norms + RoPE + the K/V rows into the cache, causal attention, O
+// projection, residual add.  Leaves the stream running.
+bool attn_batch_run(qx_cuda_engine* E, int layer, int N, const qx::KvView& kv, int max_pos, char* err, uint64_t n) {
+    auto& B = E->batch;
+    const LayerW& w = E->layers[layer];
+    const int H = E->dm.hidden, Q = E->dm.q_dim(), KV = E->dm.kv_dim(), QH = E->dm.q_heads, KVH = E->dm.kv_heads;
+    int cnt = 0;
+    qx::launch_batch_norm(B.x, w.attn_norm, B.xn, H, N, E->stream);
+    qx::launch_batch_limbs(B.xn, H, N, B.bqx, B.sx, E->stream);
+    if (!proj_items(E, N, Q, &cnt, err, n)) return false;
+    qx::launch_moe_gemm(proj_args(E, w.wq_r, H, B.qkv, (size_t)(Q + 2 * KV), 0), cnt, E->stream);
+    if (!proj_items(E, N, KV, &cnt, err, n)) return false;
+    qx::launch_moe_gemm(proj_args(E, w.wk_r, H, B.qkv, (size_t)(Q + 2 * KV), Q), cnt, E->stream);
+    qx::launch_moe_gemm(proj_args(E, w.wv_r, H, B.qkv, (size_t)(Q + 2 * KV), Q + KV), cnt, E->stream);
+    qx::launch_batch_qkv_post(B.qkv, w.q_norm, w.k_norm, E->dev.rope, layer, B.tpos, B.tslot, kv, N, QH, KVH, B.qn,
+                              E->stream);
+    qx::launch_batch_attn(B.qn, kv, layer, B.tpos, B.tslot, max_pos, N, QH, KVH, B.ctxo, E->stream);
+    qx::launch_batch_limbs(B.ctxo, Q, N, B.bqx, B.sx, E->stream);
+    if (!proj_items(E, N, H, &cnt, err, n)) return false;
+    qx::launch_moe_gemm(proj_args(E, w.wo_r, Q, B.ao, (size_t)H, 0), cnt, E->stream);
+    qx::launch_batch_add(B.x, B.ao, (size_t)N * H, E->stream);
+    E->prof.kernel_launches += 10;
+    return cuda_ok(cudaGetLastError(), "kernel launch", err, n);
+}
+
+}  // namespace
+
 QX_API int qx_cuda_prefill(qx_cuda_engine* E, const uint32_t* tokens, uint32_t ntok, uint32_t position,
                            uint32_t* next_token, float* final_residual, char* err, uint64_t n) {
     if (!E || !tokens || !next_token || ntok == 0 || ntok > QX_CUDA_MAX_BATCH) {
@@ -1039,8 +1080,7 @@ QX_API int qx_cuda_prefill(qx_cuda_engine* E, const uint32_t* tokens, uint32_t n
     DeviceGuard g(E->device);
     if (!batch_reserve(E, ntok, err, n)) return 0;
     auto& B = E->batch;
-    const int N = (int)ntok, H = E->dm.hidden, Q = E->dm.q_dim(), KV = E->dm.kv_dim();
-    const int QH = E->dm.q_heads, KVH = E->dm.kv_heads, C = E->dm.ctx;
+    const int N = (int)ntok, H = E->dm.hidden, C = E->dm.ctx;
     Dev& d = E->dev;
     {
         std::vector<int> ids(N);
@@ -1048,30 +1088,17 @@ QX_API int qx_cuda_prefill(qx_cuda_engine* E, const uint32_t* tokens, uint32_t n
         if (!h2d(E, B.tcols, ids.data(), (size_t)N * 4, err, n) || !h2d(E, B.tok, tokens, (size_t)N * 4, err, n))
             return 0;
     }
+    {
+        std::vector<int> pos(N), zero(N, 0);
+        for (int t = 0; t < N; ++t) pos[t] = (int)position + t;
+        if (!h2d(E, B.tpos, pos.data(), (size_t)N * 4, err, n) || !h2d(E, B.tslot, zero.data(), (size_t)N * 4, err, n))
+            return 0;
+    }
+    const qx::KvView kv{d.kcache, d.vcache, d.kscale, d.vscale, 0, C};
     qx::launch_batch_embed(B.tok, d.tok_embd, H, E->dm.vocab, N, B.x, d.err, E->stream);
     E->prof.kernel_launches++;
     for (int layer = 0; layer < E->dm.layers; ++layer) {
-        const LayerW& w = E->layers[layer];
-        int cnt = 0;
-        // attention RMSNorm, limbs, Q/K/V on the tensor cores
-        qx::launch_batch_norm(B.x, w.attn_norm, B.xn, H, N, E->stream);
-        qx::launch_batch_limbs(B.xn, H, N, B.bqx, B.sx, E->stream);
-        if (!proj_items(E, N, Q, &cnt, err, n)) return 0;
-        qx::launch_moe_gemm(proj_args(E, w.wq_r, H, B.qkv, (size_t)(Q + 2 * KV), 0), cnt, E->stream);
-        if (!proj_items(E, N, KV, &cnt, err, n)) return 0;
-        qx::launch_moe_gemm(proj_args(E, w.wk_r, H, B.qkv, (size_t)(Q + 2 * KV), Q), cnt, E->stream);
-        qx::launch_moe_gemm(proj_args(E, w.wv_r, H, B.qkv, (size_t)(Q + 2 * KV), Q + KV), cnt, E->stream);
-        // head norms, RoPE, the K/V rows of every token into the cache, causal attention
-        qx::launch_batch_qkv_post(B.qkv, w.q_norm, w.k_norm, d.rope, layer, (int)position, N, QH, KVH, C, B.qn,
-                                  d.kcache, d.vcache, d.kscale, d.vscale, E->stream);
-        qx::launch_batch_attn(B.qn, d.kcache, d.vcache, d.kscale, d.vscale, layer, (int)position, N, QH, KVH, C,
-                              B.ctxo, E->stream);
-        // O projection + residual
-        qx::launch_batch_limbs(B.ctxo, Q, N, B.bqx, B.sx, E->stream);
-        if (!proj_items(E, N, H, &cnt, err, n)) return 0;
-        qx::launch_moe_gemm(proj_args(E, w.wo_r, Q, B.ao, (size_t)H, 0), cnt, E->stream);
-        qx::launch_batch_add(B.x, B.ao, (size_t)N * H, E->stream);
-        E->prof.kernel_launches += 10;
+        if (!attn_batch_run(E, layer, N, kv, (int)position + N - 1, err, n)) return 0;
         // the MoE FFN, then its output is the next layer's residual
         if (!moe_batch_run(E, (uint32_t)layer, N, err, n)) return 0;
         std::swap(B.x, B.out);
@@ -1092,6 +1119,76 @@ QX_API int qx_cuda_prefill(qx_cuda_engine* E, const uint32_t* tokens, uint32_t n
     if (!finish(E, err, n)) return 0;
     *next_token = (uint32_t)E->h_io[2];
     E->prof.decode_steps += ntok;
+    return 1;
+}
+
+QX_API int qx_cuda_decode_batch(qx_cuda_engine* E, uint32_t nseq, const uint32_t* slots, const uint32_t* tokens,
+                                const uint32_t* positions, uint32_t* next_tokens, char* err, uint64_t n) {
+    if (!E || !slots || !tokens || !positions || !next_tokens || nseq == 0 || nseq > QX_CUDA_MAX_SLOTS) {
+        set_err(err, n, "invalid batched decode argument");
+        return 0;
+    }
+    int max_pos = 0;
+    for (uint32_t i = 0; i < nseq; ++i) {
+        if (slots[i] >= QX_CUDA_MAX_SLOTS) { set_err(err, n, "invalid batched decode argument"); return 0; }
+        for (uint32_t j = 0; j < i; ++j)
+            if (slots[j] == slots[i]) { set_err(err, n, "a sequence slot appears twice in one batch"); return 0; }
+        if (tokens[i] >= (uint32_t)E->dm.vocab) { set_err(err, n, "prompt token out of range"); return 0; }
+        if (positions[i] >= (uint32_t)E->dm.ctx) { set_err(err, n, "steps exceed ctx"); return 0; }
+        max_pos = std::max(max_pos, (int)positions[i]);
+    }
+    for (const auto& w : E->layers)
+        if (!batch_supported(E, w, true, err, n)) return 0;
+    if (!E->dev.head_r || E->dm.vocab % 128) { set_err(err, n, "batched decode needs the re-laid head"); return 0; }
+    DeviceGuard g(E->device);
+    if (!batch_reserve(E, std::max<uint32_t>(nseq, 16), err, n)) return 0;
+    auto& B = E->batch;
+    const size_t L = E->dm.layers, C = E->dm.ctx, KV = E->dm.kv_dim(), rows = L * C;
+    if (!B.slot_mem) {                    // every slot's KV, zeroed once (positions beyond a slot's are not read)
+        const size_t bytes = (size_t)QX_CUDA_MAX_SLOTS * rows * (2 * KV + 8);
+        if (!cuda_ok(cudaMalloc(&B.slot_mem, bytes), "cudaMalloc(sequence slots)", err, n)) return 0;
+        if (!cuda_ok(cudaMemsetAsync(B.slot_mem, 0, bytes, E->stream), "memset", err, n)) return 0;
+        int8_t* p = (int8_t*)B.slot_mem;
+        B.slots.k = p;
+        B.slots.v = p + (size_t)QX_CUDA_MAX_SLOTS * rows * KV;
+        B.slots.ks = (float*)(p + (size_t)QX_CUDA_MAX_SLOTS * rows * 2 * KV);
+        B.slots.vs = B.slots.ks + (size_t)QX_CUDA_MAX_SLOTS * rows;
+        B.slots.slot_rows = rows;
+        B.slots.ctx = (int)C;
+    }
+    const int N = (int)nseq, H = E->dm.hidden, V = E->dm.vocab;
+    Dev& d = E->dev;
+    {
+        std::vector<int> ids(N), pos(N), sl(N);
+        for (int t = 0; t < N; ++t) ids[t] = t, pos[t] = (int)positions[t], sl[t] = (int)slots[t];
+        if (!h2d(E, B.tcols, ids.data(), (size_t)N * 4, err, n) || !h2d(E, B.tok, tokens, (size_t)N * 4, err, n) ||
+            !h2d(E, B.tpos, pos.data(), (size_t)N * 4, err, n) || !h2d(E, B.tslot, sl.data(), (size_t)N * 4, err, n))
+            return 0;
+    }
+    qx::launch_batch_embed(B.tok, d.tok_embd, H, V, N, B.x, d.err, E->stream);
+    E->prof.kernel_launches++;
+    for (int layer = 0; layer < E->dm.layers; ++layer) {
+        if (!attn_batch_run(E, layer, N, B.slots, max_pos, err, n)) return 0;
+        if (!moe_batch_run(E, (uint32_t)layer, N, err, n)) return 0;
+        std::swap(B.x, B.out);
+    }
+    // the head of every sequence: final RMSNorm, Q6_K rows on the tensor cores
+    // (double logits), greedy pick
+    int cnt = 0;
+    qx::launch_batch_norm(B.x, d.out_norm, B.xn, H, N, E->stream);
+    qx::launch_batch_limbs(B.xn, H, N, B.bqx, B.sx, E->stream);
+    if (!proj_items(E, N, V, &cnt, err, n)) return 0;
+    qx::GemmArgs ha = proj_args(E, d.head_r, H, nullptr, (size_t)V, 0);
+    ha.row_bytes = (uint32_t)qx::r8_bytes_per_row(H);
+    ha.hdr = (2 * (H / 256) + 15) / 16 * 16;
+    ha.fmt = qx::kGemmR8;
+    ha.out_d = B.logits;
+    qx::launch_moe_gemm(ha, cnt, E->stream);
+    qx::launch_batch_argmax(B.logits, V, N, B.next, d.err, E->stream);
+    E->prof.kernel_launches += 4;
+    if (!cuda_ok(cudaGetLastError(), "kernel launch", err, n)) return 0;
+    if (!d2h(E, next_tokens, B.next, (size_t)N * 4, err, n) || !finish(E, err, n)) return 0;
+    E->prof.decode_steps += nseq;
     return 1;
 }
 

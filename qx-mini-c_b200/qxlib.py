@@ -126,7 +126,7 @@ ENGINE_SYMBOLS = [
     "qx_cuda_moe_layer", "qx_cuda_attention_layer", "qx_cuda_embed", "qx_cuda_kv_write", "qx_cuda_kv_read",
     "qx_cuda_profile_get", "qx_cuda_time_kernels", "qx_cuda_phase_trace", "qx_cuda_stream",
     "qx_cuda_ep_handle", "qx_cuda_ep_connect", "qx_cuda_ep_partition", "qx_cuda_kv_export", "qx_cuda_kv_import",
-    "qx_cuda_moe_batch", "qx_cuda_prefill",
+    "qx_cuda_moe_batch", "qx_cuda_prefill", "qx_cuda_decode_batch",
 ]
 
 VERIFY_CHECKSUMS = 0x1
@@ -151,6 +151,7 @@ def cuda():
             "qx_cuda_moe_layer": [P, U32, P, P, P, P, P, E, U64],
             "qx_cuda_moe_batch": [P, U32, U32, P, P, P, P, P, E, U64],
             "qx_cuda_prefill": [P, P, U32, U32, P, P, E, U64],
+            "qx_cuda_decode_batch": [P, U32, P, P, P, P, E, U64],
             "qx_cuda_attention_layer": [P, U32, U32, P, P, P, E, U64],
             "qx_cuda_embed": [P, U32, P, E, U64],
             "qx_cuda_kv_write": [P, U32, U32, U32, P, P, P, P, E, U64],
@@ -356,6 +357,15 @@ class Engine:
         res = np.zeros(self.hidden, np.float32) if want_residual else None
         self._call("qx_cuda_prefill", _p(tokens), tokens.size, position, _p(nxt), _p(res))
         return (int(nxt[0]), res) if want_residual else int(nxt[0])
+
+    def decode_batch(self, slots, tokens, positions):
+        """One greedy step of several sequences (qx_cuda_decode_batch)."""
+        slots = np.ascontiguousarray(slots, np.uint32)
+        tokens = np.ascontiguousarray(tokens, np.uint32)
+        positions = np.ascontiguousarray(positions, np.uint32)
+        nxt = np.zeros(slots.size, np.uint32)
+        self._call("qx_cuda_decode_batch", slots.size, _p(slots), _p(tokens), _p(positions), _p(nxt))
+        return nxt
 
     def attention_layer(self, layer, position, residual):
         res = np.array(residual, np.float32, copy=True)

@@ -170,3 +170,45 @@ def test_prefill_arguments(mini_image):
             eng.prefill(np.array([1, eng.vocab], np.uint32), 0)
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("geometry", ["mini", "full4"])
+def test_decode_batch_equals_single_sequence(geometry):
+    """qx_cuda_decode_batch: several sequences, each in its own KV slot,
+    joining at different steps, must produce the same greedy tokens as the
+    single-sequence step decoding each of them alone."""
+    cfg = qxlib.mini_config(7) if geometry == "mini" else qxlib.synth_config(7, layers=4)
+    eng = qxlib.Engine(qxlib.build_image(cfg), ctx=64)
+    try:
+        starts = [42, 7, 1000, 5, 42, 3000]
+        joins = [0, 0, 0, 3, 5, 5]                # step at which each sequence starts (position 0)
+        steps = 14
+        slots = [9, 0, 63, 4, 17, 2]
+        cur = list(starts)
+        got = [[] for _ in starts]
+        for step in range(steps):
+            live = [i for i in range(len(starts)) if joins[i] <= step]
+            nxt = eng.decode_batch([slots[i] for i in live], [cur[i] for i in live],
+                                   [step - joins[i] for i in live])
+            for i, t in zip(live, nxt):
+                got[i].append(int(t))
+                cur[i] = int(t)
+        for i, s0 in enumerate(starts):
+            eng.reset()
+            want = eng.generate(s0, 0, steps - joins[i])
+            assert got[i] == list(want), "sequence %d" % i
+    finally:
+        eng.close()
+
+
+def test_decode_batch_arguments(mini_image):
+    eng = qxlib.Engine(mini_image, ctx=16)
+    try:
+        with pytest.raises(RuntimeError, match="appears twice"):
+            eng.decode_batch([1, 1], [42, 43], [0, 0])
+        with pytest.raises(RuntimeError, match="steps exceed ctx"):
+            eng.decode_batch([1], [42], [16])
+        with pytest.raises(RuntimeError, match="invalid batched decode argument"):
+            eng.decode_batch([64], [42], [0])
+    finally:
+        eng.close()
