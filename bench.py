@@ -252,7 +252,8 @@ def time_call(call, stream, reps, warmup=3):
     return float(np.median(times))
 
 
-def stage_configs(eng, cfg, stream, reps=10, which=("head", "moe", "attention", "decode4096", "batch", "prefill")):
+def stage_configs(eng, cfg, stream, reps=10,
+                  which=("head", "moe", "attention", "decode4096", "batch", "prefill", "decode_batch")):
     """BASELINE configs 1, 2, 3 (ctx 512 and 4096), 4 at ctx 4096 and 5
     (the batched grouped-expert MoE layer at 64 and 2048 tokens) through the
     engine's entry points, on one GPU.  Each entry streams its weights from
@@ -337,6 +338,25 @@ def stage_configs(eng, cfg, stream, reps=10, which=("head", "moe", "attention", 
             "frac_of_bf16_sustained": round(2 * macs / us / 1e6 / bf16, 4),
             "note": "the reference runs a prompt one token at a time (src/qx_format.c:6250-6547); the result is "
                     "bit-identical to this engine's per-token step (tests/test_gpu_batch.py)"}
+    if "decode_batch" in which and eng.ctx >= 4096:
+        nseq, first, steps = 64, 3840, 8
+        slots = np.arange(nseq, dtype=np.uint32)
+        toks = (np.arange(nseq, dtype=np.uint32) * 2371 + 42) % cfg.vocab
+
+        def run():
+            t = toks
+            for s in range(steps):
+                t = eng.decode_batch(slots, t, np.full(nseq, first + s, np.uint32))
+        us = time_call(run, stream, 2, warmup=1)
+        tok_s = nseq * steps / (us / 1e6)
+        kv_b = nseq * sum(W.kv_bytes_per_token(cfg, p) for p in range(first, first + steps)) / steps
+        out["config5_decode_batch64_ctx4096"] = {
+            "config": "64 sequences decoding together at positions 3840..3847 (each its own INT8 KV slot; the "
+                      "history is the slots' zero-filled cache, read in full), 48 layers + head",
+            "us_per_step": round(us / steps, 1), "tokens_per_s": round(tok_s, 1),
+            "kv_GB/s": round(kv_b * steps / (us / 1e6) / 1e9, 1),
+            "note": "per sequence the reference's state-loop step; tests/test_gpu_batch.py checks the tokens "
+                    "against single-sequence decode"}
     out["peak_source"] = peak_kind
     return out
 
@@ -377,7 +397,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling case only: the same model with fewer layers (default: all 48)")
     ap.add_argument("--no-stage-configs", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "head", "moe", "attention", "batch", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "head", "moe", "attention", "batch", "prefill",
+                                                            "decode_batch"],
                     help="decode = config 4 (the bench line); head/moe/attention = configs 1-3 through the "
                          "stage entry points, one JSON line each with the stage's HBM bandwidth")
     args = ap.parse_args()
