@@ -267,6 +267,7 @@ def stage_configs(eng, cfg, stream, reps=10,
     except Exception:
         bf16 = 1400.0
     H, I, E = cfg.hidden, cfg.moe_intermediate, cfg.experts
+    moe_layer = min(W.MOE_LAYER, cfg.layers - 1)
     Q, KV = cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
     rng = np.random.default_rng(3)
     out = {}
@@ -282,7 +283,7 @@ def stage_configs(eng, cfg, stream, reps=10,
             cfg.vocab * (H // 256) * 210 + 2 * H * 4, "Q6_K head 151936x2048 + final RMSNorm + argmax")
     if "moe" in which:
         x = W.moe_input(H)
-        hbm("config2_moe", time_call(lambda: eng.moe_layer(W.MOE_LAYER, x), stream, reps),
+        hbm("config2_moe", time_call(lambda: eng.moe_layer(moe_layer, x), stream, reps),
             E * H * 4 + 8 * (2 * I * (H // 256) * 74 + H * (I // 256) * 98) + H * 4,
             "one MoE layer: F32 router, top-8, IQ2_XS gate/up + SwiGLU, IQ3_XXS down")
     if "attention" in which:
@@ -313,9 +314,9 @@ def stage_configs(eng, cfg, stream, reps=10,
     if "batch" in which:
         for n in (64, 2048):
             x = np.stack([qxlib.normal_vector(1000 + t, H) for t in range(n)])
-            us = time_call(lambda: eng.moe_batch(W.MOE_LAYER, x), stream, 5)
+            us = time_call(lambda: eng.moe_batch(moe_layer, x), stream, 5)
             macs = n * 8 * (2 * I * H + H * I) + n * E * H          # experts + router
-            _, _, sel, _ = eng.moe_batch(W.MOE_LAYER, x)
+            _, _, sel, _ = eng.moe_batch(moe_layer, x)
             used = len(set(sel.ravel().tolist()))
             nbytes = used * (2 * I * (H // 256) * 74 + H * (I // 256) * 98) + E * H * 4
             out["config5_moe_batch_%d" % n] = {
@@ -366,6 +367,8 @@ def run_stage(args):
     import torch
     torch.cuda.set_device(0)
     cfg = W.model_config(full=True)
+    if args.layers:                    # profiling case: the same geometry with fewer layers
+        cfg.layers = args.layers
     img = qxlib.build_image(cfg)
     eng = qxlib.Engine(img, ctx=4096, device=0)
     stream = torch.cuda.ExternalStream(eng.stream())
