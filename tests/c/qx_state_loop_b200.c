@@ -23,10 +23,10 @@ static int qx_state_loop_b200(const char *qxf_path, const uint32_t *prompt, uint
     qx_cuda_engine *e = NULL;
     if (!qx_cuda_engine_create_from_qxf(qxf_path, &o, &e, err, err_len)) return 0;
 
-    uint32_t next = 0, pos = 0;
-    /* prompt: one step per token (the reference's prefill is per-token too) */
-    for (; pos < prompt_len; ++pos)
-        if (!qx_cuda_decode_step(e, prompt[pos], pos, &next, NULL, NULL, NULL, NULL, err, err_len)) goto fail;
+    uint32_t next = 0, pos = prompt_len;
+    /* prompt: every token at once on the tensor cores (the same result as the
+       reference's one-token-at-a-time prompt loop) */
+    if (!qx_cuda_prefill(e, prompt, prompt_len, 0, &next, NULL, err, err_len)) goto fail;
     /* greedy generation with the argmax fed back on the device */
     if (generate > 1 && !qx_cuda_generate(e, next, pos, generate - 1, out_tokens + 1, err, err_len)) goto fail;
     out_tokens[0] = next;
