@@ -433,15 +433,35 @@ struct AttnSmem {
     __align__(16) int8_t v8[1024];
 };
 
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 constexpr int kVChunk = 128;   // positions per context pass
 constexpr int kCtxSlices = 4;  // 32-dim slices of a head's context
 constexpr int kQdStride = 130; // doubles per staged query head (conflict-free rows)
 
+// Two-phase context: chunks of kRingChunk positions.  Product thread j (the
+// threads after warp 0) owns position j / 8 of every chunk, dimensions
+// 4 (j % 8) .. + 3: 60 positions x 8 quads = one quad for each of the 480
+// threads.  Each copies its own 4 V bytes and the position's scale into a
+// ring of kRing slots (cp.async groups, kRing - 1 chunks ahead), so it needs
+// no other thread's copies; slot: 480 V words, then 480 scales.  Products go
+// to kProdBufs buffers that warp 0 consumes in order.
+constexpr int kCtxChunk = 64;
+constexpr int kRingChunk = 60;
+constexpr int kRing = 5;
+constexpr int kProdBufs = 3;
+constexpr uint32_t kRingSlot = (kMT - 32) * 8;
+constexpr uint32_t kProdBytes = kProdBufs * kRingChunk * 32 * 4;
+
 // Shared-memory staging of the attention phases (the activation region, free
 // while attention runs).  Scores: RoPE row, Q/K norm vectors, this CTA's cached
-// K rows and scales.  Context: softmax weights w_s[ctx], then the item's V
-// slices (32 bytes per position) and V scales.  Rows beyond the capacity are
-// read from global memory.
+// K rows and scales (rows beyond the capacity are read from global memory).
+// Context: softmax weights w_s[ctx], then the V ring.
 struct AttnStage {
     double* rope;
     float* qn;
@@ -450,10 +470,13 @@ struct AttnStage {
     int8_t* krows;
     int kcap;
     double* w_s;
-    int8_t* vrows;
-    float* vscl;
-    int vcap;
+    uint8_t* ring;
 };
+
+// Bytes of the context staging at a given context capacity.
+__host__ __device__ constexpr uint32_t attn_ctx_bytes(int ctx) {
+    return (uint32_t)((ctx * 8 + 15) & ~15) + kRing * kRingSlot;
+}
 
 __device__ __forceinline__ int attn_cpg(const Dev& d) { return (int)gridDim.x / d.dm.kv_heads; }
 
@@ -468,11 +491,8 @@ __device__ AttnStage attn_stage(const Dev& d, int pos, uint8_t* base, uint32_t b
     st.kcap = max(0, min(krows, kfit));
     st.kscl = reinterpret_cast<float*>(base + 2048);
     st.krows = reinterpret_cast<int8_t*>(base + 2048 + ((st.kcap * 4 + 15) & ~15));
-    const uint32_t ws = (uint32_t)((d.dm.ctx * 8 + 15) & ~15);
     st.w_s = reinterpret_cast<double*>(base);
-    st.vcap = max(0, min(pos + 1, ((int)bytes - (int)ws) / 36));
-    st.vrows = reinterpret_cast<int8_t*>(base + ws);
-    st.vscl = reinterpret_cast<float*>(base + ws + st.vcap * 32);
+    st.ring = base + ((d.dm.ctx * 8 + 15) & ~15);
     return st;
 }
 
@@ -492,16 +512,18 @@ __device__ void issue_attn_scores(const Dev& d, const LayerW& w, int layer, int 
         cp_async4(st.kscl + mrow, d.kscale + (size_t)layer * ctx + r + mrow * cpg);
 }
 
-__device__ void issue_attn_context(const Dev& d, int layer, int pos, const AttnStage& st) {
-    const int D = 128, SW = D / kCtxSlices, group = d.dm.q_heads / d.dm.kv_heads;
-    const int KV = d.dm.kv_dim(), ctx = d.dm.ctx, item = blockIdx.x;
-    if (item >= d.dm.q_heads * kCtxSlices) return;
-    const int h = item / kCtxSlices, sl = item % kCtxSlices, g = h / group;
-    const int8_t* vb = d.vcache + (size_t)layer * ctx * KV + g * D + sl * SW;
-    for (int c = threadIdx.x; c < st.vcap * 2; c += kMT)
-        cp_async16(st.vrows + (c >> 1) * SW + (c & 1) * 16, vb + (size_t)(c >> 1) * KV + (c & 1) * 16);
-    for (int t = threadIdx.x; t < st.vcap; t += kMT) cp_async4(st.vscl + t, d.vscale + (size_t)layer * ctx + t);
-    (void)pos;
+// This product thread's copies of context chunk c (V slice (g, sl)) into ring
+// slot c % kRing; every product thread commits one group per call (an empty
+// one past the end), so the group counts agree.
+__device__ __forceinline__ void ring_issue(const Dev& d, int layer, int g, int sl, int T, int c, uint8_t* ring) {
+    const int j = (int)threadIdx.x - 32, t = c * kRingChunk + (j >> 3);
+    if (t < T) {
+        uint8_t* slot = ring + (c % kRing) * kRingSlot;
+        const size_t row = (size_t)layer * d.dm.ctx + t;
+        cp_async4(slot + j * 4, d.vcache + row * d.dm.kv_dim() + g * 128 + sl * 32 + (j & 7) * 4);
+        cp_async4(slot + (kMT - 32) * 4 + j * 4, d.vscale + row);
+    }
+    cp_async_commit();
 }
 
 // Context of 32 dims over positions 0..T-1: acc_d = sum_t (float)(w_t * v_t,d)
@@ -509,7 +531,25 @@ __device__ void issue_attn_context(const Dev& d, int layer, int pos, const AttnS
 // 64-position chunk are computed by warps 1.. into one half of `prod` while
 // warp 0 (lane = dim) adds the previous chunk from the other half.
 // vv(t, dd) returns the dequantized V value; prod: 2 * 64 * 32 floats.
-constexpr int kCtxChunk = 64;
+// acc + src[0] + src[32] + ... in position order (one lane = one dimension);
+// a full chunk's loads go out 20 at a time ahead of the dependent adds.
+__device__ __forceinline__ float chunk_sum(const float* src, int n, float acc) {
+    if (n == kRingChunk) {
+        float v[20];
+#pragma unroll
+        for (int q = 0; q < kRingChunk; q += 20) {
+#pragma unroll
+            for (int u = 0; u < 20; ++u) v[u] = src[(q + u) * 32];
+#pragma unroll
+            for (int u = 0; u < 20; ++u) acc += v[u];
+        }
+    } else {
+#pragma unroll 8
+        for (int tt = 0; tt < n; ++tt) acc += src[tt * 32];
+    }
+    return acc;
+}
+
 template <class VV>
 __device__ float context_chain(int T, const double* w_s, float* prod, VV vv) {
     const int SW = 32, i = threadIdx.x, nch = (T + kCtxChunk - 1) / kCtxChunk;
@@ -526,15 +566,58 @@ __device__ float context_chain(int T, const double* w_s, float* prod, VV vv) {
     __syncthreads();
     for (int c = 0; c < nch; ++c) {
         if (i < 32) {
-            const float* src = prod + (c & 1) * kCtxChunk * SW;
-            const int n = min(kCtxChunk, T - c * kCtxChunk);
-#pragma unroll 8
-            for (int tt = 0; tt < n; ++tt) acc += src[tt * SW + i];
+            acc = chunk_sum(prod + (c & 1) * kCtxChunk * SW + i, min(kCtxChunk, T - c * kCtxChunk), acc);
         } else if (c + 1 < nch) {
             products(c + 1);
         }
         __syncthreads();
     }
+    return acc;
+}
+
+// context_chain over V streamed through the ring: the same products and the
+// same position order, with warp 0 and the product threads decoupled.  The
+// product threads fill buffer c % kProdBufs with chunk c and arrive on its
+// "full" barrier; warp 0 waits there, adds the chunk and, while a later chunk
+// will reuse the buffer, arrives on its "empty" barrier, which the product
+// threads wait on first.  Arrivals and waits pair up exactly (named barriers
+// 2 .. 2 + 2 kProdBufs, all kMT threads).  The caller issued chunks
+// 0 .. kRing - 2 with ring_issue.
+__device__ float context_ring(const Dev& d, int layer, int g, int sl, int T, const double* w_s, float* prod,
+                              uint8_t* ring) {
+    static_assert(kRingChunk * 8 == kMT - 32, "one quad per product thread");
+    const int i = threadIdx.x, nch = (T + kRingChunk - 1) / kRingChunk;
+    float acc = 0.0f;
+    if (i >= 32) {
+        const int j = i - 32, tt = j >> 3, q4 = (j & 7) * 4;
+        for (int c = 0; c < nch; ++c) {
+            const int b = c % kProdBufs, t = c * kRingChunk + tt;
+            ring_issue(d, layer, g, sl, T, c + kRing - 1, ring);
+            cp_async_wait<kRing - 1>();
+            if (c >= kProdBufs) named_sync(2 + kProdBufs + b, kMT);
+            if (t < T) {
+                const uint8_t* slot = ring + (c % kRing) * kRingSlot;
+                const uint32_t raw = *reinterpret_cast<const uint32_t*>(slot + j * 4);
+                const float vs = *reinterpret_cast<const float*>(slot + (kMT - 32) * 4 + j * 4);
+                const double w = w_s[t];
+                float4 o;
+                o.x = (float)(w * (double)(i8_to_f32((int)(raw << 24) >> 24) * vs));
+                o.y = (float)(w * (double)(i8_to_f32((int)(raw << 16) >> 24) * vs));
+                o.z = (float)(w * (double)(i8_to_f32((int)(raw << 8) >> 24) * vs));
+                o.w = (float)(w * (double)(i8_to_f32((int)raw >> 24) * vs));
+                *reinterpret_cast<float4*>(prod + b * kRingChunk * 32 + tt * 32 + q4) = o;
+            }
+            named_arrive(2 + b, kMT);
+        }
+    } else {
+        for (int c = 0; c < nch; ++c) {
+            const int b = c % kProdBufs;
+            named_sync(2 + b, kMT);
+            acc = chunk_sum(prod + b * kRingChunk * 32 + i, min(kRingChunk, T - c * kRingChunk), acc);
+            if (c + kProdBufs < nch) named_arrive(2 + kProdBufs + b, kMT);
+        }
+    }
+    __syncthreads();
     return acc;
 }
 
@@ -645,7 +728,8 @@ __device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, floa
     double* w_s = st.w_s;
     for (int item = blockIdx.x; item < d.dm.q_heads * kCtxSlices; item += gridDim.x) {
         const int h = item / kCtxSlices, sl = item % kCtxSlices, g = h / group;
-        const bool staged = item == (int)blockIdx.x;
+        if (i >= 32)                       // V streams from here
+            for (int c = 0; c < kRing - 1; ++c) ring_issue(d, layer, g, sl, T, c, st.ring);
         const double* sc = d.attn_scores + (size_t)h * ctx;
         double mloc = -1.0e300;
         for (int t = i; t < T; t += kMT) {
@@ -655,10 +739,6 @@ __device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, floa
         }
         const double mx = block_max_d(mloc, S.sd);
         mark(d, epoch, 3);
-        if (staged) {                      // V slices start once the scores are in
-            issue_attn_context(d, layer, pos, st);
-            cp_async_commit();
-        }
         for (int t = i; t < T; t += kMT) w_s[t] = exp(w_s[t] - mx);
         double den = fixed_order_sum(w_s, T, S.sd);
         mark(d, epoch, 4);
@@ -666,15 +746,8 @@ __device__ void attn_context(const Dev& d, int layer, int pos, AttnSmem& S, floa
         for (int t = i; t < T; t += kMT) w_s[t] = w_s[t] / den;
         __syncthreads();
         mark(d, epoch, 5);
-        cp_async_wait<0>();
         mark(d, epoch, 0);
-        const int8_t* vb = d.vcache + (size_t)layer * ctx * KV + g * D + sl * SW;
-        const float* vs = d.vscale + (size_t)layer * ctx;
-        const int vcap = staged ? st.vcap : 0;
-        __syncthreads();
-        const float acc = context_chain(T, w_s, prod, [&](int t, int dd) {
-            return t < vcap ? i8_to_f32(st.vrows[t * SW + dd]) * st.vscl[t] : i8_to_f32(vb[(size_t)t * KV + dd]) * vs[t];
-        });
+        const float acc = context_ring(d, layer, g, sl, T, w_s, prod, st.ring);
         if (i < SW) d.ctxv[h * D + sl * SW + i] = acc;
         mark(d, epoch, 1);
         __syncthreads();
@@ -859,10 +932,6 @@ __device__ void attn_fused(const Dev& d, int layer, int pos, AttnSmem& S, const 
 // equal upper halves share a rank, which leaves one of the eight slots empty
 // or doubly filled, and then the exact 64-bit (key, index) ranking runs.  A
 // NaN makes the weight sum NaN, reported as an error in top8_weights.
-__device__ __forceinline__ void named_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 __device__ void top8_select(const Dev& d, int* sel, double* wsel, long long* keys, double* red, int* cnt) {
     const int E = d.dm.experts, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int sw = (E + 31) >> 5, st = sw * 32;       // softmax warps / threads
@@ -1345,8 +1414,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
 // Used by the stage entry point and the per-stage decode path, so both share
 // the one-launch kernel's attention arithmetic.  Shared memory: the staging
 // region (kAttnStageBytes) followed by the query / product scratch.
-constexpr uint32_t kAttnStageBytes = 200 * 1024;   // ctx 4096: 32 KB of weights + 36 B per staged position
-constexpr uint32_t kAttnScratchBytes = kVChunk * 132 > 16 * kQdStride * 8 ? kVChunk * 132 : 16 * kQdStride * 8;
+constexpr uint32_t kAttnStageBytes = 192 * 1024;   // scores: K rows; context: 8 B per position + the V ring
+constexpr uint32_t kAttnScratchBytes =
+    std::max<uint32_t>(std::max<uint32_t>(kVChunk * 132, kProdBytes), 16 * kQdStride * 8);
 
 __global__ void __launch_bounds__(kMT, 1) k_attn_scores(Dev d, LayerW w, int layer) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -1408,8 +1478,8 @@ static MegaLayout mega_layout(const Dims& m, int grid) {
     const int XS = std::max(std::max(H, Q), 8 * I);
     MegaLayout L{};
     uint32_t off = 0;
-    L.xs = off; off += a16u(std::max((size_t)XS * 4, (size_t)kVChunk * 132));
-    L.xb = off; off += a16u(xq_words(XS) * 4);
+    L.xs = off; off += a16u(std::max({(size_t)XS * 4, (size_t)kVChunk * 132, (size_t)kProdBytes}));
+    L.xb = off; off += a16u(std::max(xq_words(XS) * 4, (size_t)attn_ctx_bytes(m.ctx)));   // also the attention staging
     L.sb = off; off += a16u((size_t)XS / 256 * 4 + 32);
     L.tab = off; off += a16u(sizeof(IqTab));
     L.part = off; off += a16u((size_t)mega_max_tasks(m, grid) * kTileRows * 8);
@@ -1434,7 +1504,7 @@ int mega_setup(int device, const Dims& m, int* grid_out) {
     if (m.vocab % 32) return 0;               // head rows in groups of 32 (the expert-parallel unit)
     const MegaLayout L = mega_layout(m, sms);
     if (L.total + a.sharedSizeBytes > (size_t)optin || !mega_tasks_fit(m, sms)) return 0;
-    if ((size_t)m.ctx * 8 > L.sb - L.xb || (size_t)kVChunk * 132 > L.xb - L.xs) return 0;
+    if (attn_ctx_bytes(m.ctx) > L.sb - L.xb || std::max((size_t)kVChunk * 132, (size_t)kProdBytes) > L.xb - L.xs) return 0;
     const int group = m.q_heads / m.kv_heads;
     if (kMT % group || group * 128 > 8 * kMT || (size_t)group * kQdStride * 8 > L.xb - L.xs || sms < m.kv_heads ||
         m.kv_heads > 8)
@@ -1650,7 +1720,8 @@ namespace qx {
 // whole context fit the staging region and the query heads fit the scratch.
 bool attn2_supported(const Dims& m) {
     const int group = m.q_heads / m.kv_heads;
-    return (size_t)m.ctx * 8 + 2048 <= kAttnStageBytes && kMT % group == 0 && group * 128 <= 8 * kMT &&
+    return (size_t)m.ctx * 8 + 2048 <= kAttnStageBytes && attn_ctx_bytes(m.ctx) <= kAttnStageBytes &&
+           kMT % group == 0 && group * 128 <= 8 * kMT &&
            (size_t)group * kQdStride * 8 <= kAttnScratchBytes;
 }
 
