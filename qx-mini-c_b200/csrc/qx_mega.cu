@@ -621,6 +621,39 @@ __device__ float context_ring(const Dev& d, int layer, int g, int sl, int T, con
     return acc;
 }
 
+// score_row of one key row against the G query heads of its KV group (rows
+// kQdStride doubles apart), stored to out[h * stride]: each head's sum in
+// dimension order exactly as score_row adds it; the key values are widened
+// once for all G heads.
+template <int G>
+__device__ __forceinline__ void score_rows_group(const double* qd, const int8_t* kp, float ks, double sqrt_d,
+                                                 double* out, int stride) {
+    double s[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) s[h] = 0.0;
+#pragma unroll 1
+    for (int j = 0; j < 128; j += 8) {
+        const int2 raw = *reinterpret_cast<const int2*>(kp + j);
+        const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
+        double kd[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) kd[u] = (double)(i8_to_f32(kb[u]) * ks);
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+#pragma unroll
+            for (int u = 0; u < 8; u += 2) {
+                const double2 q = *reinterpret_cast<const double2*>(qd + h * kQdStride + j + u);
+                s[h] = fma(q.x, kd[u], s[h]);
+                s[h] = fma(q.y, kd[u + 1], s[h]);
+            }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        const double v = s[h] / sqrt_d;
+        out[(size_t)h * stride] = isfinite(v) ? v : 0.0;
+    }
+}
+
 // Scores.  The CTAs form kv_heads groups of G/kv_heads; group g serves the
 // query heads of KV head g, CTA r of the group positions r, r + cpg, ...;
 // thread i scores query head i % group at one of those positions.  Every CTA
@@ -701,6 +734,25 @@ __device__ void attn_scores(const Dev& d, const LayerW& w, int layer, int pos, A
     mark(d, epoch, 1);
     const int T = pos + 1, per = kMT / group, hj = i % group;
     const double sqrt_d = sqrt((double)D);
+    auto key_row = [&](int mrow, int t, const int8_t*& kp, float& ks) {
+        const size_t stt = (size_t)layer * ctx + t;
+        kp = t == pos ? S.k8 + g * D : mrow < st.kcap ? st.krows + mrow * 128 : d.kcache + stt * KV + g * D;
+        ks = t == pos ? ksc : mrow < st.kcap ? st.kscl[mrow] : d.kscale[stt];
+    };
+    if (group % 2 == 0) {                 // thread: one position, two heads (the key widened once for both)
+        const int sub = group / 2, h0 = 2 * (i % sub);
+        double* out = d.attn_scores + (size_t)(g * group + h0) * ctx;
+        for (int mrow = i / sub; r + mrow * cpg < T; mrow += kMT / sub) {
+            const int t = r + mrow * cpg;
+            const int8_t* kp;
+            float ks;
+            key_row(mrow, t, kp, ks);
+            score_rows_group<2>(qd + h0 * kQdStride, kp, ks, sqrt_d, out + t, ctx);
+        }
+        __syncthreads();
+        mark(d, epoch, 2);
+        return;
+    }
     const double* q = qd + hj * kQdStride;
     double* out = d.attn_scores + (size_t)(g * group + hj) * ctx;
     for (int mrow = i / group; r + mrow * cpg < T; mrow += per) {
