@@ -407,9 +407,7 @@ __global__ void __launch_bounds__(256) k_batch_norm(const float* x, const float*
     __shared__ double scratch[8];
     const float* xt = x + (size_t)blockIdx.x * H;
     float* yt = xn + (size_t)blockIdx.x * H;
-    double ss = 0.0;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += (double)xt[i] * (double)xt[i];
-    ss = block_sum_d(ss, scratch);
+    const double ss = sum_sq_fixed(xt, H, scratch);
     const double rms = sqrt(ss / (double)H + 1.0e-6);
     for (int i = threadIdx.x; i < H; i += blockDim.x) yt[i] = (float)((double)xt[i] / rms) * w[i];
 }
@@ -521,8 +519,8 @@ __global__ void __launch_bounds__(256) k_batch_router(const float* xn, const flo
     __syncwarp();
     double ws[8];
     int picked = 0;   // bit q: expert lane + 32 q is taken
-#pragma unroll
     double sum = 0.0;
+#pragma unroll
     for (int k = 0; k < 8; ++k) {
         double bv = -1.0;
         int bi = 0x7fffffff;

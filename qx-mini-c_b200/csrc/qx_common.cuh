@@ -15,15 +15,10 @@ namespace qx {
 // xs[i] = (float)((double)x[i] / rms) * w[i], rms = sqrt(sum x^2 / n + 1e-6)
 // in double (qx_apply_f32_rmsnorm, src/qx_format.c:3358-3371).
 __device__ inline void rmsnorm_to_smem(const float* x, const float* w, float* xs, int n, double* scratch) {
-    double ss = 0.0;
-    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(x + i);
-        *reinterpret_cast<float4*>(xs + i) = v;
-        ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y;
-        ss += (double)v.z * (double)v.z + (double)v.w * (double)v.w;
-    }
-    ss = block_sum_d(ss, scratch);
-    const double rms = sqrt(ss / (double)n + 1.0e-6);
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
+    __syncthreads();
+    const double rms = sqrt(sum_sq_fixed(xs, n, scratch) / (double)n + 1.0e-6);
     for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
         const float4 wv = *reinterpret_cast<const float4*>(w + i);
         float4 v = *reinterpret_cast<float4*>(xs + i);

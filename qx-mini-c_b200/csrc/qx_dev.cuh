@@ -82,6 +82,23 @@ __device__ __forceinline__ double block_sum_d(double v, double* scratch) {
     return t;
 }
 
+// Sum of x[i]^2 over n floats (n % 4 == 0, 16-byte aligned) in the one order
+// every RMSNorm of this library uses, whatever its block size (>= 256):
+// thread i < 256 adds the float4 groups i, i + 256, ... as (a^2 + b^2) then
+// (c^2 + d^2), then block_sum_d adds the warp sums in warp order; threads
+// beyond 256 add 0.0, which changes no sum.  (Each square is exact in double;
+// only the additions round, so every path that uses this rounds alike.)
+__device__ __forceinline__ double sum_sq_fixed(const float* x, int n, double* scratch) {
+    double ss = 0.0;
+    if (threadIdx.x < 256)
+        for (int i = threadIdx.x * 4; i < n; i += 256 * 4) {
+            const float4 v = *reinterpret_cast<const float4*>(x + i);
+            ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y;
+            ss += (double)v.z * (double)v.z + (double)v.w * (double)v.w;
+        }
+    return block_sum_d(ss, scratch);
+}
+
 // ---- asynchronous copies into shared memory ------------------------------
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);

@@ -1175,9 +1175,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             }
             // attention RMSNorm of xs in place
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
-            double ss = 0.0;
-            for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
-            ss = block_sum_d(ss, scratch);
+            const double ss = sum_sq_fixed(xs, H, scratch);
             const double rms = sqrt(ss / (double)H + 1.0e-6), rinv = 1.0 / rms;
             if (isfinite(rms))
                 for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)div_by((double)xs[i], rms, rinv) * nw[i];
@@ -1246,9 +1244,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             group_wait(G, kGRouter, d);          // router rows and norm vector
             copy_to_smem(d.x, xs, H);
             const float* nw = reinterpret_cast<const float*>(buf[qb] + L.norm);
-            double ss = 0.0;
-            for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
-            ss = block_sum_d(ss, scratch);
+            const double ss = sum_sq_fixed(xs, H, scratch);
             const double rms = sqrt(ss / (double)H + 1.0e-6), rinv = 1.0 / rms;
             if (isfinite(rms))
                 for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)div_by((double)xs[i], rms, rinv) * nw[i];
@@ -1374,9 +1370,7 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
         } else {
             copy_to_smem(d.x, xs, H);
         }
-        double ss = 0.0;
-        for (int i = threadIdx.x; i < H; i += kMT) ss += (double)xs[i] * (double)xs[i];
-        ss = block_sum_d(ss, scratch);
+        const double ss = sum_sq_fixed(xs, H, scratch);
         const double rms = sqrt(ss / (double)H + 1.0e-6), rinv = 1.0 / rms;
         if (isfinite(rms))
             for (int i = threadIdx.x; i < H; i += kMT) xs[i] = (float)div_by((double)xs[i], rms, rinv) * d.out_norm[i];

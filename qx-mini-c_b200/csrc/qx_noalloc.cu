@@ -70,13 +70,9 @@ __global__ void __launch_bounds__(kThreads) k_head_noalloc(const float* x, const
         cp_async_commit();
     }
     // RMSNorm in double (qx_apply_f32_rmsnorm, src/qx_format.c:3358-3371)
-    double ss = 0.0;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-        const float v = x[i];
-        xs[i] = v;
-        ss += (double)v * (double)v;
-    }
-    ss = block_sum_d(ss, scratch);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[i];
+    __syncthreads();
+    const double ss = sum_sq_fixed(xs, H, scratch);
     const double rms = sqrt(ss / (double)H + 1.0e-6);
     for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = (float)((double)xs[i] / rms) * nw[i];
     __syncthreads();
