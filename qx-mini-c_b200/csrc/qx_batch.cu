@@ -681,6 +681,146 @@ __global__ void __launch_bounds__(128) k_batch_attn(const float* qn, KvView kv, 
     ctx_out[(size_t)t * Q + h * D + i] = acc;
 }
 
+// vd[r][j] = (double)((float)v[r][j] * vs[r]) for rows r < rows: the widened
+// value every context product of row r uses (the same expression).
+__global__ void k_widen_v(const int8_t* v, const float* vs, int rows, int KV, double* vd) {
+    const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < (size_t)rows * KV) vd[e] = (double)(i8_to_f32(v[e]) * vs[e / KV]);
+}
+
+// k_batch_attn for all G query heads of one KV group at once: CTA = (token,
+// KV group), 256 threads.  Every scalar operation and its order are those of
+// the per-token step (score_row's dimension-order FMA chain, fmax, exp,
+// fixed_order_sum's lane-strided denominator, one division, the position-order
+// float context sum), so the results are bit-identical; what changes is that
+// a key or value is widened to double once for all the heads that use it.
+// Scores: thread -> positions i, i + 512, ... for all G heads; softmax: warp h
+// forms head h's denominator; context: thread -> dimension i % 128 for heads
+// (i / 128) * G/4 .. + G/4 - 1.  w_s: [T][G] doubles (dynamic shared memory).
+// Tokens t0 + blockIdx.x.  vd (optional, slot 0 only): the layer's V rows
+// already widened, vd[p][j] = (double)((float)v * vscale) (k_widen_v), read
+// in place of the INT8 rows.
+template <int G>
+__global__ void __launch_bounds__(512, 2) k_batch_attn_grp(const float* qn, KvView kv, int layer, const int* tpos,
+                                                        const int* tslot, int QH, int KVH, float* ctx_out, int t0,
+                                                        const double* vd) {
+    constexpr int D = 128, NT = 512, HH = G / 4;
+    extern __shared__ __align__(16) double w_s[];
+    __shared__ __align__(16) double qd[G * D];
+    __shared__ double red[NT / 32][G];
+    __shared__ double hv[2][G];
+    const int t = t0 + blockIdx.x, g = blockIdx.y, i = threadIdx.x, warp = i >> 5, lane = i & 31;
+    const int Q = QH * D, KV = KVH * D, T = tpos[t] + 1, ctx = kv.ctx;
+    const size_t srow = (size_t)tslot[t] * kv.slot_rows;
+    const int8_t* kcache = kv.k + srow * KV;
+    const int8_t* vcache = kv.v + srow * KV;
+    const float* kscale = kv.ks + srow;
+    const float* vscale = kv.vs + srow;
+    for (int j = i; j < G * D; j += NT) qd[j] = (double)qn[(size_t)t * Q + (size_t)g * G * D + j];
+    __syncthreads();
+    const double sqrt_d = sqrt((double)D);
+    double mloc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) mloc[h] = -1.0e300;
+    for (int p = i; p < T; p += NT) {
+        const size_t st = (size_t)layer * ctx + p;
+        const int8_t* kp = kcache + st * KV + g * D;
+        const float ks = kscale[st];
+        double s[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) s[h] = 0.0;
+#pragma unroll 1
+        for (int j = 0; j < D; j += 8) {
+            const int2 raw = *reinterpret_cast<const int2*>(kp + j);
+            const int8_t* kb = reinterpret_cast<const int8_t*>(&raw);
+            double kd[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) kd[u] = (double)(i8_to_f32(kb[u]) * ks);
+#pragma unroll
+            for (int h = 0; h < G; ++h)
+#pragma unroll
+                for (int u = 0; u < 8; ++u) s[h] = fma(qd[h * D + j + u], kd[u], s[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            double v = s[h] / sqrt_d;
+            v = isfinite(v) ? v : 0.0;
+            w_s[p * G + h] = v;
+            mloc[h] = fmax(mloc[h], v);
+        }
+    }
+    // per-head maxima (fmax: the order does not matter)
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        double m = mloc[h];
+        for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) red[warp][h] = m;
+    }
+    __syncthreads();
+    if (i < G) {
+        double m = red[0][i];
+        for (int k = 1; k < NT / 32; ++k) m = fmax(m, red[k][i]);
+        hv[0][i] = m;
+    }
+    __syncthreads();
+    for (int e = i; e < T * G; e += NT) w_s[e] = exp(w_s[e] - hv[0][e % G]);
+    __syncthreads();
+    if (warp < G) {                       // head `warp`: fixed_order_sum's order
+        double sum = 0.0;
+        for (int p = lane; p < T; p += 32) sum += w_s[p * G + warp];
+        sum = warp_sum_d(sum);
+        if (lane == 0) hv[1][warp] = (!isfinite(sum) || sum <= 0.0) ? 1.0 : sum;
+    }
+    __syncthreads();
+    for (int e = i; e < T * G; e += NT) w_s[e] = w_s[e] / hv[1][e % G];
+    __syncthreads();
+    const int d = i & (D - 1), h0 = (i >> 7) * HH;
+    const int8_t* vb = vcache + (size_t)layer * ctx * KV + g * D + d;
+    const float* vs = vscale + (size_t)layer * ctx;
+    float acc[HH];
+#pragma unroll
+    for (int k = 0; k < HH; ++k) acc[k] = 0.0f;
+    constexpr int U = 16;                 // positions whose loads go out together
+    int p = 0;
+    if (vd) {
+        const double* vp = vd + g * D + d;
+        for (; p + U <= T; p += U) {
+            double vv[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) vv[u] = vp[(size_t)(p + u) * KV];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int k = 0; k < HH; ++k) acc[k] += (float)(w_s[(p + u) * G + h0 + k] * vv[u]);
+        }
+        for (; p < T; ++p)
+#pragma unroll
+            for (int k = 0; k < HH; ++k) acc[k] += (float)(w_s[p * G + h0 + k] * vp[(size_t)p * KV]);
+    }
+    for (; p + U <= T; p += U) {
+        int8_t vq[U];
+        float vsc[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            vq[u] = vb[(size_t)(p + u) * KV];
+            vsc[u] = vs[p + u];
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const double vd = (double)(i8_to_f32(vq[u]) * vsc[u]);
+#pragma unroll
+            for (int k = 0; k < HH; ++k) acc[k] += (float)(w_s[(p + u) * G + h0 + k] * vd);
+        }
+    }
+    for (; p < T; ++p) {
+        const double vd = (double)(i8_to_f32(vb[(size_t)p * KV]) * vs[p]);
+#pragma unroll
+        for (int k = 0; k < HH; ++k) acc[k] += (float)(w_s[p * G + h0 + k] * vd);
+    }
+#pragma unroll
+    for (int k = 0; k < HH; ++k) ctx_out[(size_t)t * Q + (size_t)(g * G + h0 + k) * D + d] = acc[k];
+}
+
 // Greedy pick per token over double logits [ntok][V]: the largest, lowest
 // index on ties (src/qx_format.c:3723-3730); a non-finite logit is an error
 // (:3715).
@@ -719,6 +859,11 @@ __global__ void k_batch_add(float* x, const float* y, size_t n) {
 
 }  // namespace
 
+// Dynamic shared memory the grouped attention kernel may use (set once by
+// moe_batch_configure; 0 until then, which selects the per-head kernel).
+size_t g_attn_grp_smem = 0;
+constexpr int kAttnBucket = 256;
+
 void launch_batch_embed(const uint32_t* tokens, const uint8_t* emb, int H, int V, int ntok, float* x, int* err,
                         cudaStream_t st) {
     k_batch_embed<<<ntok, 256, 0, st>>>(tokens, emb, H, V, x, err);
@@ -731,7 +876,31 @@ void launch_batch_qkv_post(const float* qkv, const float* q_norm, const float* k
 }
 
 void launch_batch_attn(const float* qn, const KvView& kv, int layer, const int* tpos, const int* tslot, int max_pos,
-                       int ntok, int QH, int KVH, float* ctx_out, cudaStream_t st) {
+                       int ntok, int QH, int KVH, float* ctx_out, cudaStream_t st, int first_pos, double* vd) {
+    const int G = QH / KVH;
+    if ((G == 8 || G == 4) && (size_t)(max_pos + 1) * G * 8 <= g_attn_grp_smem) {   // CTA per (token, KV group)
+        // consecutive positions (a prompt): buckets of kAttnBucket tokens, each
+        // with the shared memory of its own longest context
+        const int bucket = first_pos >= 0 ? kAttnBucket : ntok;
+        const double* vdp = nullptr;
+        if (first_pos >= 0 && vd) {      // a prompt in slot 0: widen rows 0..max_pos once
+            const int KV = KVH * 128;
+            const size_t n = (size_t)(max_pos + 1) * KV;
+            k_widen_v<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(kv.v + (size_t)layer * kv.ctx * KV,
+                                                                  kv.vs + (size_t)layer * kv.ctx, max_pos + 1, KV, vd);
+            vdp = vd;
+        }
+        for (int b0 = 0; b0 < ntok; b0 += bucket) {
+            const int n = std::min(bucket, ntok - b0);
+            const int mp = first_pos >= 0 ? first_pos + b0 + n - 1 : max_pos;
+            const size_t sm = (size_t)(mp + 1) * G * 8;
+            if (G == 8)
+                k_batch_attn_grp<8><<<dim3(n, KVH), 512, sm, st>>>(qn, kv, layer, tpos, tslot, QH, KVH, ctx_out, b0, vdp);
+            else
+                k_batch_attn_grp<4><<<dim3(n, KVH), 512, sm, st>>>(qn, kv, layer, tpos, tslot, QH, KVH, ctx_out, b0, vdp);
+        }
+        return;
+    }
     const size_t smem = (size_t)(max_pos + 1) * 8;
     k_batch_attn<<<dim3(ntok, QH), 128, smem, st>>>(qn, kv, layer, tpos, tslot, QH, KVH, ctx_out);
 }
@@ -757,6 +926,11 @@ cudaError_t moe_batch_configure() {
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k_batch_router, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k_batch_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 2048);
+    // the grouped kernel: its static arrays (query heads, reductions) take < 10 KB
+    const int grp = optin - 10 * 1024;
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_batch_attn_grp<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, grp);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_batch_attn_grp<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, grp);
+    if (e == cudaSuccess) g_attn_grp_smem = (size_t)grp;
     return e;
 }
 

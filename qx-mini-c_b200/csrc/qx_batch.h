@@ -60,8 +60,13 @@ void launch_batch_embed(const uint32_t* tokens, const uint8_t* emb, int H, int V
 void launch_batch_qkv_post(const float* qkv, const float* q_norm, const float* k_norm, const double* rope, int layer,
                            const int* tpos, const int* tslot, const KvView& kv, int ntok, int QH, int KVH, float* qn,
                            cudaStream_t st);
+// first_pos >= 0: token t is at position first_pos + t of KV slot 0 (a
+// prompt), which lets the launch size each bucket of tokens for its own
+// context length and, given vd ([max_pos + 1][kv_dim] doubles of scratch),
+// widen the layer's V rows once for every head.
 void launch_batch_attn(const float* qn, const KvView& kv, int layer, const int* tpos, const int* tslot, int max_pos,
-                       int ntok, int QH, int KVH, float* ctx_out, cudaStream_t st);
+                       int ntok, int QH, int KVH, float* ctx_out, cudaStream_t st, int first_pos = -1,
+                       double* vd = nullptr);
 void launch_batch_argmax(const double* logits, int V, int ntok, uint32_t* out, int* err, cudaStream_t st);
 void launch_batch_add(float* x, const float* y, size_t n, cudaStream_t st);
 void launch_batch_combine(const float* x, const float* y, const double* wsel, int H, int ntok, float* moe, float* out,

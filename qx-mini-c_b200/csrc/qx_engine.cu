@@ -87,6 +87,7 @@ struct qx_cuda_engine {
         uint32_t *tok, *next;
         double* logits;                  // [cap][vocab] (batched decode's head)
         double* wsel;
+        double* vd;                      // [ctx][kv_dim] widened V rows of a prompt's layer
         qx::GemmItem* items;
         size_t item_cap;
         // sequence slots of qx_cuda_decode_batch: their own INT8 KV caches
@@ -848,7 +849,7 @@ bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
         {(void**)&B.qkv, ntok * (Q + 2 * KV) * 4}, {(void**)&B.qn, ntok * Q * 4}, {(void**)&B.ctxo, ntok * Q * 4},
         {(void**)&B.ao, ntok * H * 4}, {(void**)&B.tcols, ntok * 4}, {(void**)&B.tok, ntok * 4},
         {(void**)&B.tpos, ntok * 4}, {(void**)&B.tslot, ntok * 4}, {(void**)&B.next, ntok * 4},
-        {(void**)&B.logits, nhead * V * 8}};
+        {(void**)&B.logits, nhead * V * 8}, {(void**)&B.vd, (size_t)E->dm.ctx * KV * 8}};
     for (auto& p : parts) off = align_up(off + p.second, 256);
     if (!cuda_ok(cudaMalloc(&B.mem, off), "cudaMalloc(batch)", err, n)) return false;
     off = 0;
@@ -1041,7 +1042,8 @@ namespace {
 // KV slots B.tslot of `kv`): attention RMSNorm, Q/K/V on the tensor cores,
 // head norms + RoPE + the K/V rows into the cache, causal attention, O
 // projection, residual add.  Leaves the stream running.
-bool attn_batch_run(qx_cuda_engine* E, int layer, int N, const qx::KvView& kv, int max_pos, char* err, uint64_t n) {
+bool attn_batch_run(qx_cuda_engine* E, int layer, int N, const qx::KvView& kv, int max_pos, int first_pos, char* err,
+                    uint64_t n) {
     auto& B = E->batch;
     const LayerW& w = E->layers[layer];
     const int H = E->dm.hidden, Q = E->dm.q_dim(), KV = E->dm.kv_dim(), QH = E->dm.q_heads, KVH = E->dm.kv_heads;
@@ -1055,7 +1057,7 @@ bool attn_batch_run(qx_cuda_engine* E, int layer, int N, const qx::KvView& kv, i
     qx::launch_moe_gemm(proj_args(E, w.wv_r, H, B.qkv, (size_t)(Q + 2 * KV), Q + KV), cnt, E->stream);
     qx::launch_batch_qkv_post(B.qkv, w.q_norm, w.k_norm, E->dev.rope, layer, B.tpos, B.tslot, kv, N, QH, KVH, B.qn,
                               E->stream);
-    qx::launch_batch_attn(B.qn, kv, layer, B.tpos, B.tslot, max_pos, N, QH, KVH, B.ctxo, E->stream);
+    qx::launch_batch_attn(B.qn, kv, layer, B.tpos, B.tslot, max_pos, N, QH, KVH, B.ctxo, E->stream, first_pos, B.vd);
     qx::launch_batch_limbs(B.ctxo, Q, N, B.bqx, B.sx, E->stream);
     if (!proj_items(E, N, H, &cnt, err, n)) return false;
     qx::launch_moe_gemm(proj_args(E, w.wo_r, Q, B.ao, (size_t)H, 0), cnt, E->stream);
@@ -1098,7 +1100,7 @@ QX_API int qx_cuda_prefill(qx_cuda_engine* E, const uint32_t* tokens, uint32_t n
     qx::launch_batch_embed(B.tok, d.tok_embd, H, E->dm.vocab, N, B.x, d.err, E->stream);
     E->prof.kernel_launches++;
     for (int layer = 0; layer < E->dm.layers; ++layer) {
-        if (!attn_batch_run(E, layer, N, kv, (int)position + N - 1, err, n)) return 0;
+        if (!attn_batch_run(E, layer, N, kv, (int)position + N - 1, (int)position, err, n)) return 0;
         // the MoE FFN, then its output is the next layer's residual
         if (!moe_batch_run(E, (uint32_t)layer, N, err, n)) return 0;
         std::swap(B.x, B.out);
@@ -1168,7 +1170,7 @@ QX_API int qx_cuda_decode_batch(qx_cuda_engine* E, uint32_t nseq, const uint32_t
     qx::launch_batch_embed(B.tok, d.tok_embd, H, V, N, B.x, d.err, E->stream);
     E->prof.kernel_launches++;
     for (int layer = 0; layer < E->dm.layers; ++layer) {
-        if (!attn_batch_run(E, layer, N, B.slots, max_pos, err, n)) return 0;
+        if (!attn_batch_run(E, layer, N, B.slots, max_pos, -1, err, n)) return 0;
         if (!moe_batch_run(E, (uint32_t)layer, N, err, n)) return 0;
         std::swap(B.x, B.out);
     }
