@@ -98,3 +98,66 @@ def test_create_rejects_bad_expert_parallel_options_before_touching_a_device(min
     ok = qxlib.cuda().qx_cuda_engine_create_from_image(mini_image.ctypes.data, mini_image.nbytes, C.byref(opt),
                                                        C.byref(h), err, len(err))
     assert ok == 0 and err.value == b"nccl_comm is reserved and must be NULL"
+
+
+# ---- the split MoE combine -----------------------------------------------------
+# The expert-parallel step splits the 8 selected experts of a layer by owner:
+# rank r computes the term (float)(w_k * (double)y_k) of every slot k whose
+# expert it owns (rows of the down projection y_k, double weights w_k), writes
+# it into slot k of every rank's exchange table, and each rank then adds the 8
+# slots of a row in rank order in float, as the one-GPU step does
+# (src/qx_format.c:5287-5303).  Slot k is written by exactly one rank, so the
+# sum is the one-GPU sum bit for bit.
+
+H_C = 64
+
+
+def _combine_inputs(seed):
+    rng = np.random.default_rng(seed)
+    sel = rng.choice(E, 8, replace=False)                    # rank order of the top-8
+    w = rng.random(8) + 0.01
+    w = w / w.sum()                                          # renormalised double weights
+    y = rng.standard_normal((8, H_C)).astype(np.float32)     # expert outputs (down rows)
+    x = rng.standard_normal(H_C).astype(np.float32)          # residual
+    return sel, w, y, x
+
+
+def _one_gpu_combine(sel, w, y, x):
+    moe = np.zeros(H_C, np.float32)
+    for k in range(8):
+        moe = (moe + (w[k] * y[k].astype(np.float64)).astype(np.float32)).astype(np.float32)
+    return (x + moe).astype(np.float32)
+
+
+def _combine_main(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        e0, e1, _, _ = qxlib.ep_partition(E, V, world, rank)
+        for seed in range(20):
+            sel, w, y, x = _combine_inputs(seed)
+            table = np.zeros((8, H_C), np.float32)           # this rank's contribution to the exchange
+            for k in range(8):
+                if e0 <= sel[k] < e1:
+                    table[k] = (w[k] * y[k].astype(np.float64)).astype(np.float32)
+            got = [None] * world
+            dist.all_gather_object(got, table)
+            owners = np.array([[np.any(t[k] != 0) for k in range(8)] for t in got])
+            slots = np.sum(got, axis=0, dtype=np.float64).astype(np.float32)   # one writer per slot: exact
+            moe = np.zeros(H_C, np.float32)
+            for k in range(8):
+                moe = (moe + slots[k]).astype(np.float32)
+            np.save(os.path.join(out_dir, "c%d_%d.npy" % (rank, seed)), (x + moe).astype(np.float32))
+            np.save(os.path.join(out_dir, "o%d_%d.npy" % (rank, seed)), owners.sum(axis=0))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_split_moe_combine_equals_the_one_gpu_combine(tmp_path, world):
+    mp.spawn(_combine_main, args=(world, free_port(), str(tmp_path)), nprocs=world, join=True)
+    for seed in range(20):
+        want = _one_gpu_combine(*_combine_inputs(seed))
+        for r in range(world):
+            np.testing.assert_array_equal(np.load(tmp_path / ("c%d_%d.npy" % (r, seed))), want)
+            assert list(np.load(tmp_path / ("o%d_%d.npy" % (r, seed)))) == [1] * 8   # one writer per slot
