@@ -119,7 +119,7 @@ constexpr int kEpMaxRanks = 8;
 __host__ __device__ inline size_t ep_terms_bytes(int hidden) { return (size_t)2 * 8 * hidden * 4; }
 __host__ __device__ inline size_t ep_xchg_bytes(int hidden) { return ep_terms_bytes(hidden) + 4096; }
 struct EpTail {                  // at offset ep_terms_bytes(H)
-    unsigned layer_flag[kEpMaxRanks];
+    unsigned layer_cnt[kEpMaxRanks];     // per source rank: its CTAs' releases of MoE terms
     unsigned head_flag[kEpMaxRanks];
     double best_val[kEpMaxRanks];
     int best_idx[kEpMaxRanks];

@@ -373,6 +373,9 @@ __device__ __forceinline__ EpTail* ep_tail(uint8_t* base, int H) {
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -407,10 +410,14 @@ __device__ void ep_combine(const Dev& d, int prev_layer, float* xs) {
     __syncthreads();
 }
 
-// CTA-wide: wait for every rank's MoE terms of `prev_layer`.
+// CTA-wide: wait for every rank's MoE terms of `prev_layer`: every CTA of
+// every rank adds 1 to this rank's layer_cnt[rank] per layer, so after layer
+// L of step s the count is (s * layers + L + 1) * grid.
 __device__ void ep_wait_layer(const Dev& d, unsigned seqb, int prev_layer) {
-    if (threadIdx.x == 0)
-        ep_wait_flags(ep_tail(d.ep_local, d.dm.hidden)->layer_flag, d.ep_world, seqb + prev_layer + 1, d.err);
+    if (threadIdx.x == 0) {
+        const unsigned want = ((seqb / 64u) * (unsigned)d.dm.layers + (unsigned)prev_layer + 1u) * gridDim.x;
+        ep_wait_flags(ep_tail(d.ep_local, d.dm.hidden)->layer_cnt, d.ep_world, want, d.err);
+    }
     __syncthreads();
 }
 
@@ -1327,16 +1334,26 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
             // the weighted terms (float)(w_j * y_j) of every (row, slot) in
             // parallel (xs is free again), then per row in rank order
             float* terms = xs;
-            for (int u = threadIdx.x; u < mine * kTileRows * n_own; u += kMT) {
-                const int r = u / n_own, j = u % n_own;
-                const float term = (float)(wsel[own[j]] *
-                                           (double)finite_or_zero_d(tile_row(part, n_own * (r / kTileRows) + j, nblk, r % kTileRows)));
-                if (!ep) {
-                    terms[u] = term;
-                } else {                         // this rank's slots into every rank's exchange buffer
+            auto term_of = [&](int r, int j) {
+                return (float)(wsel[own[j]] *
+                               (double)finite_or_zero_d(tile_row(part, n_own * (r / kTileRows) + j, nblk, r % kTileRows)));
+            };
+            if (!ep) {
+                for (int u = threadIdx.x; u < mine * kTileRows * n_own; u += kMT) terms[u] = term_of(u / n_own, u % n_own);
+            } else {
+                // this rank's slots into every rank's exchange buffer, 4 rows per
+                // 16-byte store; then the CTA's release on every rank's counter
+                const int quads = mine * kTileRows / 4;
+                for (int u = threadIdx.x; u < quads * n_own; u += kMT) {
+                    const int j = u / quads, r = (u % quads) * 4;
+                    const float4 v = make_float4(term_of(r, j), term_of(r + 1, j), term_of(r + 2, j), term_of(r + 3, j));
                     const int row = item_id(r / kTileRows) * kTileRows + r % kTileRows;
-                    for (int p = 0; p < d.ep_world; ++p) ep_terms(d.ep_peers[p], layer & 1, own[j], H)[row] = term;
+                    for (int p = 0; p < d.ep_world; ++p)
+                        *reinterpret_cast<float4*>(ep_terms(d.ep_peers[p], layer & 1, own[j], H) + row) = v;
                 }
+                __syncthreads();
+                if (threadIdx.x == 0)            // the CTA's stores happen before (bar.sync), so they are released
+                    for (int p = 0; p < d.ep_world; ++p) red_release_sys_add(&ep_tail(d.ep_peers[p], H)->layer_cnt[d.ep_rank], 1u);
             }
             if (!ep) {
                 __syncthreads();
@@ -1348,15 +1365,9 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_step(Dev d, const LayerW* __r
                     xown = xown + moe;
                     d.x[row] = xown;
                 }
-            } else {
-                __threadfence_system();
             }
-            grid_sync(bar, epoch, nsync, d);
-            if (ep && blockIdx.x == 0 && threadIdx.x == 0) {   // every CTA's stores are ordered before the barrier
-                __threadfence_system();
-                for (int p = 0; p < d.ep_world; ++p)
-                    st_release_sys(&ep_tail(d.ep_peers[p], H)->layer_flag[d.ep_rank], seqb + layer + 1);
-            }
+            if (ep) skip_sync(epoch, d);         // the next layer waits on every rank's counters instead
+            else grid_sync(bar, epoch, nsync, d);
         }
         qb = 1 - qb;
     }
