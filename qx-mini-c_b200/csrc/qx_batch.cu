@@ -43,6 +43,7 @@ namespace {
 
 constexpr int kGemmThreads = 128;   // 4 warps: one TMEM lane quarter each
 constexpr int kTokTile = 16;        // tokens (or expert slots) per tile: N = 128 columns
+constexpr int kTiles = 2;           // column tiles per CTA: each decoded weight block serves both
 constexpr int kRowTile = 128;       // weight rows per tile: M = 128
 constexpr int kSlab = 4096;         // bytes of one 32-value K step of a 128-row operand
 constexpr int kTmemCols = 256;      // hi accumulator in columns [0, 128), lo in [128, 256)
@@ -257,11 +258,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     uint8_t* bop = base + 16 * kSlab;
     __shared__ __align__(8) uint64_t mbar;
     __shared__ uint32_t tmem_base_s;
-    __shared__ int cols_s[kTokTile], bidx_s[kTokTile];
-    __shared__ int sexp_s[kTokTile][kMaxBlk];
+    __shared__ int cols_s[kTiles * kTokTile], bidx_s[kTiles * kTokTile];
+    __shared__ int sexp_s[kTiles * kTokTile][kMaxBlk];
     const GemmItem it = a.items[blockIdx.x];
-    const int r = threadIdx.x, warp = r >> 5, ncol = it.ncols;
-    if (r < kTokTile) {
+    const int r = threadIdx.x, warp = r >> 5, ncol = it.ncols, ntile = (ncol + kTokTile - 1) / kTokTile;
+    if (r < kTiles * kTokTile) {
         const int c = r < ncol ? a.cols[it.col0 + r] : -1;
         cols_s[r] = c;
         bidx_s[r] = c < 0 ? -1 : (a.b_by_token ? c / 8 : c);
@@ -282,15 +283,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = tmem_base_s;
-    for (int i = r; i < kTokTile * a.nblk; i += kGemmThreads) {
+    for (int i = r; i < kTiles * kTokTile * a.nblk; i += kGemmThreads) {
         const int j = i / a.nblk, b = i % a.nblk;
         sexp_s[j][b] = bidx_s[j] < 0 ? 0 : a.sexp[(size_t)bidx_s[j] * a.nblk + b];
     }
     const uint8_t* mat = a.weights + (size_t)it.expert * a.expert_stride + (size_t)(it.row0 + r) * a.row_bytes;
     const uint32_t idesc = idesc_i8(kRowTile, 8 * kTokTile);
-    double acc[kTokTile];
+    double acc[kTiles * kTokTile];
 #pragma unroll
-    for (int j = 0; j < kTokTile; ++j) acc[j] = 0.0;
+    for (int j = 0; j < kTiles * kTokTile; ++j) acc[j] = 0.0;
     unsigned phase = 0;
     bool ok = true;
     using Src = RowSrcN<FMT == kGemmR8 ? 16 : 8>;
@@ -301,93 +302,102 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     };
     Src src;
     src_at(0, src);
-    // B: each column's 2 KB of a block (8 slabs x 256 B: limbs 0-6 and the
-    // ones column of 32 values) to slab s, 8-row group j
-    auto stage_b = [&](int b) {
+    // B of column tile t: each column's 2 KB of a block (8 slabs x 256 B:
+    // limbs 0-6 and the ones column of 32 values) to slab s, 8-row group j.
+    // Rows of columns past the item keep whatever they held: their MMA
+    // columns are never folded into a stored result.
+    auto stage_b = [&](int b, int t) {
         for (int i = r; i < kTokTile * 128; i += kGemmThreads) {
-            const int j = i >> 7, c16 = i & 127;
-            if (bidx_s[j] < 0) continue;
+            const int j = i >> 7, c16 = i & 127, col = t * kTokTile + j;
+            if (bidx_s[col] < 0) continue;
             const int s = c16 >> 4, w = c16 & 15;
             cp_async16(bop + s * kSlab + j * 256 + w * 16,
-                       a.bq + ((size_t)bidx_s[j] * a.nblk + b) * 2048 + s * 256 + w * 16);
+                       a.bq + ((size_t)bidx_s[col] * a.nblk + b) * 2048 + s * 256 + w * 16);
         }
         cp_async_commit();
     };
-    stage_b(0);
+    stage_b(0, 0);
     for (int b = 0; b < a.nblk && ok; ++b) {
         // A: this thread's row of block b (source loaded during the previous block)
         if constexpr (FMT == kGemmIq2r) decode_iq2r_row(src, r, ahi, alo);
         else if constexpr (FMT == kGemmR4Iq4) decode_r4_row<true>(src, r, ahi, alo);
         else if constexpr (FMT == kGemmR8) decode_r8_row(src, r, ahi, alo);
         else decode_r4_row<false>(src, r, ahi, alo);
-        cp_async_wait<0>();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core
-        __syncthreads();
-        if (r == 0) {
+        const double dfac = (double)h2f(*reinterpret_cast<const uint16_t*>(mat + 2 * b));
+#pragma unroll
+        for (int t = 0; t < kTiles; ++t) {
+            if (t >= ntile || !ok) break;
+            cp_async_wait<0>();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core
+            __syncthreads();
+            if (r == 0) {
+                tc_fence_after();
+                const uint32_t ah = smem_addr(ahi), al = smem_addr(alo), bb = smem_addr(bop);
+#pragma unroll
+                for (int s = 0; s < 8; ++s) {
+                    const uint64_t bd = umma_desc(bb + s * kSlab, 128, 256);
+                    mma_i8(tbase, umma_desc(ah + s * kSlab, 128, 256), bd, idesc, s > 0);
+                    mma_i8(tbase + 128, umma_desc(al + s * kSlab, 128, 256), bd, idesc, s > 0);
+                }
+                mma_commit(&mbar);
+            }
+            if (t == 0 && b + 1 < a.nblk) src_at(b + 1, src);   // in flight during the MMAs and the folds
+            // bounded wait for the MMAs (2 s; a healthy block takes microseconds);
+            // every thread agrees on the outcome before it touches TMEM
+            {
+                const unsigned long long t0 = gtimer();
+                uint32_t done = 0;
+                while (!done) {
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+                        : "=r"(done)
+                        : "r"(smem_addr(&mbar)), "r"(phase)
+                        : "memory");
+                    if (!done && gtimer() - t0 > 2000000000ull) break;
+                }
+                ok = __syncthreads_and((int)done) != 0;
+                if (!ok && r == 0) atomicOr(a.err, kErrTimeout);
+                phase ^= 1u;
+            }
             tc_fence_after();
-            const uint32_t ah = smem_addr(ahi), al = smem_addr(alo), bb = smem_addr(bop);
+            if (ok) {
+                // the MMAs have read B: refill it with the next tile (or the
+                // next block's first tile) during the fold
+                if (t + 1 < ntile) stage_b(b, t + 1);
+                else if (b + 1 < a.nblk) stage_b(b + 1, 0);
+                // fold: column j's exact block integer X = sum_n c_n 2^(8n) (limb 6
+                // minus 128 x the ones column removes the 2^55 offset) times
+                // d * 2^(fexp - S_j)
+                const uint32_t lane_addr = tbase + ((uint32_t)(32 * warp) << 16);
 #pragma unroll
-            for (int s = 0; s < 8; ++s) {
-                const uint64_t bd = umma_desc(bb + s * kSlab, 128, 256);
-                mma_i8(tbase, umma_desc(ah + s * kSlab, 128, 256), bd, idesc, s > 0);
-                mma_i8(tbase + 128, umma_desc(al + s * kSlab, 128, 256), bd, idesc, s > 0);
-            }
-            mma_commit(&mbar);
-        }
-        if (b + 1 < a.nblk) src_at(b + 1, src);   // in flight during the MMAs and the fold
-        // bounded wait for the MMAs (2 s; a healthy block takes microseconds);
-        // every thread agrees on the outcome before it touches TMEM
-        {
-            const unsigned long long t0 = gtimer();
-            uint32_t done = 0;
-            while (!done) {
-                asm volatile(
-                    "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
-                    : "=r"(done)
-                    : "r"(smem_addr(&mbar)), "r"(phase)
-                    : "memory");
-                if (!done && gtimer() - t0 > 2000000000ull) break;
-            }
-            ok = __syncthreads_and((int)done) != 0;
-            if (!ok && r == 0) atomicOr(a.err, kErrTimeout);
-            phase ^= 1u;
-        }
-        tc_fence_after();
-        if (ok && b + 1 < a.nblk) stage_b(b + 1);   // the MMAs have read B: refill it during the fold
-        if (ok) {
-            // fold: column j's exact block integer X = sum_n c_n 2^(8n) (limb 6
-            // minus 128 x the ones column removes the 2^55 offset) times
-            // d * 2^(fexp - S_j)
-            const double dfac = (double)h2f(*reinterpret_cast<const uint16_t*>(mat + 2 * b));
-            const uint32_t lane_addr = tbase + ((uint32_t)(32 * warp) << 16);
+                for (int p = 0; p < kTokTile / 2; ++p) {
+                    uint32_t hv[16], lv[16];
+                    tmem_ld16(lane_addr + 16 * p, hv);
+                    tmem_ld16(lane_addr + 128 + 16 * p, lv);
+                    tmem_wait_ld();
 #pragma unroll
-            for (int p = 0; p < kTokTile / 2; ++p) {
-                uint32_t hv[16], lv[16];
-                tmem_ld16(lane_addr + 16 * p, hv);
-                tmem_ld16(lane_addr + 128 + 16 * p, lv);
-                tmem_wait_ld();
+                    for (int h = 0; h < 2; ++h) {
+                        int c[8];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    int c[8];
-#pragma unroll
-                    for (int n = 0; n < 8; ++n) c[n] = 64 * (int)hv[8 * h + n] + (int)lv[8 * h + n];
-                    c[6] -= 128 * c[7];
-                    const long long plo = (long long)c[0] + ((long long)c[1] << 8) + ((long long)c[2] << 16) +
-                                          ((long long)c[3] << 24);
-                    const long long phi = (long long)c[4] + ((long long)c[5] << 8) + ((long long)c[6] << 16);
-                    const int j = 2 * p + h;
-                    const double f = dfac * blk_pow2(sexp_s[j][b], a.fexp);
-                    acc[j] = fma((double)phi, f * 4294967296.0, acc[j]);
-                    acc[j] = fma((double)plo, f, acc[j]);
+                        for (int n = 0; n < 8; ++n) c[n] = 64 * (int)hv[8 * h + n] + (int)lv[8 * h + n];
+                        c[6] -= 128 * c[7];
+                        const long long plo = (long long)c[0] + ((long long)c[1] << 8) + ((long long)c[2] << 16) +
+                                              ((long long)c[3] << 24);
+                        const long long phi = (long long)c[4] + ((long long)c[5] << 8) + ((long long)c[6] << 16);
+                        const int j = t * kTokTile + 2 * p + h;
+                        const double f = dfac * blk_pow2(sexp_s[j][b], a.fexp);
+                        acc[j] = fma((double)phi, f * 4294967296.0, acc[j]);
+                        acc[j] = fma((double)plo, f, acc[j]);
+                    }
                 }
             }
+            tc_fence_before();
+            __syncthreads();   // the accumulators (and, after the last tile, the slabs) are free
         }
-        tc_fence_before();
-        __syncthreads();   // the accumulators and slabs are free for the next block
     }
     if (ok) {
 #pragma unroll
-        for (int j = 0; j < kTokTile; ++j) {
+        for (int j = 0; j < kTiles * kTokTile; ++j) {
             const double v = acc[j];
             if (j < ncol) {
                 const size_t o = (size_t)cols_s[j] * a.out_stride + a.out_off + it.row0 + r;

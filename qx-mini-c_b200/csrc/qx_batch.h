@@ -10,8 +10,9 @@ namespace qx {
 // One CTA of the grouped GEMM: rows [row0, row0 + 128) of expert `expert`
 // against the columns cols[col0 .. col0 + ncols) (ncols <= 16).
 struct GemmItem {
-    int expert, col0, ncols, row0;
+    int expert, col0, ncols, row0;   // ncols <= kGemmItemCols
 };
+constexpr int kGemmItemCols = 32;    // columns (tokens or slots) per work item: two 16-column tiles
 enum { kGemmIq2r = 0, kGemmR4Iq3 = 1, kGemmR4Iq4 = 2, kGemmR8 = 3 };
 
 struct GemmArgs {

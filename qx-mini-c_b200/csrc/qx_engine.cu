@@ -904,11 +904,11 @@ qx::GemmArgs proj_args(qx_cuda_engine* E, const uint8_t* weights, int K, float* 
     return a;
 }
 
-// Work items of a projection over N tokens: 16-token tiles x 128-row tiles.
+// Work items of a projection over N tokens: 32-token column pairs x 128-row tiles.
 bool proj_items(qx_cuda_engine* E, int N, int rows, int* count, char* err, uint64_t n) {
     std::vector<qx::GemmItem> items;
-    for (int c0 = 0; c0 < N; c0 += 16)
-        for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({0, c0, std::min(16, N - c0), r0});
+    for (int c0 = 0; c0 < N; c0 += qx::kGemmItemCols)
+        for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({0, c0, std::min(qx::kGemmItemCols, N - c0), r0});
     if (items.size() > E->batch.item_cap) { set_err(err, n, "batched work list too long"); return false; }
     *count = (int)items.size();
     return h2d(E, E->batch.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n);
@@ -949,8 +949,9 @@ bool moe_batch_run(qx_cuda_engine* E, uint32_t layer, int N, char* err, uint64_t
     auto make_items = [&](int rows) {
         items.clear();
         for (int e = 0; e < EX; ++e)
-            for (int c0 = start[e]; c0 < start[e + 1]; c0 += 16)
-                for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({e, c0, std::min(16, start[e + 1] - c0), r0});
+            for (int c0 = start[e]; c0 < start[e + 1]; c0 += qx::kGemmItemCols)
+                for (int r0 = 0; r0 < rows; r0 += 128)
+                    items.push_back({e, c0, std::min(qx::kGemmItemCols, start[e + 1] - c0), r0});
     };
     if (!h2d(E, B.cols, cols.data(), (size_t)S * 4, err, n)) return false;
     // gate and up: rows of I values of K = H, columns = slots, B = the token's limbs
