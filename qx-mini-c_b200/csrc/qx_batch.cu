@@ -260,6 +260,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     __shared__ uint32_t tmem_base_s;
     __shared__ int cols_s[kTiles * kTokTile], bidx_s[kTiles * kTokTile];
     __shared__ int sexp_s[kTiles * kTokTile][kMaxBlk];
+    if (a.nitems && (int)blockIdx.x >= *a.nitems) return;     // past a device-built list
     const GemmItem it = a.items[blockIdx.x];
     const int r = threadIdx.x, warp = r >> 5, ncol = it.ncols, ntile = (ncol + kTokTile - 1) / kTokTile;
     if (r < kTiles * kTokTile) {
@@ -409,6 +410,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(GemmArgs a) {
     tc_fence_after();
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTmemCols) : "memory");
+}
+
+// ---- expert slot lists ----------------------------------------------------------
+__global__ void k_slot_count(const int* sel, int nslots, int E, int* count) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s < nslots) {
+        const int e = sel[s];
+        if (e >= 0 && e < E) atomicAdd(count + e, 1);
+    }
+}
+
+// CTA e (256 threads): expert e's start and item offsets from the counts, its
+// slots compacted in slot order (ballot per warp, warp offsets per pass), and
+// its work items.
+__global__ void __launch_bounds__(256) k_slot_lists(const int* sel, int nslots, int E, const int* count, int* cols,
+                                                    GemmItem* items_gu, int rows_gu, GemmItem* items_dn, int rows_dn,
+                                                    int* nitems) {
+    __shared__ int wsum[8];
+    __shared__ int base_s[4];
+    const int e = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    if (warp == 0) {                      // exclusive prefixes over the experts before e
+        int st = 0, ct = 0, tot_ct = 0;
+        for (int k = lane; k < E; k += 32) {
+            const int c = count[k], n = (c + kGemmItemCols - 1) / kGemmItemCols;
+            if (k < e) { st += c; ct += n; }
+            tot_ct += n;
+        }
+        for (int o = 16; o; o >>= 1) {
+            st += __shfl_xor_sync(0xffffffffu, st, o);
+            ct += __shfl_xor_sync(0xffffffffu, ct, o);
+            tot_ct += __shfl_xor_sync(0xffffffffu, tot_ct, o);
+        }
+        if (lane == 0) {
+            base_s[0] = st;
+            base_s[1] = ct;
+            if (e == 0) {
+                nitems[0] = tot_ct * (rows_gu / kRowTile);
+                nitems[1] = tot_ct * (rows_dn / kRowTile);
+            }
+        }
+    }
+    __syncthreads();
+    const int start = base_s[0], ct0 = base_s[1], cnt = count[e];
+    int done = 0;
+    for (int s0 = 0; s0 < nslots; s0 += 256) {
+        const int s = s0 + t;
+        const bool mine = s < nslots && sel[s] == e;
+        const unsigned m = __ballot_sync(0xffffffffu, mine);
+        if (lane == 0) wsum[warp] = __popc(m);
+        __syncthreads();
+        int before = done;
+        for (int w = 0; w < warp; ++w) before += wsum[w];
+        if (mine) cols[start + before + __popc(m & ((1u << lane) - 1u))] = s;
+        int all = 0;
+        for (int w = 0; w < 8; ++w) all += wsum[w];
+        done += all;
+        __syncthreads();
+    }
+    const int nct = (cnt + kGemmItemCols - 1) / kGemmItemCols, rgu = rows_gu / kRowTile, rdn = rows_dn / kRowTile;
+    for (int i = t; i < nct * rgu; i += 256) {
+        const int c = i / rgu, rt = i % rgu;
+        items_gu[(size_t)(ct0 + c) * rgu + rt] =
+            GemmItem{e, start + c * kGemmItemCols, min(kGemmItemCols, cnt - c * kGemmItemCols), rt * kRowTile};
+    }
+    for (int i = t; i < nct * rdn; i += 256) {
+        const int c = i / rdn, rt = i % rdn;
+        items_dn[(size_t)(ct0 + c) * rdn + rt] =
+            GemmItem{e, start + c * kGemmItemCols, min(kGemmItemCols, cnt - c * kGemmItemCols), rt * kRowTile};
+    }
 }
 
 // ---- activations -------------------------------------------------------------
@@ -967,6 +1037,13 @@ void launch_moe_gemm(const GemmArgs& a, int nitems, cudaStream_t st) {
         case kGemmR4Iq4: k_moe_gemm<kGemmR4Iq4><<<nitems, kGemmThreads, kSmemGemm, st>>>(a); break;
         default: k_moe_gemm<kGemmR8><<<nitems, kGemmThreads, kSmemGemm, st>>>(a); break;
     }
+}
+
+void launch_slot_lists(const int* sel, int nslots, int E, int* count, int* cols, GemmItem* items_gu, int rows_gu,
+                       GemmItem* items_dn, int rows_dn, int* nitems, cudaStream_t st) {
+    cudaMemsetAsync(count, 0, (size_t)E * 4, st);
+    k_slot_count<<<(nslots + 255) / 256, 256, 0, st>>>(sel, nslots, E, count);
+    k_slot_lists<<<E, 256, 0, st>>>(sel, nslots, E, count, cols, items_gu, rows_gu, items_dn, rows_dn, nitems);
 }
 
 void launch_batch_swiglu(const float* gu, int I, int nslots, float* h, cudaStream_t st) {

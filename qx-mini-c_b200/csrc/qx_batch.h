@@ -34,6 +34,7 @@ struct GemmArgs {
     size_t out_stride;
     int out_off;
     int* err;
+    const int* nitems;            // if set: the number of valid items (device-built lists); CTAs past it exit
 };
 
 // An INT8 KV cache of `slots` sequences: [slot][layer][ctx][kv] bytes and
@@ -61,6 +62,15 @@ void launch_batch_embed(const uint32_t* tokens, const uint8_t* emb, int H, int V
 void launch_batch_qkv_post(const float* qkv, const float* q_norm, const float* k_norm, const double* rope, int layer,
                            const int* tpos, const int* tslot, const KvView& kv, int ntok, int QH, int KVH, float* qn,
                            cudaStream_t st);
+// The expert slot lists on the device: count[e] = slots that chose expert e
+// (count zeroed first), then cols = the slots grouped by expert in slot order,
+// and the GEMM work items of the gate/up (rows_gu weight rows) and down
+// (rows_dn) projections in expert, column-pair, row-tile order, with their
+// counts in nitems[0], nitems[1].  Slots with an expert outside [0, E) (a
+// failed router, which raised its error flag) are left out.
+void launch_slot_lists(const int* sel, int nslots, int E, int* count, int* cols, GemmItem* items_gu, int rows_gu,
+                       GemmItem* items_dn, int rows_dn, int* nitems, cudaStream_t st);
+
 // first_pos >= 0: token t is at position first_pos + t of KV slot 0 (a
 // prompt), which lets the launch size each bucket of tokens for its own
 // context length and, given vd ([max_pos + 1][kv_dim] doubles of scratch),

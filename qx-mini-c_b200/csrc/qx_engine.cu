@@ -84,6 +84,7 @@ struct qx_cuda_engine {
         float *x, *xn, *gu, *h, *y, *out, *moe, *qkv, *qn, *ctxo, *ao;
         uint8_t *bqx, *bqh;
         int *sx, *sh, *sel, *cols, *tcols, *tpos, *tslot;
+        int *count, *nitems;             // device-built expert slot lists: per-expert counts, item counts
         uint32_t *tok, *next;
         double* logits;                  // [cap][vocab] (batched decode's head)
         double* wsel;
@@ -836,7 +837,7 @@ bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
     const size_t Q = E->dm.q_dim(), KV = E->dm.kv_dim(), K = std::max(H, Q);
     const size_t V = E->dm.vocab;
     const size_t nhead = std::min<size_t>(ntok, QX_CUDA_MAX_SLOTS);   // tokens the batched head serves
-    const size_t items = std::max(std::max((S / 16 + (size_t)E->dm.experts) * std::max(2 * I / 128, H / 128),
+    const size_t items = std::max(std::max((S / qx::kGemmItemCols + (size_t)E->dm.experts) * (I / 128 + H / 128),
                                            (ntok / 16 + 1) * std::max(Q / 128, H / 128)),
                                   (nhead / 16 + 1) * (V / 128));
     size_t off = 0;
@@ -849,7 +850,7 @@ bool batch_reserve(qx_cuda_engine* E, size_t ntok, char* err, uint64_t n) {
         {(void**)&B.qkv, ntok * (Q + 2 * KV) * 4}, {(void**)&B.qn, ntok * Q * 4}, {(void**)&B.ctxo, ntok * Q * 4},
         {(void**)&B.ao, ntok * H * 4}, {(void**)&B.tcols, ntok * 4}, {(void**)&B.tok, ntok * 4},
         {(void**)&B.tpos, ntok * 4}, {(void**)&B.tslot, ntok * 4}, {(void**)&B.next, ntok * 4},
-        {(void**)&B.logits, nhead * V * 8}, {(void**)&B.vd, (size_t)E->dm.ctx * KV * 8}};
+        {(void**)&B.logits, nhead * V * 8}, {(void**)&B.count, (size_t)E->dm.experts * 4}, {(void**)&B.nitems, 8}, {(void**)&B.vd, (size_t)E->dm.ctx * KV * 8}};
     for (auto& p : parts) off = align_up(off + p.second, 256);
     if (!cuda_ok(cudaMalloc(&B.mem, off), "cudaMalloc(batch)", err, n)) return false;
     off = 0;
@@ -904,11 +905,14 @@ qx::GemmArgs proj_args(qx_cuda_engine* E, const uint8_t* weights, int K, float* 
     return a;
 }
 
-// Work items of a projection over N tokens: 32-token column pairs x 128-row tiles.
+// Work items of a projection over N tokens: column tiles x 128-row tiles.  A
+// prompt-sized batch takes two 16-token tiles per item (one weight decode for
+// both); a small one keeps one tile per item, for twice the CTAs.
 bool proj_items(qx_cuda_engine* E, int N, int rows, int* count, char* err, uint64_t n) {
     std::vector<qx::GemmItem> items;
-    for (int c0 = 0; c0 < N; c0 += qx::kGemmItemCols)
-        for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({0, c0, std::min(qx::kGemmItemCols, N - c0), r0});
+    const int w = N >= 512 ? qx::kGemmItemCols : 16;
+    for (int c0 = 0; c0 < N; c0 += w)
+        for (int r0 = 0; r0 < rows; r0 += 128) items.push_back({0, c0, std::min(w, N - c0), r0});
     if (items.size() > E->batch.item_cap) { set_err(err, n, "batched work list too long"); return false; }
     *count = (int)items.size();
     return h2d(E, E->batch.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n);
@@ -925,42 +929,16 @@ bool moe_batch_run(qx_cuda_engine* E, uint32_t layer, int N, char* err, uint64_t
     qx::launch_batch_limbs(B.xn, H, N, B.bqx, B.sx, E->stream);
     qx::launch_batch_router(B.xn, w.router, H, EX, N, B.sel, B.wsel, E->dev.err, E->stream);
     E->prof.kernel_launches += 3;
-    // the slots (token, rank) of every expert, in token order
-    std::vector<int> sel(S);
-    if (!cuda_ok(cudaMemcpyAsync(sel.data(), B.sel, (size_t)S * 4, cudaMemcpyDeviceToHost, E->stream), "d2h", err, n) ||
-        !cuda_ok(cudaStreamSynchronize(E->stream), "router", err, n))
-        return false;
-    E->prof.device_to_host_bytes += (uint64_t)S * 4;
-    std::vector<int> count(EX, 0), start(EX + 1, 0), cols(S);
-    for (int s = 0; s < S; ++s) {
-        if (sel[s] < 0 || sel[s] >= EX) {   // a non-finite router softmax: fail the call, clear the device flag
-            finish(E, err, n);
-            set_err(err, n, "invalid selected router weights");
-            return false;
-        }
-        count[sel[s]]++;
-    }
-    for (int e = 0; e < EX; ++e) start[e + 1] = start[e] + count[e];
-    {
-        std::vector<int> fill(start.begin(), start.end() - 1);
-        for (int s = 0; s < S; ++s) cols[fill[sel[s]]++] = s;
-    }
-    std::vector<qx::GemmItem> items;
-    auto make_items = [&](int rows) {
-        items.clear();
-        for (int e = 0; e < EX; ++e)
-            for (int c0 = start[e]; c0 < start[e + 1]; c0 += qx::kGemmItemCols)
-                for (int r0 = 0; r0 < rows; r0 += 128)
-                    items.push_back({e, c0, std::min(qx::kGemmItemCols, start[e + 1] - c0), r0});
-    };
-    if (!h2d(E, B.cols, cols.data(), (size_t)S * 4, err, n)) return false;
-    // gate and up: rows of I values of K = H, columns = slots, B = the token's limbs
-    make_items(I);
-    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return false; }
-    if (!h2d(E, B.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return false;
+    // the slots (token, rank) of every expert in token order and both GEMMs'
+    // work items, built on the device (no host round trip)
+    const size_t max_ct = (size_t)S / qx::kGemmItemCols + (size_t)EX;   // bounds sum_e ceil(count_e / 32)
+    const int max_gu = (int)(max_ct * (size_t)(I / 128)), max_dn = (int)(max_ct * (size_t)(H / 128));
+    if ((size_t)max_gu + (size_t)max_dn > B.item_cap) { set_err(err, n, "batched expert work list too long"); return false; }
+    qx::launch_slot_lists(B.sel, S, EX, B.count, B.cols, B.items, I, B.items + max_gu, H, B.nitems, E->stream);
     const size_t rb2 = qx::iq2r_row_bytes(H);
     qx::GemmArgs ga{};
     ga.items = B.items;
+    ga.nitems = B.nitems;
     ga.cols = B.cols;
     ga.expert_stride = (size_t)I * rb2;
     ga.row_bytes = (uint32_t)rb2;
@@ -976,19 +954,18 @@ bool moe_batch_run(qx_cuda_engine* E, uint32_t layer, int N, char* err, uint64_t
     ga.err = E->dev.err;
     ga.weights = w.gate_r;
     ga.out_off = 0;
-    qx::launch_moe_gemm(ga, (int)items.size(), E->stream);
+    qx::launch_moe_gemm(ga, max_gu, E->stream);
     ga.weights = w.up_r;
     ga.out_off = I;
-    qx::launch_moe_gemm(ga, (int)items.size(), E->stream);
+    qx::launch_moe_gemm(ga, max_gu, E->stream);
     // SwiGLU, then the down input's limbs per slot
     qx::launch_batch_swiglu(B.gu, I, S, B.h, E->stream);
     qx::launch_batch_limbs(B.h, I, S, B.bqh, B.sh, E->stream);
     // down: rows of H values of K = I, columns = slots, B = the slot's limbs
-    make_items(H);
-    if (items.size() > B.item_cap) { set_err(err, n, "batched expert work list too long"); return false; }
-    if (!h2d(E, B.items, items.data(), items.size() * sizeof(qx::GemmItem), err, n)) return false;
     const size_t rb4 = qx::r4_bytes_per_row(I);
     qx::GemmArgs gd = ga;
+    gd.items = B.items + max_gu;
+    gd.nitems = B.nitems + 1;
     gd.weights = w.down_r;
     gd.expert_stride = (size_t)H * rb4;
     gd.row_bytes = (uint32_t)rb4;
@@ -1003,9 +980,9 @@ bool moe_batch_run(qx_cuda_engine* E, uint32_t layer, int N, char* err, uint64_t
     gd.out = B.y;
     gd.out_stride = (size_t)H;
     gd.out_off = 0;
-    qx::launch_moe_gemm(gd, (int)items.size(), E->stream);
+    qx::launch_moe_gemm(gd, max_dn, E->stream);
     qx::launch_batch_combine(B.x, B.y, B.wsel, H, N, B.moe, B.out, E->stream);
-    E->prof.kernel_launches += 6;
+    E->prof.kernel_launches += 8;   // slot count + lists, gate, up, SwiGLU, limbs, down, combine
     return cuda_ok(cudaGetLastError(), "kernel launch", err, n);
 }
 
