@@ -212,3 +212,27 @@ def test_decode_batch_arguments(mini_image):
             eng.decode_batch([64], [42], [0])
     finally:
         eng.close()
+
+
+def test_decode_batch_long_context_equals_single_sequence():
+X
+    the attention kernel's shared memory and live in a global scratch buffer.
+    Four sequences at positions 3600..3700, in fresh slots (zero history),
+    two batched steps: each sequence's tokens must equal the single-sequence
+    step's from the same zero history."""
+    eng = qxlib.Engine(qxlib.build_image(qxlib.synth_config(7, layers=4)), ctx=3712)
+    try:
+        starts, pos0, slots = [42, 7, 1000, 3000], [3600, 3601, 3700, 3650], [5, 0, 63, 11]
+        cur, got = list(starts), [[] for _ in starts]
+        for step in range(2):
+            nxt = eng.decode_batch(slots, cur, [p + step for p in pos0])
+            for i, t in enumerate(nxt):
+                got[i].append(int(t))
+                cur[i] = int(t)
+        for i in range(len(starts)):
+            eng.reset()
+            t0 = eng.decode_step(starts[i], pos0[i])["token"]
+            t1 = eng.decode_step(t0, pos0[i] + 1)["token"]
+            assert got[i] == [t0, t1], "sequence %d" % i
+    finally:
+        eng.close()
