@@ -215,11 +215,11 @@ def test_decode_batch_arguments(mini_image):
 
 
 def test_decode_batch_long_context_equals_single_sequence():
-X
-    the attention kernel's shared memory and live in a global scratch buffer.
-    Four sequences at positions 3600..3700, in fresh slots (zero history),
-    two batched steps: each sequence's tokens must equal the single-sequence
-    step's from the same zero history."""
+    """Past ~3470 positions the 8 query heads' softmax weights no longer fit
+    the grouped attention kernel's shared memory, and the batched step takes
+    the per-head kernel.  Four sequences at positions 3600..3700, in fresh
+    slots (zero history), two batched steps: each sequence's tokens must equal
+    the single-sequence step's from the same zero history."""
     eng = qxlib.Engine(qxlib.build_image(qxlib.synth_config(7, layers=4)), ctx=3712)
     try:
         starts, pos0, slots = [42, 7, 1000, 3000], [3600, 3601, 3700, 3650], [5, 0, 63, 11]
