@@ -757,7 +757,20 @@ __global__ void __launch_bounds__(128) k_batch_attn(const float* qn, KvView kv, 
     const int8_t* vb = vcache + (size_t)layer * ctx * KV + g * D + i;
     const float* vs = vscale + (size_t)layer * ctx;
     float acc = 0.0f;
-    for (int p = 0; p < T; ++p) acc += (float)(w_s[p] * (double)(i8_to_f32(vb[(size_t)p * KV]) * vs[p]));
+    constexpr int U = 16;                 // positions whose loads go out together
+    int p = 0;
+    for (; p + U <= T; p += U) {
+        int8_t vq[U];
+        float vsc[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            vq[u] = vb[(size_t)(p + u) * KV];
+            vsc[u] = vs[p + u];
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) acc += (float)(w_s[p + u] * (double)(i8_to_f32(vq[u]) * vsc[u]));
+    }
+    for (; p < T; ++p) acc += (float)(w_s[p] * (double)(i8_to_f32(vb[(size_t)p * KV]) * vs[p]));
     ctx_out[(size_t)t * Q + h * D + i] = acc;
 }
 
