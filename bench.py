@@ -311,6 +311,10 @@ def stage_configs(eng, cfg, stream, reps=10,
                                   "tok_s": round(tok_s, 1), "us_per_token": round(us / steps, 1),
                                   "GB/s": round(nbytes * tok_s / 1e9, 1),
                                   "frac_of_measured_hbm": round(nbytes * tok_s / 1e9 / peak, 4)}
+        # per-phase time of one step at position 4000 (median over layers 1..)
+        tr = eng.phase_trace(W.START_TOKEN, 4000)
+        out["config4_ctx4096"]["phases_at_position_4000_us_per_layer"] = {
+            k: round(float(np.median(v[1:])), 2) for k, v in tr.items() if isinstance(v, list) and len(v) > 1}
     if "batch" in which:
         for n in (64, 2048):
             x = np.stack([qxlib.normal_vector(1000 + t, H) for t in range(n)])
