@@ -425,6 +425,7 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     d.out_norm = (const float*)W("output_norm.weight");
     d.head = W("output.weight");
     d.head_grid = qx::head_grid_size(dev, dm);
+    d.head_grid_r8 = qx::head_grid_size(dev, dm, true);
     const size_t L = dm.layers, C = dm.ctx, D = dm.head_dim;
     struct Slot { void** p; size_t bytes; };
     std::vector<Slot> slots;
@@ -449,11 +450,11 @@ QX_API int qx_cuda_engine_create(const qx_cuda_model* model, const qx_cuda_tenso
     add((void**)&d.selw_d, 8 * 8);
     add((void**)&d.hbuf, 8 * I * 4);
     add((void**)&d.logits, (size_t)dm.vocab * 4);
-    // argmax partials: one per CTA of the per-stage head or of the persistent
-    // step kernel (one CTA per SM), whichever is larger
+    // argmax partials: one per CTA of the per-stage head (either layout) or
+    // of the persistent step kernel (one CTA per SM), whichever is largest
     int sm_count = 0;
     cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    const size_t partials = (size_t)std::max(d.head_grid, sm_count);
+    const size_t partials = (size_t)std::max({d.head_grid, d.head_grid_r8, sm_count});
     add((void**)&d.best_val, partials * sizeof(double));
     add((void**)&d.best_idx, partials * 4);
     add((void**)&d.counters, qx::kCntTotal * 4);

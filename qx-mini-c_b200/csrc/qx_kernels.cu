@@ -516,29 +516,40 @@ __global__ void __launch_bounds__(kThreads) k_down(Dev d, LayerW w, int layer) {
 // ---------------------------------------------------------------------------
 constexpr int kHeadStages = 3;
 constexpr int kHeadTiles = 2;
+// With the re-laid head (R8, the persistent step's copy: int8 weights, no
+// decoding) a group is one 16-row tile, one block per warp, so the block
+// partials add in block order as the persistent step's head adds them.
+constexpr int kHeadStagesR8 = 2;   // small enough for two CTAs (16 warps) per SM
 
+__host__ __device__ constexpr uint32_t head_row_bytes(bool r8, int H) {
+    return r8 ? (uint32_t)r8_row_bytes(H) : (uint32_t)(H / 256) * 210u;
+}
+
+template <bool R8>
 __global__ void __launch_bounds__(kThreads) k_head(Dev d) {
+    constexpr int TILES = R8 ? 1 : kHeadTiles, STAGES = R8 ? kHeadStagesR8 : kHeadStages;
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ double scratch[kWarps];
     __shared__ double wbv[kWarps];
     __shared__ int wbi[kWarps];
     const int H = d.dm.hidden, V = d.dm.vocab;
     const int nblk = H / 256;
-    const uint32_t rb = (uint32_t)nblk * 210u, tb = (uint32_t)kTileRows * rb, stage = kHeadTiles * tb;
+    const uint32_t rb = head_row_bytes(R8, H), tb = (uint32_t)kTileRows * rb, stage = TILES * tb;
+    const uint8_t* src = R8 ? d.head_r : d.head;
     Carve cv(smem);
-    uint8_t* ring = cv.take<uint8_t>(kHeadStages * stage);
+    uint8_t* ring = cv.take<uint8_t>(STAGES * stage);
     float* xs = cv.take<float>(H);
     uint32_t* xb = cv.take<uint32_t>(xq_words(H));
     int* sb = cv.take<int>(H / 256);
     double* part = cv.take<double>(kWarps * kTileRows);
-    const int ngroups = V / (kTileRows * kHeadTiles);
+    const int ngroups = V / (kTileRows * TILES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
-    const int parts = kWarps / kHeadTiles, tile = warp / parts, p = warp % parts;
+    const int parts = kWarps / TILES, tile = warp / parts, p = warp % parts;
     // the first stages are issued before the norm + x quantization run
     const int first = blockIdx.x, step = gridDim.x;
     const int mine = first < ngroups ? (ngroups - first + step - 1) / step : 0;
-    for (int s = 0; s < kHeadStages - 1; ++s) {
-        if (s < mine) stage_copy(ring + (uint32_t)s * stage, d.head + (size_t)(first + s * step) * stage, stage);
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < mine) stage_copy(ring + (uint32_t)s * stage, src + (size_t)(first + s * step) * stage, stage);
         cp_async_commit();
     }
     rmsnorm_to_smem(d.x, d.out_norm, xs, H, scratch);
@@ -548,21 +559,24 @@ __global__ void __launch_bounds__(kThreads) k_head(Dev d) {
     int bi = 0x7fffffff;
     bool bad = false;
     for (int it = 0; it < mine; ++it) {
-        const int nx = it + kHeadStages - 1;
-        if (nx < mine)
-            stage_copy(ring + (uint32_t)(nx % kHeadStages) * stage, d.head + (size_t)(first + nx * step) * stage, stage);
+        const int nx = it + STAGES - 1;
+        if (nx < mine) stage_copy(ring + (uint32_t)(nx % STAGES) * stage, src + (size_t)(first + nx * step) * stage, stage);
         cp_async_commit();
-        cp_async_wait<kHeadStages - 1>();
+        cp_async_wait<STAGES - 1>();
         __syncthreads();
-        const uint8_t* base = ring + (uint32_t)(it % kHeadStages) * stage + tile * tb;
+        const uint8_t* base = ring + (uint32_t)(it % STAGES) * stage + tile * tb;
         Acc acc{};
-        dot_q6_k_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb}, lane,
-                     acc);
+        if (R8)
+            dot_r8_mma(base + g * rb, base + (g + 8) * rb, nblk, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb},
+                       lane, acc);
+        else
+            dot_q6_k_mma(base + g * rb, base + (g + 8) * rb, p * nblk / parts, (p + 1) * nblk / parts, XQ{xb, sb},
+                         lane, acc);
         store_tile_rows(part, warp, acc);
         __syncthreads();
-        if (threadIdx.x < kHeadTiles * kTileRows) {
+        if (threadIdx.x < TILES * kTileRows) {
             const int tl = threadIdx.x / kTileRows, r = threadIdx.x % kTileRows;
-            const int row = (first + it * step) * kHeadTiles * kTileRows + tl * kTileRows + r;
+            const int row = (first + it * step) * TILES * kTileRows + tl * kTileRows + r;
             const double v = sum_parts(part, tl, parts, r);
             if (!isfinite(v)) bad = true;
             d.logits[row] = (float)v;
@@ -699,8 +713,10 @@ size_t smem_down(const Dims& m, uint32_t bb = 136) {
     return 16 + a16(8 * (size_t)kTileRows * (m.moe_inter / 256) * bb) + a16(sizeof(IqTab)) + a16((size_t)8 * m.moe_inter * 4) +
            a16(xq_words(8 * m.moe_inter) * 4) + a16((size_t)8 * m.moe_inter / 256 * 4) + part_bytes();
 }
-size_t smem_head(const Dims& m) {
-    return 16 + a16((size_t)kHeadStages * kHeadTiles * kTileRows * (m.hidden / 256) * 210) + xq_bytes(m.hidden) + part_bytes();
+size_t smem_head(const Dims& m, bool r8 = false) {
+    const size_t ring = r8 ? (size_t)kHeadStagesR8 * kTileRows * head_row_bytes(true, m.hidden)
+                           : (size_t)kHeadStages * kHeadTiles * kTileRows * head_row_bytes(false, m.hidden);
+    return 16 + a16(ring) + xq_bytes(m.hidden) + part_bytes();
 }
 }  // namespace
 
@@ -727,17 +743,19 @@ cudaError_t configure_kernels() {
     set((const void*)k_proj<23>);
     set((const void*)k_proj<14>);
     set((const void*)k_proj_q5k);
-    set((const void*)k_head);
+    set((const void*)k_head<false>);
+    set((const void*)k_head<true>);
     set((const void*)k_final_norm);
     return e;
 }
 
-int head_grid_size(int device, const Dims& m) {
+int head_grid_size(int device, const Dims& m, bool r8) {
     int sms = 0, per = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_head, kThreads, smem_head(m));
+    if (r8) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_head<true>, kThreads, smem_head(m, true));
+    else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_head<false>, kThreads, smem_head(m));
     if (per < 1) per = 1;
-    const int groups = m.vocab / (kTileRows * kHeadTiles);
+    const int groups = m.vocab / (kTileRows * (r8 ? 1 : kHeadTiles));
     const int grid = sms * per;
     return grid < groups ? grid : groups;
 }
@@ -840,7 +858,8 @@ void launch_down(const Dev& d, const LayerW& w, int layer, cudaStream_t st) {
 
 void launch_head(const Dev& d, cudaStream_t st) {
     if (d.q8) launch_q8_head(d, st);
-    else k_head<<<d.head_grid, kThreads, smem_head(d.dm), st>>>(d);
+    else if (d.head_r) k_head<true><<<d.head_grid_r8, kThreads, smem_head(d.dm, true), st>>>(d);
+    else k_head<false><<<d.head_grid, kThreads, smem_head(d.dm), st>>>(d);
 }
 
 void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st) {

@@ -102,6 +102,7 @@ struct Dev {
     int* tokens_out;             // [ctx] argmax written at index pos
     int* err;                    // error bits
     int head_grid;               // CTAs of the head kernel (partials length)
+    int head_grid_r8;            // CTAs of the head kernel on the re-laid (R8) head
     unsigned long long* trace;   // optional: global-timer stamp per grid barrier (CTA 0)
     // expert parallelism (ep_world > 1; persistent step kernel only)
     int ep_rank, ep_world;
@@ -141,7 +142,7 @@ void launch_head(const Dev& d, cudaStream_t st);
 constexpr int kTopnParts = 148;
 void launch_topn(const Dev& d, int top_n, double* cand_v, int* cand_i, int* out_idx, float* out_val, cudaStream_t st);
 void launch_final_norm(const Dev& d, float* normalized, cudaStream_t st);
-int head_grid_size(int device, const Dims& m);
+int head_grid_size(int device, const Dims& m, bool r8 = false);
 size_t attn_scores_bytes(const Dims& m);
 // Grid barriers per layer of the persistent step kernel: QKV, attention
 // scores, attention context, O projection, router, gate/up, down.
