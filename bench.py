@@ -268,6 +268,7 @@ def stage_configs(eng, cfg, stream, reps=10,
         bf16 = 1400.0
     H, I, E = cfg.hidden, cfg.moe_intermediate, cfg.experts
     moe_layer = min(W.MOE_LAYER, cfg.layers - 1)
+    attn_layer = min(W.ATTN_LAYER, cfg.layers - 1)
     Q, KV = cfg.q_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
     rng = np.random.default_rng(3)
     out = {}
@@ -291,10 +292,10 @@ def stage_configs(eng, cfg, stream, reps=10,
             k = rng.integers(-127, 128, (P, KV), dtype=np.int8)
             v = rng.integers(-127, 128, (P, KV), dtype=np.int8)
             sc = (rng.random(P, dtype=np.float32) * 0.02 + 0.01).astype(np.float32)
-            eng.kv_write(W.ATTN_LAYER, 0, k, v, sc, sc)
+            eng.kv_write(attn_layer, 0, k, v, sc, sc)
             x = W.attn_input(H)
             hbm("config3_attention_ctx%d" % (P + 1),
-                time_call(lambda: eng.attention_layer(W.ATTN_LAYER, P, x), stream, reps),
+                time_call(lambda: eng.attention_layer(attn_layer, P, x), stream, reps),
                 (Q + 2 * KV) * (H // 256) * 136 + H * (Q // 256) * 136 + (P + 1) * (2 * KV + 8),
                 "attention layer at ctx %d (IQ4_XS QKV/O, INT8 KV history)" % (P + 1))
     if "decode4096" in which and eng.ctx >= 4096:

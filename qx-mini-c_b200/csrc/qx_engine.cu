@@ -712,8 +712,11 @@ bool set_scalars(qx_cuda_engine* E, uint32_t token, uint32_t pos, char* err, uin
 bool d2h(qx_cuda_engine* E, void* dst, const void* src, size_t bytes, char* err, uint64_t n) {
     if (!dst) return true;
     E->prof.device_to_host_bytes += bytes;
+    // through the pinned staging arena whenever it fits: a copy into pageable
+    // memory would wait for the stream on the spot; finish() (or kv_read)
+    // delivers the staged bytes after its one synchronisation
     const size_t off = (E->h_stage_used + 255) / 256 * 256;
-    if (bytes >= 16384 && E->h_stage && off + bytes <= E->h_stage_bytes) {
+    if (E->h_stage && off + bytes <= E->h_stage_bytes) {
         if (!cuda_ok(cudaMemcpyAsync(E->h_stage + off, src, bytes, cudaMemcpyDeviceToHost, E->stream),
                      "cudaMemcpyAsync(d2h)", err, n)) {
             E->pending.clear();               // the call fails: none of its outputs is delivered
@@ -731,8 +734,17 @@ bool d2h(qx_cuda_engine* E, void* dst, const void* src, size_t bytes, char* err,
     return false;
 }
 
+// Inputs that fit the pinned arena are copied into it first, so the transfer
+// is asynchronous; every caller synchronises the stream before it returns
+// (finish(), kv_write, kv_read), and only then is the arena reused.
 bool h2d(qx_cuda_engine* E, void* dst, const void* src, size_t bytes, char* err, uint64_t n) {
     E->prof.host_to_device_bytes += bytes;
+    const size_t off = (E->h_stage_used + 255) / 256 * 256;
+    if (E->h_stage && bytes && off + bytes <= E->h_stage_bytes) {
+        memcpy(E->h_stage + off, src, bytes);
+        E->h_stage_used = off + bytes;
+        src = E->h_stage + off;
+    }
     return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, E->stream), "cudaMemcpyAsync(h2d)", err, n);
 }
 
@@ -1216,8 +1228,10 @@ QX_API int qx_cuda_kv_write(qx_cuda_engine* E, uint32_t layer, uint32_t first, u
     bool ok = h2d(E, E->dev.kcache + base * KV, k, count * KV, err, n) &&
               h2d(E, E->dev.vcache + base * KV, v, count * KV, err, n) &&
               h2d(E, E->dev.kscale + base, ks, count * 4, err, n) && h2d(E, E->dev.vscale + base, vs, count * 4, err, n);
+    const cudaError_t ce = ok ? cudaStreamSynchronize(E->stream) : cudaSuccess;
+    E->h_stage_used = 0;                  // the staged inputs have been consumed (or the call failed)
     if (!ok) return 0;
-    return cuda_ok(cudaStreamSynchronize(E->stream), "kv write", err, n) ? 1 : 0;
+    return cuda_ok(ce, "kv write", err, n) ? 1 : 0;
 }
 
 QX_API int qx_cuda_kv_read(qx_cuda_engine* E, uint32_t layer, uint32_t first, uint32_t count, int8_t* k, int8_t* v,
