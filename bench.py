@@ -338,7 +338,8 @@ def stage_configs(eng, cfg, stream, reps=10,
         per_tok = (Q + 2 * KV) * H + H * Q + E * H + 8 * 3 * I * H          # weight multiply-adds per token and layer
         macs = n * cfg.layers * per_tok + cfg.vocab * H                    # + the head for the last token
         out["config5_prefill_2048"] = {
-            "config": "2048-token prompt prefill, 48 layers, tcgen05 projection and expert GEMMs, batched causal attention",
+            "config": "2048-token prompt prefill, %d layers, tcgen05 projection and expert GEMMs, batched causal attention"
+                      % cfg.layers,
             "us_per_call": round(us, 1), "tokens_per_s": round(n / (us / 1e6), 1),
             "useful_TFLOP/s": round(2 * macs / us / 1e6, 2),
             "frac_of_bf16_sustained": round(2 * macs / us / 1e6 / bf16, 4),
@@ -358,7 +359,7 @@ def stage_configs(eng, cfg, stream, reps=10,
         kv_b = nseq * sum(W.kv_bytes_per_token(cfg, p) for p in range(first, first + steps)) / steps
         out["config5_decode_batch64_ctx4096"] = {
             "config": "64 sequences decoding together at positions 3840..3847 (each its own INT8 KV slot; the "
-                      "history is the slots' zero-filled cache, read in full), 48 layers + head",
+                      "history is the slots' zero-filled cache, read in full), %d layers + head" % cfg.layers,
             "us_per_step": round(us / steps, 1), "tokens_per_s": round(tok_s, 1),
             "kv_GB/s": round(kv_b * steps / (us / 1e6) / 1e9, 1),
             "note": "per sequence the reference's state-loop step; tests/test_gpu_batch.py checks the tokens "
